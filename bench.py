@@ -1,0 +1,518 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 token sampler (verbo's Sampler::pick, src/sampler.cpp:50-109).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank runs the same per-rank workload (weak
+scaling: rows are independent, no collective on the data path) and rank 0
+prints ONE JSON line.  A "step" is one pass of the sampler over one batch of
+synthetic logits rows.
+
+  value     sampled rows/s of the whole job, inputs resident in HBM, timed with
+            CUDA events around K steps (barrier + synchronize on both sides,
+            max over ranks);
+  e2e       the same metric through the public call with HOST buffers: each
+            step copies its rows (and histories) from pinned host memory,
+            samples, and reads the ids back;
+  roofline  the sampling kernel's algorithmic bytes per launch (4*V + 4*H + 4
+            per row) over its average CUDA-event launch time, against the
+            measured HBM copy bandwidth;
+  cpu_baseline  the reference's own Sampler (compiled from its sources,
+            oracle/_ref) on this host's cores, on a bounded sample of rows.
+
+--impl reference times only that CPU reference (rank 0; other ranks exit).
+The c5 configuration measures the vocab-sharded form instead: per-rank
+column shard -> shard_topk -> NCCL all-gather of candidates -> merge_sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from verbo_b200 import workloads as wl  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--config", default="c3", choices=sorted(wl.WORKLOADS))
+    p.add_argument("--rows", type=int, default=0, help="rows per GPU (default: the configuration's)")
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--e2e-steps", type=int, default=0, help="steps of the host-buffer measurement (default min(K, 10))")
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    a = p.parse_args()
+    if a.warmup < 3:
+        p.error("--warmup must be >= 3")
+    return a
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def measured_peak():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.is_file():
+        d = json.loads(f.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_per_row(workload: str):
+    """DRAM bytes per row of the dominant kernel from a committed ncu capture
+    (profiles/traffic.json: {workload: {"bytes_per_row": B, ...}}), or None."""
+    f = ROOT / "profiles" / "traffic.json"
+    if not f.is_file():
+        return None
+    d = json.loads(f.read_text()).get(workload)
+    return None if d is None else float(d["bytes_per_row"])
+
+
+class Clocks:
+    """nvidia-smi sampling (200 ms) of SM clocks and throttle reasons."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def algorithmic_bytes_per_row(w: wl.Workload, cols: int | None = None) -> int:
+    cols = w.vocab if cols is None else cols
+    return 4 * cols + 4 * w.hist_len + 4
+
+
+# ----------------------------------------------------------- CPU reference ----
+def cpu_reference_rate(w: wl.Workload, x: np.ndarray, h, off, seconds: float, threads: int):
+    """Rows/s of the reference's compiled Sampler (oracle/_ref, else the C
+    restatement) over the host rows `x`, repeated until `seconds` elapse."""
+    from oracle import pyoracle as po
+
+    o = po.sampling(**w.sampling_kwargs())
+    seeds = w.sampler_seeds(0, x.shape[0])
+    if po.ref_available():
+        kind, used = "reference", threads
+        run = lambda: po.ref_sample_rows(x, o, seeds, h, off, steps=1, threads=threads)  # noqa: E731
+    else:
+        kind, used = "port", 1
+        run = lambda: po.sample_rows(x, o, po.seed_states(seeds), h, off)  # noqa: E731
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        run()
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds or n >= 1000:
+            break
+    return n * x.shape[0] / dt, kind, used, n
+
+
+def host_rows_for_budget(w: wl.Workload, seconds: float, threads: int, cap: int):
+    """Picks a sample size for the CPU leg from a one-row calibration."""
+    from oracle import pyoracle as po
+
+    x = wl.make_rows_np(w, 1)
+    h, off = wl.make_hist_np(w, 1)
+    o = po.sampling(**w.sampling_kwargs())
+    t0 = time.perf_counter()
+    if po.ref_available():
+        po.ref_sample_rows(x, o, w.sampler_seeds(0, 1), h, off, steps=1, threads=1)
+    else:
+        po.sample_rows(x, o, po.seed_states(w.sampler_seeds(0, 1)), h, off)
+    per_row = max(time.perf_counter() - t0, 1e-5)
+    eff = threads if po.ref_available() else 1
+    return int(max(eff, min(cap, seconds * eff / per_row / 2)))
+
+
+# ------------------------------------------------------ row-batched configs ----
+def bench_rows(a, w: wl.Workload, rank: int, world: int, dev):
+    import torch
+    import torch.distributed as dist
+
+    import verbo_b200 as vb
+
+    R = a.rows or w.rows
+    V = w.vocab
+    opts = vb.Sampling(**w.sampling_kwargs())
+    batch_bytes = R * V * 4
+    copies = 1 if batch_bytes > L2_BYTES else -(-2 * L2_BYTES // batch_bytes)
+    xs = [wl.make_rows_torch(w, R, dev, seed_offset=rank * 1000 + c) for c in range(copies)]
+    h, off = wl.make_hist_torch(w, R, dev, seed_offset=rank)
+    seeds = w.sampler_seeds(rank * R, R)
+    st = np.array(vb.seed_states(seeds.tolist()), dtype=np.uint64)
+    rng = torch.from_numpy(st.view(np.int64).copy()).to(dev)
+    out = torch.empty(R, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        vb.sample(xs[i % copies], opts, rng=rng, hist=h, hist_off=off, out=out, stream=stream)
+
+    for i in range(a.warmup):
+        step(i)
+    vb.check(stream)
+    clocks = Clocks(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        t_soak = time.perf_counter()
+        i = 0
+        while time.perf_counter() - t_soak < 1.0:   # >= 1 s of load around the timed region for the clock record
+            step(i)
+            i += 1
+            if i % 64 == 0:
+                torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for i in range(a.steps):
+        ev[i][0].record(stream)
+        step(i)
+        ev[i][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    if clocks:
+        clocks.stop()
+    vb.check(stream)
+    elapsed = t0.elapsed_time(t1)
+    launch_ms = sum(s.elapsed_time(e) for s, e in ev) / a.steps
+    red = torch.tensor([elapsed, launch_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(red, op=dist.ReduceOp.MAX)
+    elapsed, launch_ms = red.tolist()
+
+    # end to end through the public call with host buffers
+    e2e_steps = a.e2e_steps or min(a.steps, 10)
+    hx = torch.empty((R, V), dtype=torch.float32, pin_memory=True)
+    hx.copy_(xs[0])
+    hh = None if h is None else torch.empty(h.shape, dtype=h.dtype, pin_memory=True).copy_(h)
+    ho = None if off is None else torch.empty(off.shape, dtype=off.dtype, pin_memory=True).copy_(off)
+    ids_host = torch.empty(R, dtype=torch.int32, pin_memory=True)
+    dx = torch.empty((R, V), dtype=torch.float32, device=dev)
+    dh = None if h is None else torch.empty_like(h)
+    do = None if off is None else torch.empty_like(off)
+    h2d = R * V * 4 + (0 if h is None else h.numel() * 4 + off.numel() * 8)
+    d2h = R * 4
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        if hh is not None:
+            dh.copy_(hh, non_blocking=True)
+            do.copy_(ho, non_blocking=True)
+        vb.sample(dx, opts, rng=rng, hist=dh, hist_off=do, out=out, stream=stream)
+        ids_host.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+
+    res = dict(R=R, elapsed_ms=elapsed, launch_ms=launch_ms, e2e_ms=e2e_ms, e2e_steps=e2e_steps, h2d=h2d, d2h=d2h,
+               copies=copies, batch_bytes=batch_bytes, launches=a.steps, clocks=clocks.summary() if clocks else None)
+    host_sample = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        from oracle import pyoracle as po
+
+        thr = po.host_threads()
+        n = min(R, host_rows_for_budget(w, a.cpu_seconds, thr, R))
+        host_sample = (xs[0][:n].cpu().numpy(), None if h is None else h[: n * w.hist_len].cpu().numpy(),
+                       None if off is None else off[: n + 1].cpu().numpy())
+    return res, host_sample
+
+
+# -------------------------------------------------- vocab-sharded config (c5) ----
+def bench_sharded(a, w: wl.Workload, rank: int, world: int, dev):
+    """Each rank holds V/N contiguous columns of all R rows: shard_topk ->
+    NCCL all-gather of (value, id) candidates -> merge_sample on every rank."""
+    import torch
+    import torch.distributed as dist
+
+    import verbo_b200 as vb
+
+    R = a.rows or w.rows
+    V = w.vocab
+    if V % world:
+        raise SystemExit(f"vocab {V} is not divisible by {world} ranks")
+    cols = V // world
+    k = 64
+    opts = vb.Sampling(**w.sampling_kwargs())
+    shard_w = wl.Workload(w.name, R, cols, w.dist, w.scale, w.data_seed, w.temp, w.top_k, w.top_p, w.min_p,
+                          w.repeat, w.hist_len)
+    batch_bytes = R * cols * 4
+    copies = 1 if batch_bytes > L2_BYTES else -(-2 * L2_BYTES // batch_bytes)
+    xs = [wl.make_rows_torch(shard_w, R, dev, seed_offset=rank * 1000 + c) for c in range(copies)]
+    h, off = wl.make_hist_torch(w, R, dev, seed_offset=0)        # the same histories on every rank
+    st = np.array(vb.seed_states(w.sampler_seeds(0, R).tolist()), dtype=np.uint64)
+    rng = torch.from_numpy(st.view(np.int64).copy()).to(dev)
+    cv = torch.empty(world, R, k, dtype=torch.float32, device=dev)
+    ci = torch.empty(world, R, k, dtype=torch.int32, device=dev)
+    lv = torch.empty(R, k, dtype=torch.float32, device=dev)
+    li = torch.empty(R, k, dtype=torch.int32, device=dev)
+    out = torch.empty(R, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    ev = []
+
+    def step(i, timed=False):
+        if timed:
+            e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            e[0].record(stream)
+        vb.shard_topk(xs[i % copies], rank * cols, V, opts, k, h, off, cand_val=lv, cand_id=li, stream=stream)
+        if timed:
+            e[1].record(stream)
+            ev.append(e)
+        if world > 1:
+            dist.all_gather_into_tensor(cv, lv)
+            dist.all_gather_into_tensor(ci, li)
+        else:
+            cv[0].copy_(lv)
+            ci[0].copy_(li)
+        vb.merge_sample(cv, ci, V, opts, rng=rng, out=out, stream=stream)
+
+    for i in range(a.warmup):
+        step(i)
+    vb.check(stream)
+    clocks = Clocks(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    t_soak = time.perf_counter()
+    i = 0
+    while True:   # the same number of soak steps on every rank (collectives must match)
+        step(i)
+        i += 1
+        done = torch.tensor([1.0 if time.perf_counter() - t_soak >= 1.0 else 0.0], device=dev)
+        if world > 1:
+            dist.all_reduce(done, op=dist.ReduceOp.MIN)
+        if done.item() > 0:
+            break
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for i in range(a.steps):
+        step(i, timed=True)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    if clocks:
+        clocks.stop()
+    vb.check(stream)
+    red = torch.tensor([t0.elapsed_time(t1), sum(s.elapsed_time(e) for s, e in ev) / a.steps], dtype=torch.float64,
+                       device=dev)
+    if world > 1:
+        dist.all_reduce(red, op=dist.ReduceOp.MAX)
+    elapsed, launch_ms = red.tolist()
+    return dict(R=R, cols=cols, elapsed_ms=elapsed, launch_ms=launch_ms, copies=copies, batch_bytes=batch_bytes,
+                launches=3 * a.steps, clocks=clocks.summary() if clocks else None)
+
+
+# ------------------------------------------------------------ reference arm ----
+def bench_reference(a, w: wl.Workload, world: int):
+    from oracle import pyoracle as po
+
+    threads = po.host_threads()
+    per_step = min(2.0, 150.0 / (a.steps + a.warmup))
+    n = min(w.rows, host_rows_for_budget(w, per_step, threads, w.rows))
+    x = wl.make_rows_np(w, n)
+    h, off = wl.make_hist_np(w, n)
+    o = po.sampling(**w.sampling_kwargs())
+    seeds = w.sampler_seeds(0, n)
+    kind = "reference" if po.ref_available() else "port"
+
+    def step():
+        if kind == "reference":
+            po.ref_sample_rows(x, o, seeds, h, off, steps=1, threads=threads)
+        else:
+            po.sample_rows(x, o, po.seed_states(seeds), h, off)
+
+    for _ in range(a.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        step()
+    dt = time.perf_counter() - t0
+    value = a.steps * n / dt
+    sample = f"{n} of the {w.rows} rows of {w.name}, the same rows every step"
+    line = {
+        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": dt * 1000.0 / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": workload_config(w, n, 1),
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads if kind == "reference" else 1,
+                         "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "sampled rows/s at V=151936, 1/2/4/8 B200; HBM GB/s vs ~8 TB/s peak"
+
+
+def workload_config(w: wl.Workload, rows_per_gpu: int, world: int, **extra):
+    d = {"workload": (f"{w.name}: {w.rows} x {w.vocab} fp32 logits ({w.dist}, scale {w.scale}), temp {w.temp}, "
+                      f"top_k {w.top_k}, top_p {w.top_p}, min_p {w.min_p}, repeat {w.repeat} over {w.hist_len} ids"),
+         "vocab": w.vocab, "rows_per_gpu": rows_per_gpu, "global_rows": rows_per_gpu * world,
+         "history": w.hist_len, "parallelism": f"rows x{world}" if w.shards == 1 else f"vocab shards x{world}"}
+    d.update(extra)
+    return d
+
+
+def main():
+    a = parse_args()
+    rank, local_rank, world = dist_env()
+    w = wl.WORKLOADS[a.config]
+    if a.rows:
+        w = w.with_rows(a.rows)
+    if a.impl == "reference":
+        if rank == 0:
+            bench_reference(a, w, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import verbo_b200 as vb
+
+    vb.load_library()  # fails loudly if the CUDA library is missing
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    try:
+        if w.shards > 1:
+            res = bench_sharded(a, w, rank, world, dev)
+            host_sample = None
+        else:
+            res, host_sample = bench_rows(a, w, rank, world, dev)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peak, peak_kind = measured_peak()
+    R = res["R"]
+    sharded = w.shards > 1
+    cols = res.get("cols", w.vocab)
+    rows_job = R if sharded else R * world
+    value = rows_job * a.steps / (res["elapsed_ms"] / 1000.0)
+    alg_launch = R * (algorithmic_bytes_per_row(w, cols) + (8 * 64 if sharded else 0))
+    achieved = alg_launch / (res["launch_ms"] / 1000.0) / 1e9
+    tr = traffic_per_row(w.name)
+    line = {
+        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": res["elapsed_ms"] / a.steps, "higher_is_better": True,
+        "scaling": "strong" if sharded else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(
+            w, R, 1 if sharded else world,
+            l2=("inputs larger than L2" if res["copies"] == 1 else
+                f"{res['copies']} rotating input copies ({res['copies'] * res['batch_bytes'] >> 20} MiB) > L2"),
+            **({"columns_per_gpu": cols} if sharded else {})),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "traffic": None if tr is None else tr * R,
+                     "kernel": "shard_topk_kernel" if sharded else kernel_name(w),
+                     "alg_bytes_per_launch": alg_launch, "launch_ms": res["launch_ms"]},
+        "clocks": res["clocks"],
+        "gpu_launches": res["launches"] * world,
+    }
+    if not sharded:
+        line["e2e"] = {"value": rows_job * res["e2e_steps"] / (res["e2e_ms"] / 1000.0), "unit": "rows/s",
+                       "h2d_bytes_per_step": res["h2d"] * world, "d2h_bytes_per_step": res["d2h"] * world}
+    else:
+        line["e2e"] = None
+    if host_sample is not None:
+        x, h, off = host_sample
+        from oracle import pyoracle as po
+
+        rate, kind, cores, reps = cpu_reference_rate(w, x, h, off, a.cpu_seconds, po.host_threads())
+        line["cpu_baseline"] = {"value": rate, "unit": "rows/s", "cores": cores, "kind": kind,
+                                "sample": f"{x.shape[0]} rows of the timed batch x {reps} passes"}
+    print(json.dumps(line), flush=True)
+
+
+def kernel_name(w: wl.Workload) -> str:
+    if w.temp <= 0:
+        return "greedy_kernel"
+    if 0 < w.top_k < w.vocab and w.top_k <= 1024:
+        return "topk_kernel"
+    return "general_kernel"
+
+
+if __name__ == "__main__":
+    main()

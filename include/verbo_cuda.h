@@ -1,0 +1,142 @@
+/*
+ * verbo_cuda.h - C ABI of the B200 (sm_100a) token sampler.
+ *
+ * A drop-in for verbo's Sampler (src/sampler.cpp, include/verbo/verbo.hpp:
+ * 56-64 and 116-132), placed beside the reference's C ABI
+ * (include/verbo/verbo.h, src/capi.cpp).  Conventions follow that ABI:
+ *   - plain pointers and sizes, no C++ or torch types;
+ *   - int functions return 0 (or a token id) on success and -1 on error,
+ *     pointer functions return NULL on error;
+ *   - the message of the last error on this thread is verbo_cuda_last_error()
+ *     (as verbo_last_error, src/capi.cpp:17-30 and :46);
+ *   - VERBO_CUDA_API marks every exported symbol (the library is built with
+ *     -fvisibility=hidden, as CMakeLists.txt:36 does for libverbo).
+ *
+ * Batched entry points take DEVICE pointers and are asynchronous on the given
+ * CUDA stream (NULL = legacy default stream).  The caller owns every buffer.
+ * Device-side failures (a bounded wait that ran out) are recorded in a status
+ * word that verbo_cuda_check() reads.
+ *
+ * Row layout:
+ *   logits   rows x ld fp32, row r at logits + r*ld, `vocab` valid columns;
+ *   hist     int32 token histories in CSR form: row r owns
+ *            hist[hist_off[r] .. hist_off[r+1]); NULL hist => no history;
+ *            the penalty window is the last repeat_last ids of each row
+ *            (all of them when repeat_last <= 0), src/sampler.cpp:53-57;
+ *   rng      2 x u64 xoroshiro128+ state per row, advanced in place by one
+ *            draw per non-greedy pick (src/sampler.cpp:33-41, :103).
+ */
+#ifndef VERBO_CUDA_H
+#define VERBO_CUDA_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define VERBO_CUDA_API __declspec(dllexport)
+#else
+#define VERBO_CUDA_API __attribute__((visibility("default")))
+#endif
+
+/* verbo::Sampling, field for field (include/verbo/verbo.hpp:56-64);
+   verbo_cuda_default_sampling() returns the reference defaults
+   {temp 0.7, top_k 40, top_p 0.9, min_p 0, repeat 1, repeat_last 64, seed 0}. */
+typedef struct {
+  float temp;
+  int top_k;
+  float top_p;
+  float min_p;
+  float repeat;
+  int repeat_last;
+  unsigned long long seed;
+} verbo_sampling;
+
+/* Optional per-row diagnostics of one pick (device memory when passed to a
+   batched call).  `sum`/`tot` are the softmax normaliser and the kept mass of
+   src/sampler.cpp:80-102, `u` the uniform drawn, `keep` the kept prefix. */
+typedef struct {
+  double sum;
+  double tot;
+  double u;
+  double draw_margin;
+  double cut_margin;
+  int k;
+  int keep;
+  int id;
+  int greedy;
+} verbo_row_stats;
+
+/* Replaces verbo_last_error (include/verbo/verbo.h:30). */
+VERBO_CUDA_API const char* verbo_cuda_last_error(void);
+/* Replaces verbo_version (include/verbo/verbo.h:31). */
+VERBO_CUDA_API const char* verbo_cuda_version(void);
+/* The defaults of verbo::Sampling (include/verbo/verbo.hpp:56-64). */
+VERBO_CUDA_API verbo_sampling verbo_cuda_default_sampling(void);
+
+/* Seeds one xoroshiro128+ state exactly as Sampler::reset
+   (src/sampler.cpp:26-31): two splitmix64 outputs of `seed`; seed 0 takes the
+   clock, as the reference does.  Host memory. */
+VERBO_CUDA_API int verbo_cuda_rng_seed(unsigned long long seed, unsigned long long state[2]);
+/* One Sampler::unit draw on a host state (src/sampler.cpp:33-41). */
+VERBO_CUDA_API double verbo_cuda_rng_unit(unsigned long long state[2]);
+
+/* Sampler::pick (src/sampler.cpp:50-109) for `rows` device-resident rows with
+   one option set.  Writes out_ids[r] (device).  rng may be NULL only when
+   opts->temp <= 0 (greedy consumes no draw).  stats may be NULL.
+   Limits: 1 <= vocab <= 327680, ld >= vocab, finite temp. */
+VERBO_CUDA_API int verbo_cuda_sample(const float* logits, int rows, int vocab, long long ld, const int* hist,
+                                     const long long* hist_off, const verbo_sampling* opts,
+                                     unsigned long long* rng, int* out_ids, verbo_row_stats* stats,
+                                     void* stream);
+
+/* Vocab-sharded sampling, step 1: for a shard holding global columns
+   [col_offset, col_offset + shard_cols) of each row, apply the penalty for
+   the history ids that fall in the shard and emit the shard's k best
+   (value, global id) pairs in the reference's order (value descending, id
+   ascending) to cand_val/cand_id [rows][k] (device).  Missing slots are
+   (-inf, -1).  1 <= k <= 1024. */
+VERBO_CUDA_API int verbo_cuda_shard_topk(const float* logits, int rows, int shard_cols, long long ld,
+                                         int col_offset, int vocab, const int* hist, const long long* hist_off,
+                                         const verbo_sampling* opts, int k, float* cand_val, int* cand_id,
+                                         void* stream);
+
+/* Vocab-sharded sampling, step 2: merge the candidates of all shards, laid
+   out [nshards][rows][k] (the layout of an all-gather of step-1 outputs), and
+   finish the pick: softmax, min-p, top-p and the draw.  Equal to
+   verbo_cuda_sample on the unsharded rows when opts->temp <= 0 or
+   0 < opts->top_k <= k.  nshards * k <= 4096. */
+VERBO_CUDA_API int verbo_cuda_merge_sample(const float* cand_val, const int* cand_id, int rows, int nshards,
+                                           int k, int vocab, const verbo_sampling* opts,
+                                           unsigned long long* rng, int* out_ids, verbo_row_stats* stats,
+                                           void* stream);
+
+/* Synchronises `stream` and reports device-side failures recorded since the
+   last check (then clears them): 0 if none, -1 with a message otherwise. */
+VERBO_CUDA_API int verbo_cuda_check(void* stream);
+
+/* ---- Single-stream sampler object: the verbo::Sampler interface
+        (include/verbo/verbo.hpp:116-132) as an opaque handle. ---- */
+typedef struct verbo_cuda_sampler verbo_cuda_sampler;
+
+/* Sampler(Sampling) (src/sampler.cpp:24): seeds the RNG, empty history.
+   `device` is the CUDA device to run on. */
+VERBO_CUDA_API verbo_cuda_sampler* verbo_cuda_sampler_new(const verbo_sampling* cfg, int device);
+VERBO_CUDA_API void verbo_cuda_sampler_free(verbo_cuda_sampler* s);
+/* Sampler::pick (src/sampler.cpp:50-109).  `logits` may be host or device
+   memory; returns the token id, or -1 on error. */
+VERBO_CUDA_API int verbo_cuda_sampler_pick(verbo_cuda_sampler* s, const float* logits, int n);
+/* Sampler::accept (src/sampler.cpp:43-48). */
+VERBO_CUDA_API int verbo_cuda_sampler_accept(verbo_cuda_sampler* s, int tok);
+/* Sampler::reset (src/sampler.cpp:26-31). */
+VERBO_CUDA_API int verbo_cuda_sampler_reset(verbo_cuda_sampler* s);
+/* Sampler::cfg (include/verbo/verbo.hpp:123). */
+VERBO_CUDA_API int verbo_cuda_sampler_cfg(const verbo_cuda_sampler* s, verbo_sampling* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,188 @@
+"""ctypes access to the CPU checkers of the sampling path - TEST INFRASTRUCTURE.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU legs import this
+module.  It wraps two libraries built by ``oracle/Makefile``:
+
+* ``_build/liboracle.so``   - the C restatement of verbo's Sampler
+  (src/sampler.cpp:11-109), with per-row diagnostics;
+* ``_ref/libverbo_ref.so``  - the reference's own Sampler compiled from its
+  sources, driven through ``ref_harness.cpp``.  Optional: it exists only where
+  the reference sources were available at build time.
+
+All array arguments are numpy arrays on the host.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Optional
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_LIB = HERE / "_build" / "liboracle.so"
+REF_LIB = HERE / "_ref" / "libverbo_ref.so"
+
+
+class OracleSampling(ctypes.Structure):
+    """Field-for-field verbo::Sampling (include/verbo/verbo.hpp:56-64)."""
+
+    _fields_ = [
+        ("temp", ctypes.c_float),
+        ("top_k", ctypes.c_int),
+        ("top_p", ctypes.c_float),
+        ("min_p", ctypes.c_float),
+        ("repeat", ctypes.c_float),
+        ("repeat_last", ctypes.c_int),
+        ("seed", ctypes.c_ulonglong),
+    ]
+
+
+class RowStats(ctypes.Structure):
+    _fields_ = [
+        ("sum", ctypes.c_double),
+        ("tot", ctypes.c_double),
+        ("u", ctypes.c_double),
+        ("draw_margin", ctypes.c_double),
+        ("cut_margin", ctypes.c_double),
+        ("k", ctypes.c_int),
+        ("keep", ctypes.c_int),
+        ("id", ctypes.c_int),
+        ("greedy", ctypes.c_int),
+    ]
+
+
+STATS_DTYPE = np.dtype(
+    [("sum", "f8"), ("tot", "f8"), ("u", "f8"), ("draw_margin", "f8"), ("cut_margin", "f8"),
+     ("k", "i4"), ("keep", "i4"), ("id", "i4"), ("greedy", "i4")]
+)
+assert STATS_DTYPE.itemsize == ctypes.sizeof(RowStats)
+
+
+def sampling(temp=0.7, top_k=40, top_p=0.9, min_p=0.0, repeat=1.0, repeat_last=64, seed=0) -> OracleSampling:
+    """Defaults are verbo::Sampling's (include/verbo/verbo.hpp:56-64)."""
+    return OracleSampling(temp, top_k, top_p, min_p, repeat, repeat_last, seed)
+
+
+_P = ctypes.c_void_p
+_oracle = None
+_ref = None
+
+
+def _ptr(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data_as(_P)
+
+
+def oracle_lib():
+    global _oracle
+    if _oracle is None:
+        if not ORACLE_LIB.is_file():
+            raise RuntimeError(f"{ORACLE_LIB} missing: run `make -C oracle`")
+        lib = ctypes.CDLL(str(ORACLE_LIB))
+        lib.oracle_seed.argtypes = [ctypes.c_uint64, _P]
+        lib.oracle_unit.argtypes = [_P]
+        lib.oracle_unit.restype = ctypes.c_double
+        lib.oracle_sample_rows.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, _P, _P, _P, _P, _P, _P]
+        lib.oracle_shard_topk.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, ctypes.c_int,
+                                          ctypes.c_int, _P, _P, _P, ctypes.c_int, _P, _P]
+        lib.oracle_merge_sample.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            _P, _P, _P, _P]
+        _oracle = lib
+    return _oracle
+
+
+def ref_available() -> bool:
+    return REF_LIB.is_file()
+
+
+def ref_lib():
+    global _ref
+    if _ref is None:
+        if not REF_LIB.is_file():
+            raise RuntimeError(f"{REF_LIB} missing: build it with `make -C oracle ref REF=<verbo checkout>`")
+        lib = ctypes.CDLL(str(REF_LIB))
+        lib.ref_sample_rows.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, _P, _P, _P, _P,
+                                        ctypes.c_int, _P, ctypes.c_int]
+        _ref = lib
+    return _ref
+
+
+def seed_states(seeds: np.ndarray) -> np.ndarray:
+    """(rows,) u64 seeds -> (rows, 2) u64 xoroshiro128+ states (Sampler::reset)."""
+    lib = oracle_lib()
+    seeds = np.ascontiguousarray(seeds, dtype=np.uint64)
+    out = np.zeros((seeds.shape[0], 2), dtype=np.uint64)
+    for r, s in enumerate(seeds):
+        lib.oracle_seed(ctypes.c_uint64(int(s)), out[r].ctypes.data_as(_P))
+    return out
+
+
+def _hist(hist, hist_off):
+    if hist is None:
+        return None, None
+    return (np.ascontiguousarray(hist, dtype=np.int32), np.ascontiguousarray(hist_off, dtype=np.int64))
+
+
+def sample_rows(logits: np.ndarray, opts: OracleSampling, rng: Optional[np.ndarray] = None, hist=None,
+                hist_off=None, vocab: Optional[int] = None):
+    """C restatement of Sampler::pick over rows.  `rng` (rows,2) u64 is advanced
+    in place for non-greedy picks.  Returns (ids, stats)."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    rows, ld = logits.shape
+    vocab = ld if vocab is None else vocab
+    h, ho = _hist(hist, hist_off)
+    if rng is None:
+        rng = np.zeros((rows, 2), dtype=np.uint64)
+    assert rng.dtype == np.uint64 and rng.flags.c_contiguous
+    ids = np.zeros(rows, dtype=np.int32)
+    stats = np.zeros(rows, dtype=STATS_DTYPE)
+    oracle_lib().oracle_sample_rows(_ptr(logits), rows, vocab, ld, _ptr(h), _ptr(ho), ctypes.byref(opts),
+                                    _ptr(rng), _ptr(ids), _ptr(stats))
+    return ids, stats
+
+
+def shard_topk(shard: np.ndarray, col_offset: int, vocab: int, opts: OracleSampling, k: int, hist=None,
+               hist_off=None):
+    shard = np.ascontiguousarray(shard, dtype=np.float32)
+    rows, cols = shard.shape
+    h, ho = _hist(hist, hist_off)
+    val = np.zeros((rows, k), dtype=np.float32)
+    cid = np.zeros((rows, k), dtype=np.int32)
+    oracle_lib().oracle_shard_topk(_ptr(shard), rows, cols, cols, col_offset, vocab, _ptr(h), _ptr(ho),
+                                   ctypes.byref(opts), k, _ptr(val), _ptr(cid))
+    return val, cid
+
+
+def merge_sample(cand_val: np.ndarray, cand_id: np.ndarray, vocab: int, opts: OracleSampling,
+                 rng: Optional[np.ndarray] = None):
+    """cand_* shaped (nshards, rows, k)."""
+    cand_val = np.ascontiguousarray(cand_val, dtype=np.float32)
+    cand_id = np.ascontiguousarray(cand_id, dtype=np.int32)
+    nshards, rows, k = cand_val.shape
+    if rng is None:
+        rng = np.zeros((rows, 2), dtype=np.uint64)
+    ids = np.zeros(rows, dtype=np.int32)
+    stats = np.zeros(rows, dtype=STATS_DTYPE)
+    oracle_lib().oracle_merge_sample(_ptr(cand_val), _ptr(cand_id), rows, nshards, k, vocab,
+                                     ctypes.byref(opts), _ptr(rng), _ptr(ids), _ptr(stats))
+    return ids, stats
+
+
+def ref_sample_rows(logits: np.ndarray, opts: OracleSampling, seeds: np.ndarray, hist=None, hist_off=None,
+                    steps: int = 1, threads: int = 1, vocab: Optional[int] = None) -> np.ndarray:
+    """The reference's own Sampler: row r seeded with seeds[r], history fed
+    through accept(), then `steps` picks.  Returns (rows, steps) int32."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    rows, ld = logits.shape
+    vocab = ld if vocab is None else vocab
+    h, ho = _hist(hist, hist_off)
+    seeds = np.ascontiguousarray(seeds, dtype=np.uint64)
+    out = np.zeros((rows, steps), dtype=np.int32)
+    ref_lib().ref_sample_rows(_ptr(logits), rows, vocab, ld, _ptr(h), _ptr(ho), ctypes.byref(opts),
+                              _ptr(seeds), steps, _ptr(out), threads)
+    return out
+
+
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0))

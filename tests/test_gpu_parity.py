@@ -1,0 +1,234 @@
+"""Parity of the CUDA sampler with the oracle and the reference's golden ids.
+
+Every test calls the CUDA library through its C ABI (via verbo_b200's ctypes
+binding) on device-resident rows and compares with the C oracle, which
+tests/test_oracle.py pins against the reference's compiled Sampler.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import pyoracle as po
+from tests import golden_io
+from tests.gpu_util import compare, run_gpu, run_oracle
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+LG = np.array([[0.1, 3.0, 2.9, -1.0, 0.0]], dtype=np.float32)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib(cuda_lib):
+    if not torch.cuda.is_available():
+        pytest.fail("gpu tests need a CUDA device")
+    yield
+
+
+# ------------------------------------------------ reference known answers ----
+def test_kat_greedy():
+    ids, _, _ = run_gpu(LG, dict(temp=0.0))
+    assert ids[0, 0] == 1
+
+
+def test_kat_topk2_400_draws():
+    # tests/test_core.cpp:459-470 with the rng advancing in place on the device
+    seeds = np.array([42], dtype=np.uint64)
+    opts = dict(temp=0.7, top_k=2, top_p=1.0)
+    ids, _, _ = run_gpu(LG, opts, seeds, steps=400)
+    ora, _, _ = run_oracle(LG, opts, seeds, steps=400)
+    assert np.array_equal(ids, ora)
+    assert 150 < int((ids == 1).sum()) < 300
+
+
+def test_kat_top_p_and_min_p():
+    ids, _, _ = run_gpu(LG, dict(temp=0.7, top_k=0, top_p=0.5), np.array([1], np.uint64), steps=100)
+    assert (ids == 1).all()
+    ids, _, _ = run_gpu(LG, dict(temp=0.7, top_k=0, top_p=1.0, min_p=0.5), np.array([1], np.uint64), steps=100)
+    assert set(ids.ravel().tolist()) <= {1, 2}
+    ora, _, _ = run_oracle(LG, dict(temp=0.7, top_k=0, top_p=1.0, min_p=0.5), np.array([1], np.uint64), steps=100)
+    assert np.array_equal(ids, ora)
+
+
+def test_kat_repeat_penalty():
+    h, off = np.array([1], np.int32), np.array([0, 1], np.int64)
+    ids, _, _ = run_gpu(LG, dict(temp=0.0, repeat=2.0), hist=h, off=off)
+    assert ids[0, 0] == 2
+    ids, _, _ = run_gpu(LG, dict(temp=0.0, repeat=2.0))
+    assert ids[0, 0] == 1
+
+
+def test_sampler_object_kat():
+    # the verbo::Sampler interface: host and device logits, accept, reset
+    import verbo_b200 as vb
+
+    s = vb.Sampler(vb.Sampling(temp=0.0, repeat=2.0))
+    assert s.pick(LG[0]) == 1
+    s.accept(1)
+    assert s.pick(LG[0]) == 2
+    assert s.pick(torch.from_numpy(LG[0]).cuda()) == 2
+    s.reset()
+    assert s.pick(LG[0]) == 1
+    assert s.cfg().repeat == 2.0
+    a, b = vb.Sampler(vb.Sampling(seed=42, top_k=2, top_p=1.0)), vb.Sampler(vb.Sampling(seed=42, top_k=2, top_p=1.0))
+    xs = [a.pick(LG[0]) for _ in range(100)]
+    assert xs == [b.pick(LG[0]) for _ in range(100)]
+    ora, _, _ = run_oracle(LG, dict(temp=0.7, top_k=2, top_p=1.0), np.array([42], np.uint64), steps=100)
+    assert xs == ora[0].tolist()
+
+
+# -------------------------------------------------------- golden fixtures ----
+@pytest.mark.parametrize("case", golden_io.small_cases(), ids=lambda c: c.name)
+def test_golden_small(case):
+    steps = case.ids.shape[1]
+    ids, _, _ = run_gpu(case.logits, case.opts, case.seeds, case.hist, case.off, steps=steps)
+    _, ostats, _ = run_oracle(case.logits, case.opts, case.seeds, case.hist, case.off, steps=steps)
+    compare(ids, case.ids, ostats, case.name)
+
+
+def test_golden_configs():
+    for w, x, h, off, seeds, ref_ids in golden_io.config_cases():
+        ids, _, _ = run_gpu(x, w.sampling_kwargs(), seeds, h, off, steps=ref_ids.shape[1])
+        _, ostats, _ = run_oracle(x, w.sampling_kwargs(), seeds, h, off, steps=ref_ids.shape[1])
+        compare(ids, ref_ids, ostats, w.name)
+
+
+# ---------------------------------------------------- randomized coverage ----
+OPTION_SETS = [
+    dict(temp=0.0, repeat=1.3, repeat_last=16),                                   # greedy
+    dict(temp=0.7, top_k=40, top_p=0.9, min_p=0.05, repeat=1.1, repeat_last=64),  # streaming top-k
+    dict(temp=1.2, top_k=1, top_p=0.9),                                           # top-1
+    dict(temp=0.9, top_k=700, top_p=0.97, min_p=0.0, repeat=1.2),                 # large k, streaming kernel
+    dict(temp=1.5, top_k=0, top_p=0.99),                                          # full-vocab nucleus
+    dict(temp=1.0, top_k=0, top_p=1.0, min_p=0.1, repeat=0.9, repeat_last=0),     # full vocab, min-p only
+    dict(temp=0.6, top_k=3000, top_p=0.8, min_p=0.0),                             # k above the streaming range
+]
+
+
+@pytest.mark.parametrize("V", [5, 33, 400, 1001, 8192, 8193, 49152, 151936, 262144])
+@pytest.mark.parametrize("oi", range(len(OPTION_SETS)))
+def test_random_parity(V, oi):
+    opts = OPTION_SETS[oi]
+    g = np.random.default_rng([V, oi])
+    rows = 6 if V < 100000 else 3
+    x = (g.standard_normal((rows, V)) * g.uniform(0.3, 4.0)).astype(np.float32)
+    x[0, g.integers(0, V, size=max(1, V // 10))] = x[0, 0]                     # ties in row 0
+    H = 37
+    hist = g.integers(-2, V + 2, size=rows * H).astype(np.int32)
+    off = np.arange(rows + 1, dtype=np.int64) * H
+    seeds = np.arange(rows, dtype=np.uint64) + np.uint64(V * 31 + oi + 1)
+    ids, st, _ = run_gpu(x, opts, seeds, hist, off, steps=2)
+    ora, ost, _ = run_oracle(x, opts, seeds, hist, off, steps=2)
+    compare(ids, ora, ost, f"V={V} opts={opts}")
+    if opts["temp"] > 0:
+        # probabilities: softmax normaliser and kept mass of the last pick
+        o = ost[:, -1]
+        np.testing.assert_allclose(st["sum"], o["sum"], rtol=1e-5)
+        same = ids[:, -1] == ora[:, -1]
+        np.testing.assert_allclose(st["tot"][same], o["tot"][same], rtol=1e-5)
+        assert np.array_equal(st["keep"][same], o["keep"][same]) or (st["keep"][same] - o["keep"][same] != 0).sum() <= 1
+
+
+def test_unaligned_leading_dimension():
+    g = np.random.default_rng(7)
+    for V, ld in ((1000, 1003), (4099, 4101), (151936, 151939)):
+        x = g.standard_normal((4, V)).astype(np.float32)
+        for opts in (dict(temp=0.0, repeat=1.2), dict(temp=0.8, top_k=50, top_p=0.95), dict(temp=1.1, top_k=0, top_p=0.9)):
+            hist = g.integers(0, V, size=4 * 10).astype(np.int32)
+            off = np.arange(5, dtype=np.int64) * 10
+            seeds = np.arange(4, dtype=np.uint64) + np.uint64(77)
+            ids, _, _ = run_gpu(x, opts, seeds, hist, off, ld=ld)
+            ora, ost, _ = run_oracle(x, opts, seeds, hist, off)
+            compare(ids, ora, ost, f"V={V} ld={ld}")
+
+
+def test_nonfinite_rows():
+    V = 3000
+    g = np.random.default_rng(3)
+    x = g.standard_normal((5, V)).astype(np.float32)
+    x[0, :] = -np.inf                        # fully masked row
+    x[1, [5, 900]] = np.inf                  # +inf logits
+    x[2, : V - 3] = -np.inf                  # three finite values
+    x[3, ::2] = -np.inf                      # half masked
+    x[4, 17] = np.inf
+    x[4, 2000] = np.inf
+    for opts in (dict(temp=0.0), dict(temp=0.7, top_k=40, top_p=0.9), dict(temp=0.7, top_k=40, top_p=0.9, min_p=0.1),
+                 dict(temp=1.0, top_k=0, top_p=0.9), dict(temp=1.0, top_k=0, top_p=0.95, min_p=0.2),
+                 dict(temp=1.0, top_k=2000, top_p=1.0)):
+        seeds = np.arange(5, dtype=np.uint64) + np.uint64(5)
+        ids, _, _ = run_gpu(x, opts, seeds, steps=2)
+        ora, ost, _ = run_oracle(x, opts, seeds, steps=2)
+        compare(ids, ora, ost, str(opts))
+
+
+def test_greedy_nan_first_element():
+    # std::max_element keeps a NaN element 0 (nothing compares greater)
+    x = np.array([[np.nan, 1.0, 5.0, 2.0], [1.0, np.nan, 5.0, 5.0]], dtype=np.float32)
+    ids, _, _ = run_gpu(x, dict(temp=0.0))
+    ora, _, _ = run_oracle(x, dict(temp=0.0))
+    assert ids[:, 0].tolist() == ora[:, 0].tolist() == [0, 2]
+
+
+def test_history_windows():
+    V = 9000
+    g = np.random.default_rng(11)
+    x = (g.standard_normal((4, V)) * 2).astype(np.float32)
+    top = np.argsort(-x, axis=1)[:, :6]
+    # histories made of each row's best ids, with duplicates and ragged lengths
+    parts = [np.repeat(top[r], r + 1).astype(np.int32) for r in range(4)]
+    hist = np.concatenate(parts)
+    off = np.concatenate([[0], np.cumsum([len(p) for p in parts])]).astype(np.int64)
+    for rl in (0, 1, 3, 64):
+        for opts in (dict(temp=0.0, repeat=3.0, repeat_last=rl), dict(temp=0.5, top_k=20, top_p=0.9, repeat=3.0, repeat_last=rl)):
+            seeds = np.arange(4, dtype=np.uint64) + np.uint64(rl + 9)
+            ids, _, _ = run_gpu(x, opts, seeds, hist, off, steps=3)
+            ora, ost, _ = run_oracle(x, opts, seeds, hist, off, steps=3)
+            compare(ids, ora, ost, str(opts))
+
+
+# ------------------------------------------------------------- sharded path ----
+@pytest.mark.parametrize("nshards", [1, 2, 8])
+def test_shard_topk_and_merge(nshards):
+    import verbo_b200 as vb
+    from verbo_b200 import workloads as wl
+
+    w = wl.WORKLOADS["c5"].with_rows(24)
+    x = wl.make_rows_np(w)
+    h, off = wl.make_hist_np(w)
+    opts = w.sampling_kwargs()
+    o = vb.Sampling(**opts)
+    k = 64
+    cols = w.vocab // nshards
+    dx = torch.from_numpy(x).cuda()
+    dh, do = torch.from_numpy(h).cuda(), torch.from_numpy(off).cuda()
+    cv = torch.empty(nshards, w.rows, k, dtype=torch.float32, device="cuda")
+    ci = torch.empty(nshards, w.rows, k, dtype=torch.int32, device="cuda")
+    for s in range(nshards):
+        vb.shard_topk(dx[:, s * cols:(s + 1) * cols], s * cols, w.vocab, o, k, dh, do, cand_val=cv[s], cand_id=ci[s])
+        ov, oi = po.shard_topk(x[:, s * cols:(s + 1) * cols], s * cols, w.vocab, po.sampling(**opts), k, h, off)
+        assert np.array_equal(ci[s].cpu().numpy(), oi)
+        assert np.array_equal(cv[s].cpu().numpy(), ov)
+    seeds = w.sampler_seeds(0, w.rows)
+    from tests.gpu_util import to_dev_rng
+    rng = to_dev_rng(po.seed_states(seeds))
+    got = vb.merge_sample(cv, ci, w.vocab, o, rng=rng).cpu().numpy()
+    vb.check()
+    ora, ost, _ = run_oracle(x, opts, seeds, h, off)
+    compare(got[:, None], ora, ost, f"merge nshards={nshards}")
+    # greedy through the sharded path
+    g = vb.merge_sample(cv, ci, w.vocab, vb.Sampling(temp=0.0)).cpu().numpy()
+    assert np.array_equal(g, run_oracle(x, dict(temp=0.0, repeat=opts["repeat"], repeat_last=opts["repeat_last"]),
+                                        None, h, off)[0][:, 0])
+
+
+def test_shard_topk_small_shards_pad():
+    import verbo_b200 as vb
+
+    g = np.random.default_rng(5)
+    x = g.standard_normal((3, 50)).astype(np.float32)
+    cv, ci = vb.shard_topk(torch.from_numpy(x).cuda(), 100, 1000, vb.Sampling(), 64)
+    ov, oi = po.shard_topk(x, 100, 1000, po.sampling(), 64)
+    assert np.array_equal(ci.cpu().numpy(), oi)
+    assert (ci.cpu().numpy()[:, 50:] == -1).all()

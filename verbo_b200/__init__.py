@@ -1,0 +1,283 @@
+"""verbo_b200 - B200 (sm_100a) drop-in for verbo's token sampler.
+
+Python face of the C ABI in include/verbo_cuda.h, in the style of the
+reference's ctypes bindings (python/verbo/__init__.py): one shared library,
+``ctypes`` signatures, ``VerboCudaError`` carrying verbo_cuda_last_error().
+
+The compute runs only in the CUDA library ``_lib/libverbo_cuda.so``; there is
+no CPU fallback.  Importing this module does not need a GPU; calling a
+batched entry point needs device tensors (torch is used here only to hold
+device memory and streams).
+
+Entry points
+------------
+``Sampling``        the option set of verbo::Sampling (include/verbo/verbo.hpp:56-64)
+``Sampler``         the verbo::Sampler object (pick / accept / reset / cfg)
+``sample``          Sampler::pick over a batch of device-resident rows
+``shard_topk``      vocab-sharded step 1: a shard's k best (value, global id)
+``merge_sample``    vocab-sharded step 2: merge shard candidates and draw
+``seed_states``     per-row xoroshiro128+ states, seeded like Sampler::reset
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Optional, Sequence
+
+__all__ = ["Sampling", "Sampler", "VerboCudaError", "load_library", "sample", "shard_topk", "merge_sample",
+           "seed_states", "check", "version", "ROW_STATS_FIELDS"]
+__version__ = "0.1.0"
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "_lib" / "libverbo_cuda.so"
+
+
+class VerboCudaError(RuntimeError):
+    pass
+
+
+class _Sampling(ctypes.Structure):
+    _fields_ = [
+        ("temp", ctypes.c_float),
+        ("top_k", ctypes.c_int),
+        ("top_p", ctypes.c_float),
+        ("min_p", ctypes.c_float),
+        ("repeat", ctypes.c_float),
+        ("repeat_last", ctypes.c_int),
+        ("seed", ctypes.c_ulonglong),
+    ]
+
+
+class _RowStats(ctypes.Structure):
+    _fields_ = [
+        ("sum", ctypes.c_double),
+        ("tot", ctypes.c_double),
+        ("u", ctypes.c_double),
+        ("draw_margin", ctypes.c_double),
+        ("cut_margin", ctypes.c_double),
+        ("k", ctypes.c_int),
+        ("keep", ctypes.c_int),
+        ("id", ctypes.c_int),
+        ("greedy", ctypes.c_int),
+    ]
+
+
+ROW_STATS_FIELDS = [f for f, _ in _RowStats._fields_]
+ROW_STATS_BYTES = ctypes.sizeof(_RowStats)
+
+
+@dataclass
+class Sampling:
+    """verbo::Sampling with the reference defaults (include/verbo/verbo.hpp:56-64).
+
+    Option names follow the CLI flags --temp/--top-k/--top-p/--min-p/--repeat/
+    --seed (cli/common.hpp:72-77); ``repeat_last`` is the penalty window."""
+
+    temp: float = 0.7
+    top_k: int = 40
+    top_p: float = 0.9
+    min_p: float = 0.0
+    repeat: float = 1.0
+    repeat_last: int = 64
+    seed: int = 0
+
+    def _c(self) -> _Sampling:
+        return _Sampling(self.temp, self.top_k, self.top_p, self.min_p, self.repeat, self.repeat_last, self.seed)
+
+
+_lib = None
+_P = ctypes.c_void_p
+
+
+def load_library():
+    """Loads libverbo_cuda.so (override with VERBO_CUDA_LIB).  Raises if it is
+    missing: there is no fallback implementation."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = Path(os.environ.get("VERBO_CUDA_LIB", LIB_PATH))
+    if not path.is_file():
+        raise VerboCudaError(f"{path} not found: build it with `python -m verbo_b200.build`")
+    lib = ctypes.CDLL(str(path))
+    sig = {
+        "verbo_cuda_last_error": (ctypes.c_char_p, []),
+        "verbo_cuda_version": (ctypes.c_char_p, []),
+        "verbo_cuda_default_sampling": (_Sampling, []),
+        "verbo_cuda_rng_seed": (ctypes.c_int, [ctypes.c_ulonglong, _P]),
+        "verbo_cuda_rng_unit": (ctypes.c_double, [_P]),
+        "verbo_cuda_sample": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, _P, _P,
+                                             ctypes.POINTER(_Sampling), _P, _P, _P, _P]),
+        "verbo_cuda_shard_topk": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, ctypes.c_int,
+                                                 ctypes.c_int, _P, _P, ctypes.POINTER(_Sampling), ctypes.c_int,
+                                                 _P, _P, _P]),
+        "verbo_cuda_merge_sample": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                   ctypes.POINTER(_Sampling), _P, _P, _P, _P]),
+        "verbo_cuda_check": (ctypes.c_int, [_P]),
+        "verbo_cuda_sampler_new": (_P, [ctypes.POINTER(_Sampling), ctypes.c_int]),
+        "verbo_cuda_sampler_free": (None, [_P]),
+        "verbo_cuda_sampler_pick": (ctypes.c_int, [_P, _P, ctypes.c_int]),
+        "verbo_cuda_sampler_accept": (ctypes.c_int, [_P, ctypes.c_int]),
+        "verbo_cuda_sampler_reset": (ctypes.c_int, [_P]),
+        "verbo_cuda_sampler_cfg": (ctypes.c_int, [_P, ctypes.POINTER(_Sampling)]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def _err() -> VerboCudaError:
+    return VerboCudaError(load_library().verbo_cuda_last_error().decode())
+
+
+def _ok(rc: int) -> int:
+    if rc < 0:
+        raise _err()
+    return rc
+
+
+def version() -> str:
+    return load_library().verbo_cuda_version().decode()
+
+
+def _dptr(t) -> Optional[int]:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise VerboCudaError("batched entry points take CUDA tensors")
+    if not t.is_contiguous():
+        raise VerboCudaError("tensors must be contiguous")
+    return t.data_ptr()
+
+
+def _stream(stream) -> Optional[int]:
+    if stream is None:
+        import torch
+
+        return torch.cuda.current_stream().cuda_stream
+    return getattr(stream, "cuda_stream", stream)
+
+
+def seed_states(seeds: Sequence[int]):
+    """Host list of per-row [s0, s1] states seeded like Sampler::reset
+    (src/sampler.cpp:26-31; seed 0 takes the clock)."""
+    lib = load_library()
+    out = []
+    st = (ctypes.c_ulonglong * 2)()
+    for s in seeds:
+        _ok(lib.verbo_cuda_rng_seed(int(s), st))
+        out.append([st[0], st[1]])
+    return out
+
+
+def sample(logits, opts: Sampling, rng=None, hist=None, hist_off=None, out=None, stats=None, vocab=None,
+           stream=None):
+    """Sampler::pick for each row of `logits` (CUDA float32 [rows, ld]).
+
+    rng: CUDA int64/uint64 tensor [rows, 2] advanced in place (required when
+    temp > 0).  hist/hist_off: CUDA int32 ids and int64 CSR offsets [rows+1].
+    stats: optional CUDA uint8 tensor of rows * ROW_STATS_BYTES.  Returns the
+    int32 id tensor (asynchronous on `stream`)."""
+    import torch
+
+    rows, ld = logits.shape
+    vocab = ld if vocab is None else vocab
+    if logits.dtype != torch.float32:
+        raise VerboCudaError("logits must be float32")
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    o = opts._c()
+    rc = load_library().verbo_cuda_sample(_dptr(logits), rows, vocab, ld, _dptr(hist), _dptr(hist_off),
+                                          ctypes.byref(o), _dptr(rng), _dptr(out), _dptr(stats), _stream(stream))
+    _ok(rc)
+    return out
+
+
+def shard_topk(shard, col_offset: int, vocab: int, opts: Sampling, k: int, hist=None, hist_off=None,
+               cand_val=None, cand_id=None, stream=None):
+    """A shard's k best (value, global id) per row: shard is CUDA float32
+    [rows, ld] holding global columns [col_offset, col_offset + cols)."""
+    import torch
+
+    rows, cols = shard.shape
+    if cand_val is None:
+        cand_val = torch.empty(rows, k, dtype=torch.float32, device=shard.device)
+    if cand_id is None:
+        cand_id = torch.empty(rows, k, dtype=torch.int32, device=shard.device)
+    o = opts._c()
+    _ok(load_library().verbo_cuda_shard_topk(_dptr(shard), rows, cols, shard.stride(0), col_offset, vocab,
+                                             _dptr(hist), _dptr(hist_off), ctypes.byref(o), k, _dptr(cand_val),
+                                             _dptr(cand_id), _stream(stream)))
+    return cand_val, cand_id
+
+
+def merge_sample(cand_val, cand_id, vocab: int, opts: Sampling, rng=None, out=None, stats=None, stream=None):
+    """Merges candidates laid out [nshards, rows, k] and finishes the pick."""
+    import torch
+
+    nshards, rows, k = cand_val.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=cand_val.device)
+    o = opts._c()
+    _ok(load_library().verbo_cuda_merge_sample(_dptr(cand_val), _dptr(cand_id), rows, nshards, k, vocab,
+                                               ctypes.byref(o), _dptr(rng), _dptr(out), _dptr(stats),
+                                               _stream(stream)))
+    return out
+
+
+def check(stream=None) -> None:
+    """Synchronises the stream and raises if a kernel recorded a failure."""
+    _ok(load_library().verbo_cuda_check(_stream(stream)))
+
+
+class Sampler:
+    """verbo::Sampler (include/verbo/verbo.hpp:116-132) on a CUDA device.
+
+    ``pick`` takes a host buffer (numpy float32 or any object exposing the
+    buffer protocol / a ctypes address) or a CUDA tensor."""
+
+    def __init__(self, cfg: Optional[Sampling] = None, device: int = 0):
+        self._lib = load_library()
+        self._cfg = cfg if cfg is not None else Sampling()
+        c = self._cfg._c()
+        h = self._lib.verbo_cuda_sampler_new(ctypes.byref(c), device)
+        if not h:
+            raise _err()
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.verbo_cuda_sampler_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def pick(self, logits, n: Optional[int] = None) -> int:
+        if hasattr(logits, "is_cuda") and logits.is_cuda:
+            ptr, size = logits.data_ptr(), logits.numel()
+        else:
+            import numpy as np
+
+            arr = np.ascontiguousarray(logits, dtype=np.float32)
+            self._keep = arr
+            ptr, size = arr.ctypes.data, arr.size
+        return _ok(self._lib.verbo_cuda_sampler_pick(self._h, ptr, size if n is None else n))
+
+    def accept(self, tok: int) -> None:
+        _ok(self._lib.verbo_cuda_sampler_accept(self._h, int(tok)))
+
+    def reset(self) -> None:
+        _ok(self._lib.verbo_cuda_sampler_reset(self._h))
+
+    def cfg(self) -> Sampling:
+        c = _Sampling()
+        _ok(self._lib.verbo_cuda_sampler_cfg(self._h, ctypes.byref(c)))
+        return Sampling(c.temp, c.top_k, c.top_p, c.min_p, c.repeat, c.repeat_last, c.seed)

@@ -1,0 +1,427 @@
+// C ABI of the B200 sampler (include/verbo_cuda.h).  Mirrors the conventions
+// of the reference's C ABI (src/capi.cpp): every entry point runs inside
+// guard(), which turns exceptions into a -1 / NULL return and a thread-local
+// message for verbo_cuda_last_error().  No compute happens here: the host
+// validates arguments, plans the cluster split and launches the kernels of
+// kernels.cu.  There is no CPU fallback.
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+#include "verbo_cuda.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+template <typename F>
+auto guard(F&& fn, decltype(fn()) fail) -> decltype(fn()) {
+  try {
+    g_err.clear();
+    return fn();
+  } catch (const std::exception& e) {
+    g_err = e.what();
+  } catch (...) {
+    g_err = "verbo_cuda: unknown error";
+  }
+  return fail;
+}
+
+[[noreturn]] void fail(const std::string& m) { throw std::runtime_error("verbo_cuda: " + m); }
+
+void cuda_ok(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) fail(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int bitlen(unsigned long long x) {
+  int b = 0;
+  while (x) {
+    ++b;
+    x >>= 1;
+  }
+  return b;
+}
+
+// splitmix64, as src/sampler.cpp:11-16.
+unsigned long long splitmix(unsigned long long& s) {
+  unsigned long long z = (s += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Sampler::reset seeding, src/sampler.cpp:26-31 (seed 0 = clock, like the reference).
+void seed_state(unsigned long long seed, unsigned long long st[2]) {
+  unsigned long long s = seed;
+  if (s == 0) {
+    const double ms =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+    s = static_cast<unsigned long long>(ms * 1000.0);
+  }
+  st[0] = splitmix(s);
+  st[1] = splitmix(s);
+}
+
+vb::DevOpts make_opts(const verbo_sampling& s, int vocab, bool have_hist) {
+  if (!std::isfinite(s.temp)) fail("temp must be finite");
+  vb::DevOpts o{};
+  o.temp = s.temp;
+  o.top_p = s.top_p;
+  o.min_p = s.min_p;
+  o.repeat = s.repeat;
+  o.top_k = s.top_k;
+  o.repeat_last = s.repeat_last;
+  o.k = (s.top_k > 0 && s.top_k < vocab) ? s.top_k : vocab;
+  o.greedy = s.temp <= 0.0f ? 1 : 0;
+  o.penalize = (have_hist && s.repeat != 1.0f) ? 1 : 0;
+  o.vocab = vocab;
+  o.inv_temp = o.greedy ? 0.0 : 1.0 / static_cast<double>(s.temp);
+  return o;
+}
+
+// Split `ncols` columns over a cluster of C CTAs (a power of two, at most 8)
+// with slices of about 8192 columns or more; slices are multiples of 4.
+void plan(int ncols, int& C, int& slice) {
+  C = 1;
+  while (C < 8 && static_cast<long long>(C) * 8192 < ncols) C <<= 1;
+  slice = (ncols + C - 1) / C;
+  slice = (slice + 3) & ~3;
+}
+
+vb::RowArgs row_args(const float* logits, int rows, int ncols, long long ld, int col_off, int vocab,
+                     const int* hist, const long long* hist_off) {
+  vb::RowArgs a{};
+  a.logits = logits;
+  a.ld = ld;
+  a.rows = rows;
+  a.ncols = ncols;
+  a.col_off = col_off;
+  a.hist = hist;
+  a.hist_off = hist_off;
+  a.idxbits = bitlen(static_cast<unsigned long long>(vocab - 1));
+  if (a.idxbits < 1) a.idxbits = 1;
+  a.fixbits = 63 - bitlen(static_cast<unsigned long long>(vocab));
+  plan(ncols, a.cluster, a.slice);
+  return a;
+}
+
+void check_hist(const int* hist, const long long* hist_off) {
+  if ((hist == nullptr) != (hist_off == nullptr)) fail("hist and hist_off must both be given or both be NULL");
+}
+
+int sample_impl(const float* logits, int rows, int vocab, long long ld, const int* hist, const long long* hist_off,
+                const verbo_sampling* opts, unsigned long long* rng, int* out_ids, verbo_row_stats* stats,
+                cudaStream_t s) {
+  if (!opts) fail("opts is NULL");
+  if (rows < 0) fail("rows must be >= 0");
+  if (rows == 0) return 0;
+  if (!logits || !out_ids) fail("logits and out_ids must not be NULL");
+  if (vocab < 1 || vocab > vb::kMaxVocab) fail("vocab must be in [1, " + std::to_string(vb::kMaxVocab) + "]");
+  if (ld < vocab) fail("ld must be >= vocab");
+  check_hist(hist, hist_off);
+  const vb::DevOpts o = make_opts(*opts, vocab, hist != nullptr);
+  if (!o.greedy && !rng) fail("rng state is required when temp > 0");
+  vb::RowArgs a = row_args(logits, rows, vocab, ld, 0, vocab, hist, hist_off);
+  a.rng = rng;
+  a.out_ids = out_ids;
+  a.stats = stats;
+  cudaError_t e;
+  if (o.greedy)
+    e = vb::launch_greedy(a, o, s);
+  else if (o.k < vocab && o.k <= vb::kMaxK)
+    e = vb::launch_topk(a, o, false, s);
+  else
+    e = vb::launch_general(a, o, s);
+  cuda_ok(e, "kernel launch");
+  return 0;
+}
+
+}  // namespace
+
+struct verbo_cuda_sampler {
+  verbo_sampling cfg{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<int> hist;
+  float* d_row = nullptr;
+  int row_cap = 0;
+  int* d_hist = nullptr;
+  int hist_cap = 0;
+  long long* d_off = nullptr;
+  unsigned long long* d_rng = nullptr;
+  int* d_out = nullptr;
+  int* h_out = nullptr;  // pinned
+};
+
+namespace {
+
+void sampler_release(verbo_cuda_sampler* s) {
+  if (!s) return;
+  cudaSetDevice(s->device);
+  if (s->stream) cudaStreamSynchronize(s->stream);
+  cudaFree(s->d_row);
+  cudaFree(s->d_hist);
+  cudaFree(s->d_off);
+  cudaFree(s->d_rng);
+  cudaFree(s->d_out);
+  cudaFreeHost(s->h_out);
+  if (s->stream) cudaStreamDestroy(s->stream);
+}
+
+void sampler_reset(verbo_cuda_sampler* s) {
+  unsigned long long st[2];
+  seed_state(s->cfg.seed, st);
+  cuda_ok(cudaSetDevice(s->device), "cudaSetDevice");
+  cuda_ok(cudaMemcpyAsync(s->d_rng, st, sizeof(st), cudaMemcpyHostToDevice, s->stream), "upload rng");
+  cuda_ok(cudaStreamSynchronize(s->stream), "sync");
+  s->hist.clear();
+}
+
+}  // namespace
+
+extern "C" {
+
+VERBO_CUDA_API const char* verbo_cuda_last_error(void) { return g_err.c_str(); }
+
+VERBO_CUDA_API const char* verbo_cuda_version(void) { return "0.1.0-sm100a"; }
+
+VERBO_CUDA_API verbo_sampling verbo_cuda_default_sampling(void) {
+  verbo_sampling s;
+  s.temp = 0.7f;
+  s.top_k = 40;
+  s.top_p = 0.9f;
+  s.min_p = 0.0f;
+  s.repeat = 1.0f;
+  s.repeat_last = 64;
+  s.seed = 0;
+  return s;
+}
+
+VERBO_CUDA_API int verbo_cuda_rng_seed(unsigned long long seed, unsigned long long state[2]) {
+  return guard(
+      [&]() {
+        if (!state) fail("state is NULL");
+        seed_state(seed, state);
+        return 0;
+      },
+      -1);
+}
+
+VERBO_CUDA_API double verbo_cuda_rng_unit(unsigned long long st[2]) {
+  unsigned long long s1 = st[0];
+  const unsigned long long s0 = st[1];
+  const unsigned long long r = s0 + s1;
+  st[0] = s0;
+  s1 ^= s1 << 23;
+  st[1] = s1 ^ s0 ^ (s1 >> 18) ^ (s0 >> 5);
+  return static_cast<double>(r >> 11) * (1.0 / 9007199254740992.0);
+}
+
+VERBO_CUDA_API int verbo_cuda_sample(const float* logits, int rows, int vocab, long long ld, const int* hist,
+                                     const long long* hist_off, const verbo_sampling* opts, unsigned long long* rng,
+                                     int* out_ids, verbo_row_stats* stats, void* stream) {
+  return guard(
+      [&]() {
+        return sample_impl(logits, rows, vocab, ld, hist, hist_off, opts, rng, out_ids, stats,
+                           static_cast<cudaStream_t>(stream));
+      },
+      -1);
+}
+
+VERBO_CUDA_API int verbo_cuda_shard_topk(const float* logits, int rows, int shard_cols, long long ld, int col_offset,
+                                         int vocab, const int* hist, const long long* hist_off,
+                                         const verbo_sampling* opts, int k, float* cand_val, int* cand_id,
+                                         void* stream) {
+  return guard(
+      [&]() {
+        if (!opts) fail("opts is NULL");
+        if (rows < 0) fail("rows must be >= 0");
+        if (rows == 0) return 0;
+        if (!logits || !cand_val || !cand_id) fail("logits, cand_val and cand_id must not be NULL");
+        if (k < 1 || k > vb::kMaxK) fail("k must be in [1, " + std::to_string(vb::kMaxK) + "]");
+        if (vocab < 1 || vocab > vb::kMaxVocab) fail("vocab must be in [1, " + std::to_string(vb::kMaxVocab) + "]");
+        if (shard_cols < 1 || col_offset < 0 || static_cast<long long>(col_offset) + shard_cols > vocab)
+          fail("shard [col_offset, col_offset + shard_cols) must lie in [0, vocab)");
+        if (ld < shard_cols) fail("ld must be >= shard_cols");
+        check_hist(hist, hist_off);
+        vb::DevOpts o = make_opts(*opts, vocab, hist != nullptr);
+        vb::RowArgs a = row_args(logits, rows, shard_cols, ld, col_offset, vocab, hist, hist_off);
+        a.cand_val = cand_val;
+        a.cand_id = cand_id;
+        a.cand_k = k;
+        cuda_ok(vb::launch_topk(a, o, true, static_cast<cudaStream_t>(stream)), "kernel launch");
+        return 0;
+      },
+      -1);
+}
+
+VERBO_CUDA_API int verbo_cuda_merge_sample(const float* cand_val, const int* cand_id, int rows, int nshards, int k,
+                                           int vocab, const verbo_sampling* opts, unsigned long long* rng,
+                                           int* out_ids, verbo_row_stats* stats, void* stream) {
+  return guard(
+      [&]() {
+        if (!opts) fail("opts is NULL");
+        if (rows < 0) fail("rows must be >= 0");
+        if (rows == 0) return 0;
+        if (!cand_val || !cand_id || !out_ids) fail("cand_val, cand_id and out_ids must not be NULL");
+        if (nshards < 1 || k < 1 || static_cast<long long>(nshards) * k > vb::kMaxMerge)
+          fail("nshards * k must be in [1, " + std::to_string(vb::kMaxMerge) + "]");
+        if (k > vb::kMaxK) fail("k must be <= " + std::to_string(vb::kMaxK));
+        if (vocab < 1) fail("vocab must be >= 1");
+        vb::DevOpts o = make_opts(*opts, vocab, false);
+        if (!o.greedy && !(opts->top_k > 0 && opts->top_k <= k && opts->top_k < vocab))
+          fail("vocab-sharded sampling needs temp <= 0 or 0 < top_k <= k");
+        if (!o.greedy && !rng) fail("rng state is required when temp > 0");
+        vb::MergeArgs a{};
+        a.cand_val = cand_val;
+        a.cand_id = cand_id;
+        a.rows = rows;
+        a.nshards = nshards;
+        a.k = k;
+        a.rng = rng;
+        a.out_ids = out_ids;
+        a.stats = stats;
+        cuda_ok(vb::launch_merge(a, o, static_cast<cudaStream_t>(stream)), "kernel launch");
+        return 0;
+      },
+      -1);
+}
+
+VERBO_CUDA_API int verbo_cuda_check(void* stream) {
+  return guard(
+      [&]() {
+        unsigned st = 0;
+        cuda_ok(vb::read_status(&st, true, static_cast<cudaStream_t>(stream)), "stream");
+        if (st & vb::kErrLoadTimeout) fail("a row load did not complete within the wait limit");
+        if (st & vb::kErrSelect) fail("a selection found no element (inconsistent input)");
+        if (st) fail("device status " + std::to_string(st));
+        return 0;
+      },
+      -1);
+}
+
+VERBO_CUDA_API verbo_cuda_sampler* verbo_cuda_sampler_new(const verbo_sampling* cfg, int device) {
+  return guard(
+      [&]() -> verbo_cuda_sampler* {
+        auto* s = new verbo_cuda_sampler();
+        try {
+          s->cfg = cfg ? *cfg : verbo_cuda_default_sampling();
+          if (!std::isfinite(s->cfg.temp)) fail("temp must be finite");
+          s->device = device;
+          cuda_ok(cudaSetDevice(device), "cudaSetDevice");
+          cuda_ok(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+          cuda_ok(cudaMalloc(&s->d_rng, 2 * sizeof(unsigned long long)), "cudaMalloc");
+          cuda_ok(cudaMalloc(&s->d_out, sizeof(int)), "cudaMalloc");
+          cuda_ok(cudaMalloc(&s->d_off, 2 * sizeof(long long)), "cudaMalloc");
+          cuda_ok(cudaMallocHost(&s->h_out, sizeof(int)), "cudaMallocHost");
+          sampler_reset(s);
+        } catch (...) {
+          sampler_release(s);
+          delete s;
+          throw;
+        }
+        return s;
+      },
+      nullptr);
+}
+
+VERBO_CUDA_API void verbo_cuda_sampler_free(verbo_cuda_sampler* s) {
+  if (!s) return;
+  sampler_release(s);
+  delete s;
+}
+
+VERBO_CUDA_API int verbo_cuda_sampler_pick(verbo_cuda_sampler* s, const float* logits, int n) {
+  return guard(
+      [&]() {
+        if (!s || !logits) fail("sampler and logits must not be NULL");
+        if (n < 1) fail("n must be >= 1");
+        cuda_ok(cudaSetDevice(s->device), "cudaSetDevice");
+        cudaPointerAttributes pa{};
+        cuda_ok(cudaPointerGetAttributes(&pa, logits), "cudaPointerGetAttributes");
+        const float* row = logits;
+        if (pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged) {
+          if (n > s->row_cap) {
+            cudaFree(s->d_row);
+            s->d_row = nullptr;
+            s->row_cap = 0;
+            cuda_ok(cudaMalloc(&s->d_row, static_cast<size_t>(n) * sizeof(float)), "cudaMalloc");
+            s->row_cap = n;
+          }
+          cuda_ok(cudaMemcpyAsync(s->d_row, logits, static_cast<size_t>(n) * sizeof(float), cudaMemcpyHostToDevice,
+                                  s->stream),
+                  "upload logits");
+          row = s->d_row;
+        }
+        // penalty window: the last repeat_last accepted ids (src/sampler.cpp:53-57)
+        const int* dh = nullptr;
+        const long long* doff = nullptr;
+        if (s->cfg.repeat != 1.0f && !s->hist.empty()) {
+          const size_t len = s->hist.size();
+          const size_t from =
+              (s->cfg.repeat_last > 0 && len > static_cast<size_t>(s->cfg.repeat_last)) ? len - s->cfg.repeat_last : 0;
+          const int w = static_cast<int>(len - from);
+          if (w > s->hist_cap) {
+            cudaFree(s->d_hist);
+            s->d_hist = nullptr;
+            s->hist_cap = 0;
+            cuda_ok(cudaMalloc(&s->d_hist, static_cast<size_t>(w) * sizeof(int)), "cudaMalloc");
+            s->hist_cap = w;
+          }
+          const long long off[2] = {0, w};
+          cuda_ok(cudaMemcpyAsync(s->d_hist, s->hist.data() + from, static_cast<size_t>(w) * sizeof(int),
+                                  cudaMemcpyHostToDevice, s->stream),
+                  "upload history");
+          cuda_ok(cudaMemcpyAsync(s->d_off, off, sizeof(off), cudaMemcpyHostToDevice, s->stream), "upload history");
+          cuda_ok(cudaStreamSynchronize(s->stream), "sync");
+          dh = s->d_hist;
+          doff = s->d_off;
+        }
+        sample_impl(row, 1, n, n, dh, doff, &s->cfg, s->d_rng, s->d_out, nullptr, s->stream);
+        cuda_ok(cudaMemcpyAsync(s->h_out, s->d_out, sizeof(int), cudaMemcpyDeviceToHost, s->stream), "read id");
+        cuda_ok(cudaStreamSynchronize(s->stream), "sync");
+        return *s->h_out;
+      },
+      -1);
+}
+
+VERBO_CUDA_API int verbo_cuda_sampler_accept(verbo_cuda_sampler* s, int tok) {
+  return guard(
+      [&]() {
+        if (!s) fail("sampler is NULL");
+        // Sampler::accept (src/sampler.cpp:43-48)
+        s->hist.push_back(tok);
+        if (s->cfg.repeat_last > 0 && s->hist.size() > static_cast<size_t>(s->cfg.repeat_last) * 4)
+          s->hist.erase(s->hist.begin(), s->hist.end() - s->cfg.repeat_last);
+        return 0;
+      },
+      -1);
+}
+
+VERBO_CUDA_API int verbo_cuda_sampler_reset(verbo_cuda_sampler* s) {
+  return guard(
+      [&]() {
+        if (!s) fail("sampler is NULL");
+        sampler_reset(s);
+        return 0;
+      },
+      -1);
+}
+
+VERBO_CUDA_API int verbo_cuda_sampler_cfg(const verbo_cuda_sampler* s, verbo_sampling* out) {
+  return guard(
+      [&]() {
+        if (!s || !out) fail("sampler and out must not be NULL");
+        *out = s->cfg;
+        return 0;
+      },
+      -1);
+}
+
+}  // extern "C"

@@ -1,0 +1,72 @@
+// Launch-side view of the sampling kernels (shared by kernels.cu and capi.cpp).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "verbo_cuda.h"
+
+namespace vb {
+
+constexpr int kMaxK = 1024;       // largest top_k handled by the streaming top-k kernel
+constexpr int kCandCap = 2048;    // candidate buffer of that kernel (CTA rank 0)
+constexpr int kMaxSlice = 40960;  // largest per-CTA slice of a row (floats) in the staged kernel
+constexpr int kMaxVocab = kMaxSlice * 8;
+constexpr int kMaxMerge = 4096;   // nshards * k candidates merged per row
+
+// Error bits recorded in the device status word (read by verbo_cuda_check).
+constexpr unsigned kErrLoadTimeout = 1u;  // a bulk copy did not complete within the wait limit
+constexpr unsigned kErrSelect = 2u;       // a selection found no element
+
+// Sampling options as the kernels use them (built on the host from verbo_sampling).
+struct DevOpts {
+  float temp, top_p, min_p, repeat;
+  int top_k, repeat_last;
+  int k;         // candidate count of Sampler::pick: top_k if 0 < top_k < vocab, else vocab
+  int greedy;    // temp <= 0
+  int penalize;  // repeat != 1 and histories given
+  int vocab;     // full vocabulary
+  double inv_temp;
+};
+
+struct RowArgs {
+  const float* logits;
+  long long ld;
+  int rows;
+  int ncols;    // columns processed per row (vocab, or a shard's width)
+  int col_off;  // global id of column 0 (shards)
+  const int* hist;
+  const long long* hist_off;
+  unsigned long long* rng;  // 2 per row
+  int* out_ids;
+  verbo_row_stats* stats;
+  float* cand_val;  // shard candidates out, [rows][cand_k]
+  int* cand_id;
+  int cand_k;
+  int cluster;  // CTAs per row
+  int slice;    // columns per CTA (multiple of 4)
+  int idxbits;  // bits of the largest global id
+  int fixbits;  // fixed-point fraction bits of the staged kernel's masses
+};
+
+struct MergeArgs {
+  const float* cand_val;  // [nshards][rows][k]
+  const int* cand_id;
+  int rows, nshards, k;
+  unsigned long long* rng;
+  int* out_ids;
+  verbo_row_stats* stats;
+};
+
+// Host launchers (kernels.cu).  Return a cudaError_t.
+cudaError_t launch_greedy(const RowArgs& a, const DevOpts& o, cudaStream_t s);
+cudaError_t launch_topk(const RowArgs& a, const DevOpts& o, bool emit, cudaStream_t s);
+cudaError_t launch_general(const RowArgs& a, const DevOpts& o, cudaStream_t s);
+cudaError_t launch_merge(const MergeArgs& a, const DevOpts& o, cudaStream_t s);
+size_t greedy_smem(int slice);
+size_t topk_smem(int slice);
+size_t general_smem(int slice);
+size_t merge_smem(int n);
+cudaError_t read_status(unsigned* st, bool clear, cudaStream_t s);
+
+}  // namespace vb
