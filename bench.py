@@ -58,6 +58,8 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=0, help="steps of the host-buffer measurement (default min(K, 10))")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-soak", action="store_true", help="skip the 1 s load window kept for the clock record")
+    p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
     a = p.parse_args()
     if a.warmup < 3:
         p.error("--warmup must be >= 3")
@@ -212,6 +214,7 @@ def bench_rows(a, w: wl.Workload, rank: int, world: int, dev):
     clocks = Clocks(torch.cuda.current_device()) if rank == 0 else None
     if clocks:
         clocks.start()
+    if clocks and not a.no_soak:
         t_soak = time.perf_counter()
         i = 0
         while time.perf_counter() - t_soak < 1.0:   # >= 1 s of load around the timed region for the clock record
@@ -243,10 +246,31 @@ def bench_rows(a, w: wl.Workload, rank: int, world: int, dev):
         dist.all_reduce(red, op=dist.ReduceOp.MAX)
     elapsed, launch_ms = red.tolist()
 
-    # end to end through the public call with host buffers
+    res = dict(R=R, elapsed_ms=elapsed, launch_ms=launch_ms, copies=copies, batch_bytes=batch_bytes,
+               launches=a.steps, clocks=clocks.summary() if clocks else None)
+    if not a.no_e2e:
+        res.update(e2e_rows(a, w, R, V, xs[0], h, off, opts, rng, out, stream, world, dev))
+    host_sample = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        from oracle import pyoracle as po
+
+        thr = po.host_threads()
+        n = min(R, host_rows_for_budget(w, a.cpu_seconds, thr, R))
+        host_sample = (xs[0][:n].cpu().numpy(), None if h is None else h[: n * w.hist_len].cpu().numpy(),
+                       None if off is None else off[: n + 1].cpu().numpy())
+    return res, host_sample
+
+
+def e2e_rows(a, w, R, V, x0, h, off, opts, rng, out, stream, world, dev):
+    """The same metric through the public call with host buffers."""
+    import torch
+    import torch.distributed as dist
+
+    import verbo_b200 as vb
+
     e2e_steps = a.e2e_steps or min(a.steps, 10)
     hx = torch.empty((R, V), dtype=torch.float32, pin_memory=True)
-    hx.copy_(xs[0])
+    hx.copy_(x0)
     hh = None if h is None else torch.empty(h.shape, dtype=h.dtype, pin_memory=True).copy_(h)
     ho = None if off is None else torch.empty(off.shape, dtype=off.dtype, pin_memory=True).copy_(off)
     ids_host = torch.empty(R, dtype=torch.int32, pin_memory=True)
@@ -281,18 +305,7 @@ def bench_rows(a, w: wl.Workload, rank: int, world: int, dev):
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e_ms.item())
-
-    res = dict(R=R, elapsed_ms=elapsed, launch_ms=launch_ms, e2e_ms=e2e_ms, e2e_steps=e2e_steps, h2d=h2d, d2h=d2h,
-               copies=copies, batch_bytes=batch_bytes, launches=a.steps, clocks=clocks.summary() if clocks else None)
-    host_sample = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        from oracle import pyoracle as po
-
-        thr = po.host_threads()
-        n = min(R, host_rows_for_budget(w, a.cpu_seconds, thr, R))
-        host_sample = (xs[0][:n].cpu().numpy(), None if h is None else h[: n * w.hist_len].cpu().numpy(),
-                       None if off is None else off[: n + 1].cpu().numpy())
-    return res, host_sample
+    return dict(e2e_ms=e2e_ms, e2e_steps=e2e_steps, h2d=h2d, d2h=d2h)
 
 
 # -------------------------------------------------- vocab-sharded config (c5) ----
@@ -351,7 +364,7 @@ def bench_sharded(a, w: wl.Workload, rank: int, world: int, dev):
         clocks.start()
     t_soak = time.perf_counter()
     i = 0
-    while True:   # the same number of soak steps on every rank (collectives must match)
+    while not a.no_soak:   # the same number of soak steps on every rank (collectives must match)
         step(i)
         i += 1
         done = torch.tensor([1.0 if time.perf_counter() - t_soak >= 1.0 else 0.0], device=dev)
@@ -491,7 +504,7 @@ def main():
         "clocks": res["clocks"],
         "gpu_launches": res["launches"] * world,
     }
-    if not sharded:
+    if not sharded and "e2e_ms" in res:
         line["e2e"] = {"value": rows_job * res["e2e_steps"] / (res["e2e_ms"] / 1000.0), "unit": "rows/s",
                        "h2d_bytes_per_step": res["h2d"] * world, "d2h_bytes_per_step": res["d2h"] * world}
     else:

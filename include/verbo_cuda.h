@@ -86,7 +86,7 @@ VERBO_CUDA_API double verbo_cuda_rng_unit(unsigned long long state[2]);
 /* Sampler::pick (src/sampler.cpp:50-109) for `rows` device-resident rows with
    one option set.  Writes out_ids[r] (device).  rng may be NULL only when
    opts->temp <= 0 (greedy consumes no draw).  stats may be NULL.
-   Limits: 1 <= vocab <= 327680, ld >= vocab, finite temp. */
+   Limits: 1 <= vocab <= 327680, ld >= vocab, temp not NaN or +inf. */
 VERBO_CUDA_API int verbo_cuda_sample(const float* logits, int rows, int vocab, long long ld, const int* hist,
                                      const long long* hist_off, const verbo_sampling* opts,
                                      unsigned long long* rng, int* out_ids, verbo_row_stats* stats,

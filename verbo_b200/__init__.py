@@ -144,12 +144,18 @@ def version() -> str:
     return load_library().verbo_cuda_version().decode()
 
 
-def _dptr(t) -> Optional[int]:
+def _dptr(t, rows_strided: bool = False) -> Optional[int]:
+    """Device address of a CUDA tensor.  With rows_strided, a 2-D view whose
+    rows are contiguous but spaced by stride(0) (e.g. a column shard) is
+    accepted; the caller passes stride(0) as the leading dimension."""
     if t is None:
         return None
     if not t.is_cuda:
         raise VerboCudaError("batched entry points take CUDA tensors")
-    if not t.is_contiguous():
+    if rows_strided:
+        if t.dim() != 2 or (t.shape[1] > 1 and t.stride(1) != 1):
+            raise VerboCudaError("rows must be contiguous (stride(1) == 1)")
+    elif not t.is_contiguous():
         raise VerboCudaError("tensors must be contiguous")
     return t.data_ptr()
 
@@ -184,14 +190,15 @@ def sample(logits, opts: Sampling, rng=None, hist=None, hist_off=None, out=None,
     int32 id tensor (asynchronous on `stream`)."""
     import torch
 
-    rows, ld = logits.shape
-    vocab = ld if vocab is None else vocab
+    rows, cols = logits.shape
+    vocab = cols if vocab is None else vocab
     if logits.dtype != torch.float32:
         raise VerboCudaError("logits must be float32")
     if out is None:
         out = torch.empty(rows, dtype=torch.int32, device=logits.device)
     o = opts._c()
-    rc = load_library().verbo_cuda_sample(_dptr(logits), rows, vocab, ld, _dptr(hist), _dptr(hist_off),
+    rc = load_library().verbo_cuda_sample(_dptr(logits, True), rows, vocab, logits.stride(0), _dptr(hist),
+                                          _dptr(hist_off),
                                           ctypes.byref(o), _dptr(rng), _dptr(out), _dptr(stats), _stream(stream))
     _ok(rc)
     return out
@@ -209,7 +216,7 @@ def shard_topk(shard, col_offset: int, vocab: int, opts: Sampling, k: int, hist=
     if cand_id is None:
         cand_id = torch.empty(rows, k, dtype=torch.int32, device=shard.device)
     o = opts._c()
-    _ok(load_library().verbo_cuda_shard_topk(_dptr(shard), rows, cols, shard.stride(0), col_offset, vocab,
+    _ok(load_library().verbo_cuda_shard_topk(_dptr(shard, True), rows, cols, shard.stride(0), col_offset, vocab,
                                              _dptr(hist), _dptr(hist_off), ctypes.byref(o), k, _dptr(cand_val),
                                              _dptr(cand_id), _stream(stream)))
     return cand_val, cand_id

@@ -68,8 +68,10 @@ void seed_state(unsigned long long seed, unsigned long long st[2]) {
   st[1] = splitmix(s);
 }
 
+// temp <= 0 (including -inf) is greedy, as in the reference; NaN and +inf
+// would make every softmax weight NaN and are rejected.
 vb::DevOpts make_opts(const verbo_sampling& s, int vocab, bool have_hist) {
-  if (!std::isfinite(s.temp)) fail("temp must be finite");
+  if (std::isnan(s.temp) || s.temp == INFINITY) fail("temp must not be NaN or +inf");
   vb::DevOpts o{};
   o.temp = s.temp;
   o.top_p = s.top_p;
@@ -312,7 +314,7 @@ VERBO_CUDA_API verbo_cuda_sampler* verbo_cuda_sampler_new(const verbo_sampling* 
         auto* s = new verbo_cuda_sampler();
         try {
           s->cfg = cfg ? *cfg : verbo_cuda_default_sampling();
-          if (!std::isfinite(s->cfg.temp)) fail("temp must be finite");
+          if (std::isnan(s->cfg.temp) || s->cfg.temp == INFINITY) fail("temp must not be NaN or +inf");
           s->device = device;
           cuda_ok(cudaSetDevice(device), "cudaSetDevice");
           cuda_ok(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "cudaStreamCreate");
