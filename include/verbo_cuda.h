@@ -97,7 +97,7 @@ VERBO_CUDA_API int verbo_cuda_sample(const float* logits, int rows, int vocab, l
    the history ids that fall in the shard and emit the shard's k best
    (value, global id) pairs in the reference's order (value descending, id
    ascending) to cand_val/cand_id [rows][k] (device).  Missing slots are
-   (-inf, -1).  1 <= k <= 1024. */
+   (-inf, -1).  1 <= k <= 256. */
 VERBO_CUDA_API int verbo_cuda_shard_topk(const float* logits, int rows, int shard_cols, long long ld,
                                          int col_offset, int vocab, const int* hist, const long long* hist_off,
                                          const verbo_sampling* opts, int k, float* cand_val, int* cand_id,
@@ -107,7 +107,7 @@ VERBO_CUDA_API int verbo_cuda_shard_topk(const float* logits, int rows, int shar
    out [nshards][rows][k] (the layout of an all-gather of step-1 outputs), and
    finish the pick: softmax, min-p, top-p and the draw.  Equal to
    verbo_cuda_sample on the unsharded rows when opts->temp <= 0 or
-   0 < opts->top_k <= k.  nshards * k <= 4096. */
+   0 < opts->top_k <= k.  k <= 256, nshards * k <= 4096. */
 VERBO_CUDA_API int verbo_cuda_merge_sample(const float* cand_val, const int* cand_id, int rows, int nshards,
                                            int k, int vocab, const verbo_sampling* opts,
                                            unsigned long long* rng, int* out_ids, verbo_row_stats* stats,

@@ -6,11 +6,15 @@
 // kernels.cu.  There is no CPU fallback.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <stdexcept>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "kernels.cuh"
@@ -113,6 +117,56 @@ vb::RowArgs row_args(const float* logits, int rows, int ncols, long long ld, int
   return a;
 }
 
+// Scratch of the split-row kernels, one set per (device, stream) so that calls
+// on different streams never share it.  `counters` holds one u32 per row; the
+// kernels leave every counter at zero, so it is zeroed only when it grows.
+// `data` holds the per-slice partial results and needs no initialisation.
+struct Scratch {
+  unsigned* counters = nullptr;
+  long long counter_rows = 0;
+  void* data = nullptr;
+  size_t data_bytes = 0;
+};
+std::mutex g_scratch_mu;
+std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
+
+void attach_split_scratch(vb::RowArgs& a, cudaStream_t s) {
+  int dev = 0;
+  cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
+  size_t off_count = 0, off_keys = 0;
+  const size_t bytes = vb::split_scratch_bytes(a.rows, a.cluster, &off_count, &off_keys) - off_count;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  Scratch& sc = g_scratch[{dev, s}];
+  if (sc.counter_rows < a.rows || sc.data_bytes < bytes) cuda_ok(cudaStreamSynchronize(s), "stream");
+  if (sc.counter_rows < a.rows) {
+    const long long n = std::max<long long>(a.rows, 2 * sc.counter_rows);
+    cudaFree(sc.counters);
+    sc.counters = nullptr;
+    sc.counter_rows = 0;
+    cuda_ok(cudaMalloc(&sc.counters, static_cast<size_t>(n) * sizeof(unsigned)), "cudaMalloc scratch");
+    cuda_ok(cudaMemsetAsync(sc.counters, 0, static_cast<size_t>(n) * sizeof(unsigned), s), "cudaMemsetAsync");
+    sc.counter_rows = n;
+  }
+  if (sc.data_bytes < bytes) {
+    const size_t n = std::max(bytes, 2 * sc.data_bytes);
+    cudaFree(sc.data);
+    sc.data = nullptr;
+    sc.data_bytes = 0;
+    cuda_ok(cudaMalloc(&sc.data, n), "cudaMalloc scratch");
+    sc.data_bytes = n;
+  }
+  a.counters = sc.counters;
+  a.slice_count = static_cast<unsigned*>(sc.data);
+  a.slice_keys = reinterpret_cast<unsigned long long*>(static_cast<char*>(sc.data) + (off_keys - off_count));
+}
+
+// Slices of the split-row kernels: the fewest slices of <= kSplitSlice columns.
+void plan_split(vb::RowArgs& a) {
+  a.cluster = (a.ncols + vb::kSplitSlice - 1) / vb::kSplitSlice;
+  a.slice = (a.ncols + a.cluster - 1) / a.cluster;
+  a.slice = (a.slice + 3) & ~3;
+}
+
 void check_hist(const int* hist, const long long* hist_off) {
   if ((hist == nullptr) != (hist_off == nullptr)) fail("hist and hist_off must both be given or both be NULL");
 }
@@ -134,12 +188,13 @@ int sample_impl(const float* logits, int rows, int vocab, long long ld, const in
   a.out_ids = out_ids;
   a.stats = stats;
   cudaError_t e;
-  if (o.greedy)
-    e = vb::launch_greedy(a, o, s);
-  else if (o.k < vocab && o.k <= vb::kMaxK)
-    e = vb::launch_topk(a, o, false, s);
-  else
+  if (o.greedy || (o.k < vocab && o.k <= vb::kSplitMaxK)) {
+    plan_split(a);
+    attach_split_scratch(a, s);
+    e = vb::launch_split(a, o, o.greedy ? vb::kSplitGreedy : vb::kSplitSample, s);
+  } else {
     e = vb::launch_general(a, o, s);
+  }
   cuda_ok(e, "kernel launch");
   return 0;
 }
@@ -246,7 +301,7 @@ VERBO_CUDA_API int verbo_cuda_shard_topk(const float* logits, int rows, int shar
         if (rows < 0) fail("rows must be >= 0");
         if (rows == 0) return 0;
         if (!logits || !cand_val || !cand_id) fail("logits, cand_val and cand_id must not be NULL");
-        if (k < 1 || k > vb::kMaxK) fail("k must be in [1, " + std::to_string(vb::kMaxK) + "]");
+        if (k < 1 || k > vb::kSplitMaxK) fail("k must be in [1, " + std::to_string(vb::kSplitMaxK) + "]");
         if (vocab < 1 || vocab > vb::kMaxVocab) fail("vocab must be in [1, " + std::to_string(vb::kMaxVocab) + "]");
         if (shard_cols < 1 || col_offset < 0 || static_cast<long long>(col_offset) + shard_cols > vocab)
           fail("shard [col_offset, col_offset + shard_cols) must lie in [0, vocab)");
@@ -257,7 +312,9 @@ VERBO_CUDA_API int verbo_cuda_shard_topk(const float* logits, int rows, int shar
         a.cand_val = cand_val;
         a.cand_id = cand_id;
         a.cand_k = k;
-        cuda_ok(vb::launch_topk(a, o, true, static_cast<cudaStream_t>(stream)), "kernel launch");
+        plan_split(a);
+        attach_split_scratch(a, static_cast<cudaStream_t>(stream));
+        cuda_ok(vb::launch_split(a, o, vb::kSplitEmit, static_cast<cudaStream_t>(stream)), "kernel launch");
         return 0;
       },
       -1);
@@ -274,7 +331,7 @@ VERBO_CUDA_API int verbo_cuda_merge_sample(const float* cand_val, const int* can
         if (!cand_val || !cand_id || !out_ids) fail("cand_val, cand_id and out_ids must not be NULL");
         if (nshards < 1 || k < 1 || static_cast<long long>(nshards) * k > vb::kMaxMerge)
           fail("nshards * k must be in [1, " + std::to_string(vb::kMaxMerge) + "]");
-        if (k > vb::kMaxK) fail("k must be <= " + std::to_string(vb::kMaxK));
+        if (k > vb::kSplitMaxK) fail("k must be <= " + std::to_string(vb::kSplitMaxK));
         if (vocab < 1) fail("vocab must be >= 1");
         vb::DevOpts o = make_opts(*opts, vocab, false);
         if (!o.greedy && !(opts->top_k > 0 && opts->top_k <= k && opts->top_k < vocab))

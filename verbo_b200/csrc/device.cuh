@@ -163,41 +163,45 @@ __device__ __forceinline__ T warp_sum(T x) {
 // Block-wide exclusive scan of one value per thread.  `ws` holds kWarps
 // entries of shared scratch.  Returns the exclusive prefix; *total gets the
 // block total.  Contains two __syncthreads.
-template <class T>
+// NT = threads of the block (a multiple of 32, at most 1024).
+template <class T, int NT = kThreads>
 __device__ __forceinline__ T block_excl_scan(T x, T* ws, T* total) {
+  constexpr int W = NT / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   T incl = warp_incl_scan(x);
   if (lane == 31) ws[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    T w = lane < kWarps ? ws[lane] : T(0);
+    T w = lane < W ? ws[lane] : T(0);
     w = warp_incl_scan(w);
-    if (lane < kWarps) ws[lane] = w;
+    if (lane < W) ws[lane] = w;
   }
   __syncthreads();
-  *total = ws[kWarps - 1];
+  *total = ws[W - 1];
   return incl - x + (warp ? ws[warp - 1] : T(0));
 }
 
-template <class T>
+template <class T, int NT = kThreads>
 __device__ __forceinline__ T block_min(T x, T* ws) {
+  constexpr int W = NT / 32;
   x = warp_min(x);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (lane == 0) ws[warp] = x;
   __syncthreads();
   T r = ws[0];
-  for (int i = 1; i < kWarps; ++i) r = ws[i] < r ? ws[i] : r;
+  for (int i = 1; i < W; ++i) r = ws[i] < r ? ws[i] : r;
   __syncthreads();
   return r;
 }
-template <class T>
+template <class T, int NT = kThreads>
 __device__ __forceinline__ T block_sum(T x, T* ws) {
+  constexpr int W = NT / 32;
   x = warp_sum(x);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (lane == 0) ws[warp] = x;
   __syncthreads();
   T r = ws[0];
-  for (int i = 1; i < kWarps; ++i) r += ws[i];
+  for (int i = 1; i < W; ++i) r += ws[i];
   __syncthreads();
   return r;
 }

@@ -171,7 +171,7 @@ struct TailShared {
 __device__ void tail_pick(const uint64_t* c, int k, const DevOpts& o, unsigned long long* rng, int* out_id,
                           verbo_row_stats* st, double* pr, double* q, TailShared* ts) {
   const float mx = dval(c[0]);
-  for (int i = threadIdx.x; i < k; i += kThreads) {
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
     const float v = dval(c[i]);
     pr[i] = exp(__ddiv_rn(static_cast<double>(__fsub_rn(v, mx)), static_cast<double>(o.temp)));
   }
@@ -191,7 +191,7 @@ __device__ void tail_pick(const uint64_t* c, int k, const DevOpts& o, unsigned l
   __syncthreads();
   const bool use_p = o.top_p > 0.0f && o.top_p < 1.0f;
   if (use_p)
-    for (int i = threadIdx.x; i < ts->keep; i += kThreads) q[i] = __ddiv_rn(pr[i], ts->sum);
+    for (int i = threadIdx.x; i < ts->keep; i += blockDim.x) q[i] = __ddiv_rn(pr[i], ts->sum);
   __syncthreads();
   if (threadIdx.x != 0) return;
   const double inf = __longlong_as_double(0x7ff0000000000000ll);
@@ -1052,6 +1052,416 @@ cudaError_t read_status(unsigned* st, bool clear, cudaStream_t s) {
     e = cudaMemcpyToSymbol(g_status, &z, sizeof(unsigned));
   }
   return e;
+}
+
+
+// ================================================== split-row kernels (v2) ==
+// One CTA of kSplitThreads per (row, slice of <= kSplitSlice columns), no
+// thread-block clusters.  Each thread issues all of its 16-byte loads before
+// using any (kSplitChunks in flight per thread), applies the penalty from a
+// per-slice bitmap, and reduces its columns to a tiny partial result.  The
+// slice publishes that partial to global scratch; the last CTA of the row to
+// finish (a per-row atomic counter after a __threadfence, no waiting) merges
+// the partials and finishes the row.  Nothing waits on another CTA, so other
+// rows keep streaming while a row's merge runs.
+namespace split {
+
+constexpr int NT = kSplitThreads;
+constexpr int NW = NT / 32;
+constexpr int kBinsS = 2048;  // 11-bit digits of the candidate key
+constexpr int kUnionCap = 2048;
+
+struct Shared {
+  unsigned long long ws64[NW];
+  uint32_t ws32[NW];
+  Found found;
+  uint32_t ncand;
+  int last;
+  int incomplete;
+  TailShared tail;
+};
+
+// Loads the thread's chunks of the slice into registers: chunk i covers slice
+// columns 4*q .. 4*q+3 with q = threadIdx.x + i*NT.  Columns beyond n are
+// left as NaN and never used (callers test j < n).
+__device__ __forceinline__ void load_regs(const float* src, int n, float4 (&x)[kSplitChunks]) {
+  const bool vec = (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  const float nan = __int_as_float(0x7fc00000);
+#pragma unroll
+  for (int i = 0; i < kSplitChunks; ++i) {
+    const int q = threadIdx.x + i * NT;
+    const int j0 = 4 * q;
+    if (vec && j0 + 3 < n) {
+      x[i] = ld_stream(s4 + q);
+    } else {
+      x[i].x = j0 < n ? ld_stream1(src + j0) : nan;
+      x[i].y = j0 + 1 < n ? ld_stream1(src + j0 + 1) : nan;
+      x[i].z = j0 + 2 < n ? ld_stream1(src + j0 + 2) : nan;
+      x[i].w = j0 + 3 < n ? ld_stream1(src + j0 + 3) : nan;
+    }
+  }
+}
+
+__device__ __forceinline__ void penalize_regs(float4 (&x)[kSplitChunks], const uint32_t* bm, float rep, int n) {
+#pragma unroll
+  for (int i = 0; i < kSplitChunks; ++i) {
+    const int j0 = 4 * (threadIdx.x + i * NT);
+    if (j0 < n) {
+      const uint32_t nib = (bm[j0 >> 5] >> (j0 & 31)) & 15u;
+      if (nib) {
+        if (nib & 1u) x[i].x = penalize(x[i].x, rep);
+        if (nib & 2u) x[i].y = penalize(x[i].y, rep);
+        if (nib & 4u) x[i].z = penalize(x[i].z, rep);
+        if (nib & 8u) x[i].w = penalize(x[i].w, rep);
+      }
+    }
+  }
+}
+
+// Calls f(value, j) for every valid column of the thread's registers.
+template <class F>
+__device__ __forceinline__ void for_regs(const float4 (&x)[kSplitChunks], int n, F&& f) {
+#pragma unroll
+  for (int i = 0; i < kSplitChunks; ++i) {
+    const int j0 = 4 * (threadIdx.x + i * NT);
+    if (j0 < n) f(x[i].x, j0);
+    if (j0 + 1 < n) f(x[i].y, j0 + 1);
+    if (j0 + 2 < n) f(x[i].z, j0 + 2);
+    if (j0 + 3 < n) f(x[i].w, j0 + 3);
+  }
+}
+
+// The thread's best column by the reference's order (value descending, lowest
+// column on ties) as a 64-bit key.  Float compares do the work: `v > best`
+// keeps the first (lowest) column on ties, treats -0 == +0, and never selects
+// a NaN, so NaN logits rank as -inf and the NaN placeholders beyond n are
+// ignored.  A thread whose valid columns are all -inf/NaN yields its lowest
+// valid column with the key of -inf.
+__device__ __forceinline__ unsigned long long regs_best(const float4 (&x)[kSplitChunks], int n, long long g_lo) {
+  const float ninf = -__int_as_float(0x7f800000);
+  float bv = ninf;
+  int bj = -1;
+#pragma unroll
+  for (int i = 0; i < kSplitChunks; ++i) {
+    const int j0 = 4 * (threadIdx.x + i * NT);
+    if (x[i].x > bv) { bv = x[i].x; bj = j0; }
+    if (x[i].y > bv) { bv = x[i].y; bj = j0 + 1; }
+    if (x[i].z > bv) { bv = x[i].z; bj = j0 + 2; }
+    if (x[i].w > bv) { bv = x[i].w; bj = j0 + 3; }
+  }
+  if (bj < 0) {
+    if (4 * static_cast<int>(threadIdx.x) >= n) return kNoKey;
+    bj = 4 * threadIdx.x;
+  }
+  return dkey(bv, static_cast<uint32_t>(g_lo + bj));
+}
+
+// First bin (of kBinsS counts, 8 per thread) where the running count reaches target >= 1.
+__device__ Found find_bins(const uint32_t* H, uint32_t target, Shared& sh) {
+  if (threadIdx.x == 0) sh.found.bin = -1;
+  const uint4 a = reinterpret_cast<const uint4*>(H)[2 * threadIdx.x];
+  const uint4 b = reinterpret_cast<const uint4*>(H)[2 * threadIdx.x + 1];
+  const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t s = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s += v[i];
+  uint32_t total;
+  const uint32_t ex = block_excl_scan<uint32_t, NT>(s, sh.ws32, &total);
+  if (ex < target && target <= ex + s) {
+    uint32_t e = ex;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (target <= e + v[i]) {
+        sh.found.bin = 8 * threadIdx.x + i;
+        sh.found.before = e;
+        sh.found.cnt = v[i];
+        break;
+      }
+      e += v[i];
+    }
+  }
+  __syncthreads();
+  const Found f = sh.found;
+  __syncthreads();
+  return f;
+}
+
+// Exact selection of the `k` smallest keys among those produced by `each`
+// (which calls its argument with every candidate key of this thread): 11-bit
+// radix passes with early exit.  Returns (prefix, shift) such that the
+// selected set is {key : (key >> shift) <= prefix}.  H: kBinsS zeroed counts
+// (left zeroed).  nbits: significant bits of the keys.
+template <class Each>
+__device__ __forceinline__ void radix_select(Each&& each, uint32_t k, int nbits, uint32_t* H, Shared& sh,
+                             unsigned long long* prefix_out, int* shift_out) {
+  unsigned long long prefix = 0;
+  int resolved = 0;
+  uint32_t krem = k;
+  while (true) {
+    const int shift = max(0, nbits - resolved - 11);
+    const int width = nbits - resolved - shift;
+    const unsigned long long mask = (1ull << width) - 1;
+    const int hi = nbits - resolved;
+    each([&](unsigned long long key) {
+      if (resolved == 0 || (key >> hi) == prefix) atomicAdd(&H[(key >> shift) & mask], 1u);
+    });
+    __syncthreads();
+    Found f = find_bins(H, krem, sh);
+    for (int b = threadIdx.x; b < kBinsS; b += NT) H[b] = 0;
+    if (f.bin < 0) {  // unreachable: the set holds at least k keys
+      if (threadIdx.x == 0) raise_status(kErrSelect);
+      f.bin = 0;
+      f.before = 0;
+      f.cnt = krem;
+    }
+    prefix = (prefix << width) | static_cast<unsigned long long>(f.bin);
+    resolved += width;
+    krem -= f.before;
+    if (f.cnt == krem || shift == 0) {
+      *prefix_out = prefix;
+      *shift_out = shift;
+      __syncthreads();
+      return;
+    }
+  }
+}
+
+}  // namespace split
+
+namespace split {
+
+__device__ __forceinline__ unsigned long long to_ckey(unsigned long long d, int idxbits) {
+  return ((d >> 32) << idxbits) | (d & 0xffffffffull);
+}
+
+template <int kMode, bool kPen>
+__global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const DevOpts o) {
+  const int C = a.cluster;
+  const int row = blockIdx.x / C;
+  const int s = blockIdx.x - row * C;
+  const int lo = s * a.slice;
+  const int n = max(0, min(a.ncols - lo, a.slice));
+  const float* src = a.logits + static_cast<long long>(row) * a.ld + lo;
+  const long long g_lo = static_cast<long long>(a.col_off) + lo;
+  extern __shared__ __align__(16) unsigned char smem[];
+  uint32_t* H = reinterpret_cast<uint32_t*>(smem);                          // kBinsS counts (top-k modes)
+  uint64_t* U = reinterpret_cast<uint64_t*>(H + kBinsS);  // kUnionCap keys (top-k modes)
+  uint32_t* bm = kMode == kSplitGreedy ? reinterpret_cast<uint32_t*>(smem) : reinterpret_cast<uint32_t*>(U + kUnionCap);
+  __shared__ Shared sh;
+
+  float4 x[kSplitChunks];
+  load_regs(src, n, x);  // all loads in flight before anything else
+  if (kMode != kSplitGreedy)
+    for (int b = threadIdx.x; b < kBinsS; b += NT) H[b] = 0;
+  if (threadIdx.x == 0) sh.ncand = 0;
+  if (kPen) {
+    const int nw = (a.slice >> 5) + 2;
+    for (int i = threadIdx.x; i < nw; i += NT) bm[i] = 0;
+    __syncthreads();
+    const long long h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
+    const long long len = h1 - h0;
+    const long long from = (o.repeat_last > 0 && len > o.repeat_last) ? len - o.repeat_last : 0;
+    for (long long j = h0 + from + threadIdx.x; j < h1; j += NT) {
+      const long long t = static_cast<long long>(a.hist[j]) - g_lo;
+      if (t >= 0 && t < n) atomicOr(&bm[t >> 5], 1u << (t & 31));
+    }
+  }
+  __syncthreads();
+  if (kPen) penalize_regs(x, bm, o.repeat, n);
+  const long long slot = static_cast<long long>(row) * C + s;
+
+  if (kMode == kSplitGreedy) {
+    unsigned long long best = regs_best(x, n, g_lo);
+    // std::max_element returns element 0 when it is NaN: key 0 beats every other key.
+    if (g_lo == 0 && threadIdx.x == 0 && n > 0 && x[0].x != x[0].x) best = 0;
+    best = block_min<unsigned long long, NT>(best, sh.ws64);
+    if (threadIdx.x == 0) a.slice_keys[slot] = best;
+  } else {
+    const uint32_t k = kMode == kSplitEmit ? static_cast<uint32_t>(min(a.cand_k, a.ncols)) : static_cast<uint32_t>(o.k);
+    const uint32_t kl = min(k, static_cast<uint32_t>(n));
+    // Bound from the slice's thread maxima: the first 11-bit key bin where
+    // their count reaches kl has at least kl elements at or above it, so the
+    // slice's top-kl lies in bins <= b*.
+    const unsigned long long tmin = regs_best(x, n, g_lo);
+    if (tmin != kNoKey) atomicAdd(&H[tmin >> 53], 1u);
+    __syncthreads();
+    uint32_t count = 0;
+    unsigned long long* out = a.slice_keys + slot * kSliceCap;
+    if (kl > 0) {
+      const Found fb = find_bins(H, kl, sh);
+      for (int b = threadIdx.x; b < kBinsS; b += NT) H[b] = 0;
+      const uint32_t bstar = fb.bin >= 0 ? static_cast<uint32_t>(fb.bin) : kBinsS - 1u;
+      // bins <= b*  <=>  ord32(v) >= T  <=>  v >= unord32(T) for non-NaN v.
+      // T <= ord32(-inf) means every column is a candidate (-inf and NaN too).
+      const uint32_t T = ~(((bstar + 1u) << 21) - 1u);
+      const bool all = T <= 0x007fffffu;
+      const float tv = unord32(T);
+      uint32_t mine = 0;
+      if (all) {
+        for_regs(x, n, [&](float, int) { ++mine; });
+      } else {
+#pragma unroll
+        for (int i = 0; i < kSplitChunks; ++i)
+          mine += uint32_t(x[i].x >= tv) + uint32_t(x[i].y >= tv) + uint32_t(x[i].z >= tv) + uint32_t(x[i].w >= tv);
+      }
+      uint32_t tot;
+      const uint32_t ex = block_excl_scan<uint32_t, NT>(mine, sh.ws32, &tot);
+      if (tot <= static_cast<uint32_t>(kSliceCap) && tot >= kl) {
+        uint32_t at = ex;
+        for_regs(x, n, [&](float v, int j) {
+          if (all || v >= tv) out[at++] = dkey(v, static_cast<uint32_t>(g_lo + j));
+        });
+        count = tot;
+      } else {
+        // more than kSliceCap candidates (ties, masked rows): exact top-kl
+        unsigned long long prefix;
+        int shift;
+        const int nbits = 32 + a.idxbits;
+        // (rare path: re-read the slice from L2 so the register copy can die)
+        auto each_col = [&](auto f) {
+          for (int j = threadIdx.x; j < n; j += NT) {
+            float v = ld_stream1(src + j);
+            if (kPen && ((bm[j >> 5] >> (j & 31)) & 1u)) v = penalize(v, o.repeat);
+            f(v, j);
+          }
+        };
+        radix_select(
+            [&](auto f) { each_col([&](float v, int j) { f(ckey(v, static_cast<uint32_t>(g_lo + j), a.idxbits)); }); },
+            kl, nbits, H, sh, &prefix, &shift);
+        each_col([&](float v, int j) {
+          const uint32_t gid = static_cast<uint32_t>(g_lo + j);
+          if ((ckey(v, gid, a.idxbits) >> shift) <= prefix) {
+            const uint32_t p = atomicAdd(&sh.ncand, 1u);
+            if (p < static_cast<uint32_t>(kSliceCap)) out[p] = dkey(v, gid);
+          }
+        });
+        count = kl;
+      }
+    }
+    if (threadIdx.x == 0) a.slice_count[slot] = count;
+  }
+
+  // publish; the last slice of the row to finish merges
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) sh.last = atomicAdd(&a.counters[row], 1u) == static_cast<unsigned>(C - 1);
+  __syncthreads();
+  if (!sh.last) return;
+  __threadfence();
+
+  if (kMode == kSplitGreedy) {
+    if (threadIdx.x < 32) {
+      unsigned long long m = kNoKey;
+      for (int i = threadIdx.x; i < C; i += 32) {
+        const unsigned long long v = __ldcg(&a.slice_keys[static_cast<long long>(row) * C + i]);
+        m = v < m ? v : m;
+      }
+      m = warp_min(m);
+      if (threadIdx.x == 0) {
+        const int id = static_cast<int>(did(m));
+        a.out_ids[row] = id;
+        if (a.stats) write_stats(a.stats + row, 0.0, 0.0, 0.0, __longlong_as_double(0x7ff0000000000000ll),
+                                 __longlong_as_double(0x7ff0000000000000ll), o.vocab, 1, id, 1);
+        a.counters[row] = 0;
+      }
+    }
+    return;
+  }
+
+  const uint32_t k = kMode == kSplitEmit ? static_cast<uint32_t>(min(a.cand_k, a.ncols)) : static_cast<uint32_t>(o.k);
+  __shared__ uint32_t soff[kMaxSlices + 1];
+  const uint32_t ci = threadIdx.x < static_cast<unsigned>(C) ? __ldcg(&a.slice_count[static_cast<long long>(row) * C + threadIdx.x]) : 0u;
+  uint32_t utot;
+  const uint32_t cex = block_excl_scan<uint32_t, NT>(ci, sh.ws32, &utot);
+  if (threadIdx.x < static_cast<unsigned>(C)) {
+    soff[threadIdx.x] = cex;
+    soff[kMaxSlices] = 0;
+  }
+  __shared__ uint32_t scnt[kMaxSlices];
+  if (threadIdx.x < static_cast<unsigned>(C)) scnt[threadIdx.x] = ci;
+  if (threadIdx.x == 0) sh.ncand = 0;
+  __syncthreads();
+  const unsigned long long* base = a.slice_keys + static_cast<long long>(row) * C * kSliceCap;
+  uint32_t total;
+  if (utot <= static_cast<uint32_t>(kUnionCap)) {
+    for (int e = threadIdx.x; e < C * kSliceCap; e += NT) {
+      const int i = e / kSliceCap, j = e - i * kSliceCap;
+      if (j < static_cast<int>(scnt[i])) U[soff[i] + j] = __ldcg(base + e);
+    }
+    total = utot;
+  } else {
+    unsigned long long prefix;
+    int shift;
+    const int nbits = 32 + a.idxbits;
+    auto each = [&](auto f) {
+      for (int e = threadIdx.x; e < C * kSliceCap; e += NT) {
+        const int i = e / kSliceCap, j = e - i * kSliceCap;
+        if (j < static_cast<int>(scnt[i])) f(to_ckey(__ldcg(base + e), a.idxbits));
+      }
+    };
+    radix_select(each, k, nbits, H, sh, &prefix, &shift);
+    for (int e = threadIdx.x; e < C * kSliceCap; e += NT) {
+      const int i = e / kSliceCap, j = e - i * kSliceCap;
+      if (j < static_cast<int>(scnt[i])) {
+        const unsigned long long d = __ldcg(base + e);
+        if ((to_ckey(d, a.idxbits) >> shift) <= prefix) {
+          const uint32_t p = atomicAdd(&sh.ncand, 1u);
+          if (p < static_cast<uint32_t>(kUnionCap)) U[p] = d;
+        }
+      }
+    }
+    total = k;
+  }
+  __syncthreads();
+  const int P = next_pow2(max(static_cast<int>(total), 2));
+  for (int i = static_cast<int>(total) + threadIdx.x; i < P; i += NT) U[i] = kNoKey;
+  __syncthreads();
+  bitonic_sort_u64(U, P);
+  if (kMode == kSplitEmit) {
+    for (int i = threadIdx.x; i < a.cand_k; i += NT) {
+      const long long at = static_cast<long long>(row) * a.cand_k + i;
+      const bool ok = i < static_cast<int>(k);
+      a.cand_val[at] = ok ? dval(U[i]) : -__int_as_float(0x7f800000);
+      a.cand_id[at] = ok ? static_cast<int>(did(U[i])) : -1;
+    }
+  } else {
+    double* pr = reinterpret_cast<double*>(H);  // H is free: fp64 scratch of the tail
+    tail_pick(U, static_cast<int>(k), o, a.rng + 2ll * row, a.out_ids + row, a.stats ? a.stats + row : nullptr, pr,
+              pr + kSplitMaxK, &sh.tail);
+  }
+  if (threadIdx.x == 0) a.counters[row] = 0;
+}
+
+}  // namespace split
+
+size_t split_scratch_bytes(long long rows, int slices, size_t* off_count, size_t* off_keys) {
+  auto up = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
+  const size_t counters = up(static_cast<size_t>(rows) * 4);
+  const size_t counts = up(static_cast<size_t>(rows) * slices * 4);
+  const size_t keys = static_cast<size_t>(rows) * slices * kSliceCap * 8;
+  *off_count = counters;
+  *off_keys = counters + counts;
+  return counters + counts + keys;
+}
+
+template <int kMode, bool kPen>
+static cudaError_t launch_split_t(const RowArgs& a, const DevOpts& o, cudaStream_t s) {
+  const size_t bmb = static_cast<size_t>((a.slice >> 5) + 2) * 4;
+  const size_t sm = kMode == kSplitGreedy ? bmb : split::kBinsS * 4 + split::kUnionCap * 8 + bmb;
+  split::split_kernel<kMode, kPen><<<a.rows * a.cluster, split::NT, sm, s>>>(a, o);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split(const RowArgs& a, const DevOpts& o, int mode, cudaStream_t s) {
+  switch (mode * 2 + (o.penalize ? 1 : 0)) {
+    case 0: return launch_split_t<kSplitGreedy, false>(a, o, s);
+    case 1: return launch_split_t<kSplitGreedy, true>(a, o, s);
+    case 2: return launch_split_t<kSplitSample, false>(a, o, s);
+    case 3: return launch_split_t<kSplitSample, true>(a, o, s);
+    case 4: return launch_split_t<kSplitEmit, false>(a, o, s);
+    default: return launch_split_t<kSplitEmit, true>(a, o, s);
+  }
 }
 
 }  // namespace vb
