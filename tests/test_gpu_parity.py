@@ -232,3 +232,34 @@ def test_shard_topk_small_shards_pad():
     ov, oi = po.shard_topk(x, 100, 1000, po.sampling(), 64)
     assert np.array_equal(ci.cpu().numpy(), oi)
     assert (ci.cpu().numpy()[:, 50:] == -1).all()
+
+
+def test_min_p_extremes_keep_first():
+    # keep starts at 1 (src/sampler.cpp:89): min_p >= 1 keeps the maximum (and its ties)
+    g = np.random.default_rng(21)
+    V = 5000
+    x = g.standard_normal((4, V)).astype(np.float32)
+    x[1, [10, 20, 30]] = x[1].max() + 1.0          # tied maxima
+    for top_k in (0, 40, 600):
+        for mp in (1.0, 1.5, 0.999):
+            opts = dict(temp=0.9, top_k=top_k, top_p=0.9, min_p=mp)
+            seeds = np.arange(4, dtype=np.uint64) + np.uint64(3)
+            ids, _, _ = run_gpu(x, opts, seeds, steps=3)
+            ora, ost, _ = run_oracle(x, opts, seeds, steps=3)
+            compare(ids, ora, ost, str(opts))
+
+
+def test_crowded_bins_use_exact_fallback():
+    # rows whose values pile into a few value bins: the nucleus kernel's
+    # gather overflows and the exact radix selection takes over
+    g = np.random.default_rng(8)
+    V = 151936
+    x = np.round(g.standard_normal((3, V)) * 2).astype(np.float32) / 4   # ~30 distinct values
+    x[2] = 0.75
+    for opts in (dict(temp=1.0, top_k=0, top_p=0.9), dict(temp=0.7, top_k=0, top_p=1.0, min_p=0.3),
+                 dict(temp=2.0, top_k=0, top_p=0.5)):
+        seeds = np.arange(3, dtype=np.uint64) + np.uint64(40)
+        ids, st, _ = run_gpu(x, opts, seeds, steps=2)
+        ora, ost, _ = run_oracle(x, opts, seeds, steps=2)
+        compare(ids, ora, ost, str(opts))
+        np.testing.assert_allclose(st["sum"], ost[:, -1]["sum"], rtol=1e-9)

@@ -1,30 +1,28 @@
 // sm_100a kernels of the token-sampling path: a drop-in for the per-row work
 // of verbo's Sampler::pick (src/sampler.cpp:50-109).
 //
-// Every kernel runs one thread-block cluster per logits row (or shard row):
-// the row's columns are split into `cluster` contiguous slices, one per CTA,
-// and the CTAs combine results through distributed shared memory (DSMEM).
-//
-//   greedy_kernel   temp <= 0.  One streaming pass: penalty from a per-slice
-//                   bitmap, then the minimum of the 64-bit candidate key
-//                   (= argmax with lowest-index ties, sampler.cpp:66-70).
-//   topk_kernel     0 < top_k <= 1024.  One streaming pass keeping each
-//                   thread's 4 best keys; a cluster-wide histogram of the
-//                   thread maxima bounds the top-k from below; the candidates
-//                   above the bound go to CTA 0, which sorts them and runs the
-//                   reference's softmax / min-p / top-p / draw sequence in the
-//                   same fp64 order (sampler.cpp:79-108).  If a thread could
-//                   hold more than 4 candidates, the cluster instead runs an
-//                   exact radix select by re-reading the row.  With `emit` it
-//                   writes a shard's sorted top-k instead of sampling.
-//   general_kernel  top_k == 0 (or > 1024, or >= vocab).  The slice is staged
-//                   in shared memory with bulk async copies; the full-vocab
-//                   softmax mass, min-p set, top-p cutoff and the draw are
-//                   found by mass-weighted radix selection over the keys,
-//                   with masses accumulated in 64-bit fixed point (exact and
-//                   order-independent).  No full sort.
-//   merge_kernel    merges per-shard candidates and runs the same tail as
-//                   topk_kernel.
+//   split_kernel    (greedy, 0 < top_k <= 256, and shard top-k)  One CTA of
+//                   256 threads per (row, slice of <= 10240 columns), no
+//                   clusters.  Every thread issues all of its 16-byte loads
+//                   up front (10 in flight), applies the penalty from a
+//                   per-slice bitmap, and reduces its columns with float
+//                   compares.  Greedy publishes the slice's best key; top-k
+//                   bounds the slice's top-k by a histogram of thread maxima
+//                   and publishes every column above the bound.  The last CTA
+//                   of the row (per-row atomic counter) merges: the best key,
+//                   or a sort of the union of candidates followed by the
+//                   reference's softmax / min-p / top-p / draw in the same
+//                   fp64 order (sampler.cpp:79-108).
+//   general_kernel  (top_k == 0, top_k > 256 or top_k >= vocab)  One thread-
+//                   block cluster per row; each CTA stages its slice in shared
+//                   memory with bulk async copies.  Masses exp((v - M) / T) in
+//                   64-bit fixed point (exact, order independent) go into a
+//                   value-space histogram relative to the row maximum; the
+//                   top-p cutoff bin and the bins the draw can reach are
+//                   gathered once into every CTA and resolved there.  An exact
+//                   mass-weighted radix selection over the keys handles rows
+//                   whose bins are too crowded.  No full sort.
+//   merge_kernel    merges per-shard candidates and runs the same tail.
 #include "device.cuh"
 #include "kernels.cuh"
 
@@ -45,63 +43,6 @@ __device__ __forceinline__ double rng_unit(unsigned long long& s1_io, unsigned l
   return __dmul_rn(static_cast<double>(r >> 11), 1.0 / 9007199254740992.0);
 }
 
-// Penalty window of one row (src/sampler.cpp:53-57) marked in a bitmap over
-// the slice [g_lo, g_lo + n) of global columns.
-__device__ void build_bitmap(uint32_t* bm, int nwords, const RowArgs& a, const DevOpts& o, int row, long long g_lo,
-                             int n) {
-  for (int i = threadIdx.x; i < nwords; i += kThreads) bm[i] = 0;
-  __syncthreads();
-  const long long h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
-  const long long len = h1 - h0;
-  const long long from = (o.repeat_last > 0 && len > o.repeat_last) ? len - o.repeat_last : 0;
-  for (long long j = h0 + from + threadIdx.x; j < h1; j += kThreads) {
-    const long long t = static_cast<long long>(a.hist[j]) - g_lo;
-    if (t >= 0 && t < n) atomicOr(&bm[t >> 5], 1u << (t & 31));
-  }
-  __syncthreads();
-}
-
-template <bool kPen, class F>
-__device__ __forceinline__ void consume4(float4 x, int j0, const uint32_t* bm, float rep, F& f) {
-  if (kPen) {
-    const uint32_t nib = (bm[j0 >> 5] >> (j0 & 31)) & 15u;
-    if (nib) {
-      if (nib & 1u) x.x = penalize(x.x, rep);
-      if (nib & 2u) x.y = penalize(x.y, rep);
-      if (nib & 4u) x.z = penalize(x.z, rep);
-      if (nib & 8u) x.w = penalize(x.w, rep);
-    }
-  }
-  f(x.x, j0);
-  f(x.y, j0 + 1);
-  f(x.z, j0 + 2);
-  f(x.w, j0 + 3);
-}
-
-// Calls f(value_after_penalty, j) for each column j of the slice [0, n) that
-// this thread owns.  16-byte loads with 4 in flight per thread when the slice
-// start is 16-byte aligned; scalar loads otherwise and for the ragged tail.
-template <bool kPen, class F>
-__device__ __forceinline__ void stream_slice(const float* src, int n, const uint32_t* bm, float rep, F&& f) {
-  const bool vec = (reinterpret_cast<uintptr_t>(src) & 15) == 0;
-  const int nq = vec ? (n >> 2) : 0;
-  const float4* s4 = reinterpret_cast<const float4*>(src);
-  int q = threadIdx.x;
-  for (; q + 3 * kThreads < nq; q += 4 * kThreads) {
-    float4 x[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) x[u] = ld_stream(s4 + q + u * kThreads);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) consume4<kPen>(x[u], 4 * (q + u * kThreads), bm, rep, f);
-  }
-  for (; q < nq; q += kThreads) consume4<kPen>(ld_stream(s4 + q), 4 * q, bm, rep, f);
-  for (int j = 4 * nq + threadIdx.x; j < n; j += kThreads) {
-    float v = ld_stream1(src + j);
-    if (kPen && ((bm[j >> 5] >> (j & 31)) & 1u)) v = penalize(v, rep);
-    f(v, j);
-  }
-}
-
 __device__ __forceinline__ void write_stats(verbo_row_stats* st, double sum, double tot, double u, double dm,
                                             double cm, int k, int keep, int id, int greedy) {
   st->sum = sum;
@@ -113,48 +54,6 @@ __device__ __forceinline__ void write_stats(verbo_row_stats* st, double sum, dou
   st->keep = keep;
   st->id = id;
   st->greedy = greedy;
-}
-
-// ===================================================================== greedy
-template <bool kPen>
-__global__ void __launch_bounds__(kThreads) greedy_kernel(const RowArgs a, const DevOpts o) {
-  cg::cluster_group cl = cg::this_cluster();
-  const int C = a.cluster;
-  const int crank = static_cast<int>(cl.block_rank());
-  const int row = blockIdx.x / C;
-  const int lo = crank * a.slice;
-  const int n = max(0, min(a.ncols - lo, a.slice));
-  const float* src = a.logits + static_cast<long long>(row) * a.ld + lo;
-  const long long g_lo = static_cast<long long>(a.col_off) + lo;
-
-  extern __shared__ __align__(16) uint32_t bm[];
-  __shared__ uint64_t slot[kMaxCluster];
-  __shared__ uint64_t ws[kWarps];
-
-  cluster_arrive();
-  if (kPen)
-    build_bitmap(bm, (a.slice >> 5) + 2, a, o, row, g_lo, n);
-  uint64_t best = kNoKey;
-  stream_slice<kPen>(src, n, bm, o.repeat, [&](float v, int j) {
-    const uint64_t d = dkey(v, static_cast<uint32_t>(g_lo + j));
-    best = d < best ? d : best;
-  });
-  best = block_min(best, ws);
-  cluster_wait();
-  if (threadIdx.x == 0) *cl.map_shared_rank(&slot[crank], 0) = best;
-  cluster_sync_all();
-  if (crank == 0 && threadIdx.x == 0) {
-    uint64_t m = slot[0];
-    for (int i = 1; i < C; ++i) m = slot[i] < m ? slot[i] : m;
-    int id = static_cast<int>(did(m));
-    // std::max_element keeps element 0 when it is NaN (nothing compares above it).
-    float v0 = src[0];
-    if (kPen && ((bm[0] & 1u) != 0)) v0 = penalize(v0, o.repeat);
-    if (v0 != v0) id = 0;
-    a.out_ids[row] = id;
-    if (a.stats) write_stats(a.stats + row, 0.0, 0.0, 0.0, __longlong_as_double(0x7ff0000000000000ll),
-                             __longlong_as_double(0x7ff0000000000000ll), o.vocab, 1, id, 1);
-  }
 }
 
 // ======================================================== shared tail (top-k)
@@ -249,246 +148,14 @@ __device__ void tail_pick(const uint64_t* c, int k, const DevOpts& o, unsigned l
 }
 
 // ====================================================================== top-k
-constexpr int kBins = 2048;  // 11-bit radix digits (4 per thread)
-constexpr int kDig = 11;
-
 struct Found {
   int bin;
   uint32_t before;
   uint32_t cnt;
 };
 
-struct TopkShared {
-  uint32_t count;  // candidates reserved in CTA 0's buffer
-  uint32_t flag;   // some thread may have dropped a candidate
-  uint32_t c_total, c_flag;
-  Found found;
-  uint32_t ws[kWarps];
-  uint64_t ws64[kWarps];
-  TailShared tail;
-};
-
-// First bin (of kBins counts) at which the running count reaches target >= 1.
-__device__ Found find_u32x4(const uint32_t* G, uint32_t target, TopkShared& sh) {
-  if (threadIdx.x == 0) sh.found.bin = -1;
-  const uint4 c = reinterpret_cast<const uint4*>(G)[threadIdx.x];
-  const uint32_t s = c.x + c.y + c.z + c.w;
-  uint32_t total;
-  const uint32_t ex = block_excl_scan(s, sh.ws, &total);
-  if (ex < target && target <= ex + s) {
-    const uint32_t v[4] = {c.x, c.y, c.z, c.w};
-    uint32_t e = ex;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (target <= e + v[i]) {
-        sh.found.bin = 4 * threadIdx.x + i;
-        sh.found.before = e;
-        sh.found.cnt = v[i];
-        break;
-      }
-      e += v[i];
-    }
-  }
-  __syncthreads();
-  const Found f = sh.found;
-  __syncthreads();
-  return f;
-}
-
-// Adds this CTA's histogram L into G of every CTA of the cluster and zeroes L
-// (and, if given, the local buffer `clr` for the next pass).
-__device__ void push_u32(uint32_t* L, uint32_t* G, uint32_t* clr, cg::cluster_group& cl, int C) {
-  for (int b = threadIdx.x; b < kBins; b += kThreads) {
-    const uint32_t v = L[b];
-    if (v) {
-      for (int r = 0; r < C; ++r) atomicAdd(cl.map_shared_rank(G + b, r), v);
-      L[b] = 0;
-    }
-    if (clr) clr[b] = 0;
-  }
-}
-
 __device__ __forceinline__ uint64_t ckey(float v, uint32_t gid, int idxbits) {
   return (static_cast<uint64_t>(~ord32(canon(v))) << idxbits) | gid;
-}
-
-template <bool kPen, bool kEmit>
-__global__ void __launch_bounds__(kThreads) topk_kernel(const RowArgs a, const DevOpts o) {
-  cg::cluster_group cl = cg::this_cluster();
-  const int C = a.cluster;
-  const int crank = static_cast<int>(cl.block_rank());
-  const int row = blockIdx.x / C;
-  const int lo = crank * a.slice;
-  const int n = max(0, min(a.ncols - lo, a.slice));
-  const float* src = a.logits + static_cast<long long>(row) * a.ld + lo;
-  const long long g_lo = static_cast<long long>(a.col_off) + lo;
-
-  extern __shared__ __align__(16) unsigned char smem[];
-  uint32_t* L = reinterpret_cast<uint32_t*>(smem);
-  uint32_t* G = L + kBins;                                     // two buffers
-  uint64_t* cand = reinterpret_cast<uint64_t*>(G + 2 * kBins);  // kCandCap
-  uint32_t* bm = reinterpret_cast<uint32_t*>(cand + kCandCap);
-  __shared__ TopkShared sh;
-
-  cluster_arrive();
-  for (int b = threadIdx.x; b < kBins; b += kThreads) {
-    L[b] = 0;
-    G[b] = 0;
-    G[kBins + b] = 0;
-  }
-  if (threadIdx.x == 0) {
-    sh.count = 0;
-    sh.flag = 0;
-  }
-  if (kPen)
-    build_bitmap(bm, (a.slice >> 5) + 2, a, o, row, g_lo, n);
-  else
-    __syncthreads();
-  const uint32_t k = kEmit ? static_cast<uint32_t>(min(a.cand_k, a.ncols)) : static_cast<uint32_t>(o.k);
-
-  // Pass over the slice: each thread keeps its 4 smallest keys.
-  uint64_t t0 = kNoKey, t1 = kNoKey, t2 = kNoKey, t3 = kNoKey;
-  stream_slice<kPen>(src, n, bm, o.repeat, [&](float v, int j) {
-    const uint64_t d = dkey(v, static_cast<uint32_t>(g_lo + j));
-    if (d < t3) {
-      if (d < t1) {
-        t3 = t2;
-        t2 = t1;
-        if (d < t0) {
-          t1 = t0;
-          t0 = d;
-        } else {
-          t1 = d;
-        }
-      } else if (d < t2) {
-        t3 = t2;
-        t2 = d;
-      } else {
-        t3 = d;
-      }
-    }
-  });
-
-  // Histogram of thread maxima over the top 11 key bits, summed over the
-  // cluster.  The first bin b* at which it reaches k holds the k-th largest
-  // thread maximum, so at least k elements have a key bin <= b*: every
-  // top-k element does.
-  if (t0 != kNoKey) atomicAdd(&L[t0 >> 53], 1u);
-  __syncthreads();
-  cluster_wait();
-  push_u32(L, G, nullptr, cl, C);
-  cluster_sync_all();
-  const Found fb = find_u32x4(G, k, sh);
-  const uint64_t bstar = fb.bin >= 0 ? static_cast<uint64_t>(fb.bin) : static_cast<uint64_t>(kBins - 1);
-
-  // This thread's keys in bins <= b* are candidates.  If its 4th key is one,
-  // a 5th might have been dropped: the cluster then selects exactly.
-  const bool c0 = t0 != kNoKey && (t0 >> 53) <= bstar;
-  const bool c1 = c0 && t1 != kNoKey && (t1 >> 53) <= bstar;
-  const bool c2 = c1 && t2 != kNoKey && (t2 >> 53) <= bstar;
-  const bool c3 = c2 && t3 != kNoKey && (t3 >> 53) <= bstar;
-  const int mine = int(c0) + int(c1) + int(c2) + int(c3);
-  const int lane = threadIdx.x & 31;
-  const int incl = warp_incl_scan(mine);
-  const int wtot = __shfl_sync(0xffffffffu, incl, 31);
-  uint32_t base = 0;
-  if (lane == 31 && wtot) base = atomicAdd(cl.map_shared_rank(&sh.count, 0), static_cast<uint32_t>(wtot));
-  base = __shfl_sync(0xffffffffu, base, 31);
-  {
-    uint64_t* cand0 = cl.map_shared_rank(cand, 0);
-    const uint32_t pos = base + static_cast<uint32_t>(incl - mine);
-    const uint64_t tk[4] = {t0, t1, t2, t3};
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (i < mine && pos + i < static_cast<uint32_t>(kCandCap)) cand0[pos + i] = tk[i];
-  }
-  if (c3) atomicOr(cl.map_shared_rank(&sh.flag, 0), 1u);
-  cluster_sync_all();
-  if (threadIdx.x == 0) {
-    sh.c_total = *cl.map_shared_rank(&sh.count, 0);
-    sh.c_flag = *cl.map_shared_rank(&sh.flag, 0);
-  }
-  __syncthreads();
-  uint32_t total = sh.c_total;
-  const bool fallback = sh.c_flag != 0 || total > static_cast<uint32_t>(kCandCap) || total < k;
-
-  if (fallback) {
-    // Exact radix select of the k-th smallest key, re-reading the slice.
-    cluster_sync_all();  // every CTA has read CTA 0's counters
-    if (crank == 0 && threadIdx.x == 0) sh.count = 0;
-    const int nbits = 32 + a.idxbits;
-    uint64_t prefix = 0;
-    int resolved = 0;
-    uint32_t krem = k;
-    int g = 1;  // G[0] still holds the thread-maxima histogram; cleared in the first pass
-    int sel_shift = 0;
-    while (true) {
-      const int shift = max(0, nbits - resolved - kDig);
-      const int width = nbits - resolved - shift;
-      const uint64_t mask = (1ull << width) - 1;
-      const int hi = nbits - resolved;
-      stream_slice<kPen>(src, n, bm, o.repeat, [&](float v, int j) {
-        const uint64_t kc = ckey(v, static_cast<uint32_t>(g_lo + j), a.idxbits);
-        if (resolved == 0 || (kc >> hi) == prefix) atomicAdd(&L[(kc >> shift) & mask], 1u);
-      });
-      __syncthreads();
-      push_u32(L, G + g * kBins, G + (g ^ 1) * kBins, cl, C);
-      cluster_sync_all();
-      Found f = find_u32x4(G + g * kBins, krem, sh);
-      if (f.bin < 0) {  // unreachable: the cluster holds at least k elements
-        if (threadIdx.x == 0 && crank == 0) raise_status(kErrSelect);
-        f.bin = 0;
-        f.before = 0;
-        f.cnt = krem;
-      }
-      prefix = (prefix << width) | static_cast<uint64_t>(f.bin);
-      resolved += width;
-      krem -= f.before;
-      if (f.cnt == krem || shift == 0) {
-        sel_shift = shift;
-        break;
-      }
-      g ^= 1;
-    }
-    // Collect exactly the k selected elements into CTA 0's buffer.
-    uint64_t* cand0 = cl.map_shared_rank(cand, 0);
-    uint32_t* cnt0 = cl.map_shared_rank(&sh.count, 0);
-    stream_slice<kPen>(src, n, bm, o.repeat, [&](float v, int j) {
-      const uint32_t gid = static_cast<uint32_t>(g_lo + j);
-      const uint64_t kc = ckey(v, gid, a.idxbits);
-      if ((kc >> sel_shift) <= prefix) {
-        const uint32_t p = atomicAdd(cnt0, 1u);
-        if (p < static_cast<uint32_t>(kCandCap)) cand0[p] = dkey(v, gid);
-      }
-    });
-    cluster_sync_all();
-    total = k;
-  }
-
-  cluster_arrive();
-  if (crank != 0) {
-    cluster_wait();
-    return;
-  }
-  const int P = next_pow2(max(static_cast<int>(total), 2));
-  for (int i = static_cast<int>(total) + threadIdx.x; i < P; i += kThreads) cand[i] = kNoKey;
-  __syncthreads();
-  bitonic_sort_u64(cand, P);
-  if (kEmit) {
-    for (int i = threadIdx.x; i < a.cand_k; i += kThreads) {
-      const long long at = static_cast<long long>(row) * a.cand_k + i;
-      const bool ok = i < static_cast<int>(k);
-      a.cand_val[at] = ok ? dval(cand[i]) : -__int_as_float(0x7f800000);
-      a.cand_id[at] = ok ? static_cast<int>(did(cand[i])) : -1;
-    }
-  } else {
-    // L and G are free now: reuse them as the tail's fp64 scratch.
-    double* pr = reinterpret_cast<double*>(smem);
-    double* q = pr + kMaxK;
-    tail_pick(cand, static_cast<int>(k), o, a.rng + 2ll * row, a.out_ids + row, a.stats ? a.stats + row : nullptr,
-              pr, q, &sh.tail);
-  }
-  cluster_wait();
 }
 
 // ====================================================================== merge
@@ -499,7 +166,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const MergeArgs a, cons
   const int P = next_pow2(max(total, 2));
   uint64_t* cand = reinterpret_cast<uint64_t*>(smem);
   double* pr = reinterpret_cast<double*>(cand + P);
-  double* q = pr + kMaxK;
+  double* q = pr + kSplitMaxK;
   __shared__ uint32_t ws[kWarps];
   __shared__ TailShared ts;
   uint32_t valid = 0;
@@ -556,6 +223,21 @@ struct Gath {
   unsigned long long mass[kGatherCap];
 };
 
+// Value-space histogram of the nucleus path: bin = floor((M - v) * kVBins / R)
+// over the row's value range R (see general_kernel).  12 KB, aliasing two Hist.
+constexpr int kVBins = 1024;
+constexpr int kVGatherCap = 512;
+struct VHist {
+  unsigned long long m[kVBins];
+  uint32_t c[kVBins];
+};
+struct VGath {
+  unsigned long long key[kVGatherCap];
+  unsigned long long mass[kVGatherCap];
+};
+static_assert(sizeof(VHist) == 2 * sizeof(Hist), "VHist aliases two Hist");
+static_assert(sizeof(VGath) == 2 * sizeof(Gath), "VGath aliases two Gath");
+
 struct HFound {
   int bin;
   unsigned long long before_m, m, total_m;
@@ -565,7 +247,18 @@ struct HFound {
 struct GenShared {
   uint64_t bar;
   uint64_t xmin[kMaxCluster];
+  float xlo[kMaxCluster];
   unsigned long long xs[kMaxCluster];
+  unsigned long long xz[kMaxCluster];
+  unsigned long long my_s, my_z;  // this CTA's mass-pass totals, pulled by the others
+  // value-path decisions (identical in every CTA)
+  int v_gather;      // 1: resolve by one gather of bins [vb_lo, vb_hi]
+  int vb_lo, vb_hi;
+  unsigned long long vbase_m;  // mass of bins before vb_lo
+  uint32_t vbase_c;
+  unsigned long long v_tp;     // top-p target (0: no cutoff)
+  unsigned long long v_ptot;   // P-set mass
+  uint32_t v_pcnt;             // P-set count (positive fixed mass)
   uint32_t gcount[kMaxGathers];
   unsigned long long ws64[kWarps];
   uint32_t ws32[kWarps];
@@ -652,7 +345,14 @@ struct GenCtx {
   double inv_temp;
   double fscale;  // 2^fixbits
   int C, crank;
+  unsigned long long kc0;  // key of the row's first element in sorted order (always kept by min-p)
 };
+
+// The min-p set (src/sampler.cpp:86-91): weights >= thr, and always the
+// first element in sorted order (keep starts at 1).
+__device__ __forceinline__ bool in_pset(const GenCtx& x, double m, double thr, unsigned long long kc) {
+  return !(thr > 0.0) || m >= thr || kc == x.kc0;
+}
 
 __device__ __forceinline__ unsigned long long fixed_mass(const GenCtx& x, float v, double* m_out) {
   const double m = exp(static_cast<double>(__fsub_rn(canon(v), x.M)) * x.inv_temp);
@@ -687,7 +387,7 @@ __device__ void select_weighted(const GenCtx& x, bool by_mass, unsigned long lon
         if (resolved > 0 && (kc >> hi) != prefix) continue;
         double m;
         const unsigned long long qm = by_mass || thr > 0.0 ? fixed_mass(x, v, &m) : 0ull;
-        if (thr > 0.0 && !(m >= thr)) continue;
+        if (!in_pset(x, m, thr, kc)) continue;
         const int dg = static_cast<int>((kc >> shift) & mask);
         atomicAdd(&L->c[dg], 1u);
         if (by_mass && qm) atomicAdd(&L->m[dg], qm);
@@ -722,7 +422,7 @@ __device__ void select_weighted(const GenCtx& x, bool by_mass, unsigned long lon
         if (kc > klim || (kc >> shift) != prefix) continue;
         double m;
         const unsigned long long qm = by_mass || thr > 0.0 ? fixed_mass(x, v, &m) : 0ull;
-        if (thr > 0.0 && !(m >= thr)) continue;
+        if (!in_pset(x, m, thr, kc)) continue;
         const uint32_t p = atomicAdd(cnt0, 1u);
         if (p < static_cast<uint32_t>(kGatherCap))
           for (int r = 0; r < x.C; ++r) {
@@ -784,7 +484,7 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
   const int bwords = ((((a.slice >> 5) + 2) + 3) / 4) * 4;
   Hist* L = reinterpret_cast<Hist*>(bm + bwords);
   Hist* G = L + 1;   // two buffers
-  Hist* A = L + 3;   // saved first-digit histogram of the mass pass
+  // L[0..3]: radix histograms of the exact selection; the value path reuses the same bytes
   Gath* gb = reinterpret_cast<Gath*>(L + 4);  // two buffers
   __shared__ GenShared sh;
 
@@ -851,16 +551,27 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
   }
   // ---- row maximum (smallest key) across the cluster
   uint64_t best = kNoKey;
+  float lo_f = __int_as_float(0x7f800000);  // smallest finite value
   for (int j = threadIdx.x; j < n; j += kThreads) {
-    const uint64_t d = dkey(v[j], static_cast<uint32_t>(g_lo + j));
+    const float vj = v[j];
+    const uint64_t d = dkey(vj, static_cast<uint32_t>(g_lo + j));
     best = d < best ? d : best;
+    if (isfinite(vj)) lo_f = fminf(lo_f, vj);
   }
   best = block_min<unsigned long long>(best, sh.ws64);
+  lo_f = block_min<float>(lo_f, reinterpret_cast<float*>(sh.ws64));
   cluster_wait();
-  if (threadIdx.x < static_cast<unsigned>(C)) *cl.map_shared_rank(&sh.xmin[crank], threadIdx.x) = best;
+  if (threadIdx.x < static_cast<unsigned>(C)) {
+    *cl.map_shared_rank(&sh.xmin[crank], threadIdx.x) = best;
+    *cl.map_shared_rank(&sh.xlo[crank], threadIdx.x) = lo_f;
+  }
   cluster_sync_all();
   uint64_t dmin = sh.xmin[0];
-  for (int i = 1; i < C; ++i) dmin = sh.xmin[i] < dmin ? sh.xmin[i] : dmin;
+  float row_lo = sh.xlo[0];
+  for (int i = 1; i < C; ++i) {
+    dmin = sh.xmin[i] < dmin ? sh.xmin[i] : dmin;
+    row_lo = fminf(row_lo, sh.xlo[i]);
+  }
   if (crank == 0 && threadIdx.x == 0 && a.rng) {
     a.rng[2ll * row] = s1;
     a.rng[2ll * row + 1] = s0;
@@ -877,6 +588,7 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
   x.fscale = ldexp(1.0, a.fixbits);
   x.C = C;
   x.crank = crank;
+  x.kc0 = ((dmin >> 32) << a.idxbits) | (dmin & 0xffffffffull);
   int gseq = 0, gbuf = 0;
   const unsigned long long kAll = ~0ull;
   const unsigned long long idmask = (1ull << a.idxbits) - 1;
@@ -902,9 +614,27 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
     s_sum = s_tot = __longlong_as_double(0x7ff8000000000000ll);
   } else {
     const double thr = o.min_p > 0.0f ? static_cast<double>(o.min_p) : 0.0;  // pr[0] == 1
-    // ---- mass pass: S over the k-set, first-digit histogram of the min-p set
-    const int shift0 = max(0, x.nbits - kGDig);
-    unsigned long long s_local = 0;
+    VHist* Lv = reinterpret_cast<VHist*>(L);      // aliases L, G[0]
+    VHist* Gv = reinterpret_cast<VHist*>(L + 2);  // aliases G[1], A
+    VGath* vg = reinterpret_cast<VGath*>(gb);
+    if (o.k < o.vocab) {  // the k-limit selection used these buffers
+      for (int b = threadIdx.x; b < kGBins; b += kThreads)
+        for (int i = 0; i < 4; ++i) {
+          L[i].c[b] = 0;
+          L[i].m[b] = 0;
+        }
+      cluster_sync_all();
+    }
+    // Value bins: bin(v) = floor((M - v) * kVBins / R), monotone in v, over the
+    // row's value range R (capped where masses fall below e^-46).
+    const float R = fminf(__fsub_rn(x.M, row_lo), 46.0f * o.temp);
+    const float inv_w = R > 0.0f ? static_cast<float>(kVBins) / R : 0.0f;
+    auto vbin = [&](float vv) -> int {
+      const float d = __fsub_rn(x.M, canon(vv));
+      return static_cast<int>(fminf(__fmul_rn(d, inv_w), static_cast<float>(kVBins - 1)));
+    };
+    // ---- mass pass: S over the k-set; (mass, count) of the min-p set per value bin
+    unsigned long long s_local = 0, z_local = 0;
     for (int j = threadIdx.x; j < n; j += kThreads) {
       const float vv = v[j];
       const unsigned long long kc = ckey(vv, static_cast<uint32_t>(g_lo + j), a.idxbits);
@@ -912,52 +642,295 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
       double m;
       const unsigned long long qm = fixed_mass(x, vv, &m);
       s_local += qm;
-      if (thr > 0.0 && !(m >= thr)) continue;
-      const int dg = static_cast<int>(kc >> shift0);
-      atomicAdd(&L->c[dg], 1u);
-      if (qm) atomicAdd(&L->m[dg], qm);
+      if (!in_pset(x, m, thr, kc)) continue;
+      if (qm == 0) {  // below the fixed-point resolution: counted, never drawn
+        ++z_local;
+        continue;
+      }
+      const int bi = vbin(vv);
+      atomicAdd(&Lv->c[bi], 1u);
+      atomicAdd(&Lv->m[bi], qm);
     }
     s_local = block_sum(s_local, sh.ws64);
-    Hist* Gd = G + gbuf;
-    push_hist(L, Gd, G + (gbuf ^ 1), cl, C);
-    if (threadIdx.x < static_cast<unsigned>(C)) *cl.map_shared_rank(&sh.xs[crank], threadIdx.x) = s_local;
+    z_local = block_sum(z_local, sh.ws64);
+    if (threadIdx.x == 0) {
+      sh.my_s = s_local;
+      sh.my_z = z_local;
+    }
+    // Pull model: every CTA reads all local histograms with plain DSMEM loads
+    // (no remote atomics).  Lv stays untouched until every CTA has pulled it.
     cluster_sync_all();
-    gbuf ^= 1;
-    unsigned long long S = 0;
-    for (int i = 0; i < C; ++i) S += sh.xs[i];
-    A->c[threadIdx.x] = Gd->c[threadIdx.x];
-    A->m[threadIdx.x] = Gd->m[threadIdx.x];
-    __syncthreads();
-    const HFound tot = find_hist(A, true, ~0ull, sh);  // totals only
-    unsigned long long tot_m = tot.total_m;
-    uint32_t keep_c = tot.total_c;
-    unsigned long long klim_keep = klim;
-    // ---- top-p cutoff (src/sampler.cpp:92-100): first element whose running
-    // mass reaches top_p * S within the min-p set
+    const int b0 = 2 * threadIdx.x;
+    unsigned long long m0 = 0, m1 = 0, S = 0, Z = 0;
+    uint32_t c0 = 0, c1 = 0;
+    for (int r = 0; r < C; ++r) {
+      const VHist* Lr = cl.map_shared_rank(Lv, r);
+      m0 += Lr->m[b0];
+      m1 += Lr->m[b0 + 1];
+      c0 += Lr->c[b0];
+      c1 += Lr->c[b0 + 1];
+      S += *cl.map_shared_rank(&sh.my_s, r);
+      Z += *cl.map_shared_rank(&sh.my_z, r);
+    }
+    unsigned long long tm;
+    uint32_t tc;
+    const unsigned long long em = block_excl_scan(m0 + m1, sh.ws64, &tm);
+    const uint32_t ec = block_excl_scan(c0 + c1, sh.ws32, &tc);
+    // First bin whose running mass reaches t (>= 1, <= tm): bin, mass and count before it.
+    auto vfind = [&](unsigned long long t, int* bin, unsigned long long* bm_, uint32_t* bc_, uint32_t* cnt,
+                     unsigned long long* mass) {
+      if (em < t && t <= em + m0) {
+        sh.hf.bin = b0;
+        sh.hf.before_m = em;
+        sh.hf.before_c = ec;
+        sh.hf.c = c0;
+        sh.hf.m = m0;
+      } else if (em + m0 < t && t <= em + m0 + m1) {
+        sh.hf.bin = b0 + 1;
+        sh.hf.before_m = em + m0;
+        sh.hf.before_c = ec + c0;
+        sh.hf.c = c1;
+        sh.hf.m = m1;
+      }
+      __syncthreads();
+      *bin = sh.hf.bin;
+      *bm_ = sh.hf.before_m;
+      *bc_ = sh.hf.before_c;
+      *cnt = sh.hf.c;
+      *mass = sh.hf.m;
+      __syncthreads();
+    };
+    unsigned long long tp = 0;
     if (o.top_p > 0.0f && o.top_p < 1.0f) {
-      const unsigned long long tp =
-          static_cast<unsigned long long>(ceil(static_cast<double>(o.top_p) * static_cast<double>(S)));
-      const unsigned long long tpt = tp < 1ull ? 1ull : tp;
-      if (tot_m >= tpt) {
-        select_weighted(x, true, tpt, A, klim, thr, L, G, gb, gseq, gbuf, cl, sh);
+      const double t = ceil(static_cast<double>(o.top_p) * static_cast<double>(S));
+      tp = t < 1.0 ? 1ull : static_cast<unsigned long long>(t);
+      if (tp > tm) tp = 0;  // the min-p set ends before the top-p cutoff
+    }
+    // Members of the min-p set with positive fixed mass and a value bin (or
+    // sub-bin) accepted by `pick` are gathered, as (key, mass), into the same
+    // buffer of every CTA of the cluster; after the barrier every CTA sorts its
+    // copy and walks it.  Returns the member count (or cap + 1 on overflow).
+    auto gather = [&](auto pick, unsigned long long* gkey, unsigned long long* gmass, int cap) -> int {
+      uint32_t* cnt0 = cl.map_shared_rank(&sh.gcount[gseq++], 0);
+      for (int j = threadIdx.x; j < n; j += kThreads) {
+        const float vv = v[j];
+        const unsigned long long kc = ckey(vv, static_cast<uint32_t>(g_lo + j), a.idxbits);
+        if (kc > klim || !pick(vv)) continue;
+        double m;
+        const unsigned long long qm = fixed_mass(x, vv, &m);
+        if (!in_pset(x, m, thr, kc) || qm == 0) continue;
+        const uint32_t p = atomicAdd(cnt0, 1u);
+        if (p < static_cast<uint32_t>(cap))
+          for (int r = 0; r < C; ++r) {
+            *cl.map_shared_rank(&gkey[p], r) = kc;
+            *cl.map_shared_rank(&gmass[p], r) = qm;
+          }
+      }
+      cluster_sync_all();
+      if (threadIdx.x == 0) sh.ng = *cnt0;
+      __syncthreads();
+      const uint32_t got = sh.ng;
+      __syncthreads();
+      if (got > static_cast<uint32_t>(cap)) return cap + 1;
+      const int ng = static_cast<int>(got);
+      const int P = next_pow2(max(ng, 2));
+      for (int i = ng + threadIdx.x; i < P; i += kThreads) {
+        gkey[i] = kNoKey;
+        gmass[i] = 0;
+      }
+      __syncthreads();
+      sort_pairs(gkey, gmass, P);
+      return ng;
+    };
+    // Walks sorted members from running mass `cm`: index of the first whose
+    // running mass reaches t, or -1.  Run by thread 0 only.
+    auto walk = [&](const unsigned long long* gmass, int ng, unsigned long long cm, unsigned long long t,
+                    unsigned long long* cm_out, int* steps) {
+      for (int i = 0; i < ng; ++i) {
+        cm += gmass[i];
+        if (cm >= t) {
+          *cm_out = cm;
+          *steps = i + 1;
+          return i;
+        }
+      }
+      return -1;
+    };
+    // the cutoff gather lands in the local histogram's space (free after the push)
+    // Buffers: the cutoff gather goes to vg (nobody pulls it); the draw gather
+    // goes to the Lv bytes once every CTA has passed the cutoff barrier (and
+    // so finished pulling Lv), else to vg; a sub-bin histogram goes to Gv.
+    constexpr int kCutCap = kVGatherCap;
+    unsigned long long* ckeys = vg->key;
+    unsigned long long* cmass = vg->mass;
+    bool exact = true;   // resolved without the radix fallback
+    unsigned long long tot_m = tm;
+    uint32_t keep_c = tc + static_cast<uint32_t>(Z);
+    // Gv is read by every CTA before the next barrier; zero our copy now for a
+    // possible sub-bin histogram (other CTAs push into it only after that barrier).
+    const unsigned long long gm0 = m0, gm1 = m1;
+    const uint32_t gc0 = c0, gc1 = c1;
+    (void)gm0; (void)gm1; (void)gc0; (void)gc1;
+    if (tp) {
+      int bc;
+      unsigned long long Bc, mc;
+      uint32_t Cc, nc;
+      vfind(tp, &bc, &Bc, &Cc, &nc, &mc);
+      const int ng = gather([&](float vv) { return vbin(vv) == bc; }, ckeys, cmass, kCutCap);
+      if (ng > kCutCap) {
+        exact = false;
+      } else {
+        if (threadIdx.x == 0) {
+          unsigned long long cm;
+          int st = 0;
+          const int i = walk(cmass, ng, Bc, tp, &cm, &st);
+          sh.r_found = i >= 0;
+          sh.r_cum_m = i >= 0 ? cm : 0;
+          sh.r_cum_c = Cc + static_cast<uint32_t>(st);
+        }
+        __syncthreads();
+        if (!sh.r_found) exact = false;
+        tot_m = sh.r_cum_m;
+        keep_c = sh.r_cum_c;
+        __syncthreads();
+      }
+    }
+    unsigned long long klim_keep = klim;
+    if (exact) {
+      // ---- the draw: target bin from the (saved) running sums of the value histogram
+      const double rt = ceil(u * static_cast<double>(tot_m));
+      unsigned long long t = rt < 1.0 ? 1ull : static_cast<unsigned long long>(rt);
+      if (t > tot_m) t = tot_m;
+      // first bin whose running mass reaches t (from the registers of the scan)
+      if (threadIdx.x == 0) sh.hf.bin = -1;
+      __syncthreads();
+      if (em < t && t <= em + gm0) {
+        sh.hf.bin = b0;
+        sh.hf.before_m = em;
+        sh.hf.c = gc0;
+      } else if (em + gm0 < t && t <= em + gm0 + gm1) {
+        sh.hf.bin = b0 + 1;
+        sh.hf.before_m = em + gm0;
+        sh.hf.c = gc1;
+      }
+      __syncthreads();
+      const int bd = sh.hf.bin;
+      unsigned long long base = sh.hf.before_m;
+      const uint32_t nd = sh.hf.c;
+      __syncthreads();
+      int sub = -1;  // refined sub-bin of bd, or -1 for the whole bin
+      if (nd > static_cast<uint32_t>(kVGatherCap)) {
+        // refine bin bd: 1024 sub-bins of its value interval, counted into Gv
+        // (local), then pulled from every CTA like the value histogram
+        VHist* Ls = Gv;
+        for (int b = threadIdx.x; b < kVBins; b += kThreads) {
+          Ls->c[b] = 0;
+          Ls->m[b] = 0;
+        }
+        __syncthreads();
+        for (int j = threadIdx.x; j < n; j += kThreads) {
+          const float vv = v[j];
+          const unsigned long long kc = ckey(vv, static_cast<uint32_t>(g_lo + j), a.idxbits);
+          if (kc > klim || vbin(vv) != bd) continue;
+          double m;
+          const unsigned long long qm = fixed_mass(x, vv, &m);
+          if (!in_pset(x, m, thr, kc) || qm == 0) continue;
+          const float tt = __fmul_rn(__fsub_rn(x.M, canon(vv)), inv_w);
+          const int sb = min(kVBins - 1, static_cast<int>(__fmul_rn(__fsub_rn(tt, static_cast<float>(bd)), 1024.0f)));
+          atomicAdd(&Ls->c[sb], 1u);
+          atomicAdd(&Ls->m[sb], qm);
+        }
+        cluster_sync_all();
+        unsigned long long s0m = 0, s1m = 0;
+        uint32_t s0c = 0, s1c = 0;
+        for (int r = 0; r < C; ++r) {
+          const VHist* Lr = cl.map_shared_rank(Ls, r);
+          s0m += Lr->m[b0];
+          s1m += Lr->m[b0 + 1];
+          s0c += Lr->c[b0];
+          s1c += Lr->c[b0 + 1];
+        }
+        unsigned long long stm;
+        uint32_t stc;
+        const unsigned long long sem = block_excl_scan(s0m + s1m, sh.ws64, &stm);
+        (void)block_excl_scan(s0c + s1c, sh.ws32, &stc);
+        const unsigned long long tt = t - base;
+        if (threadIdx.x == 0) sh.hf.bin = -1;
+        __syncthreads();
+        if (sem < tt && tt <= sem + s0m) {
+          sh.hf.bin = b0;
+          sh.hf.before_m = sem;
+          sh.hf.c = s0c;
+        } else if (sem + s0m < tt && tt <= sem + s0m + s1m) {
+          sh.hf.bin = b0 + 1;
+          sh.hf.before_m = sem + s0m;
+          sh.hf.c = s1c;
+        }
+        __syncthreads();
+        sub = sh.hf.bin;
+        base += sh.hf.before_m;
+        if (sub < 0 || sh.hf.c > static_cast<uint32_t>(kVGatherCap)) exact = false;
+        __syncthreads();
+      }
+      if (exact) {
+        unsigned long long* dkeys = tp ? reinterpret_cast<unsigned long long*>(Lv) : vg->key;
+        unsigned long long* dmass = tp ? dkeys + kVGatherCap : vg->mass;
+        const int ng = gather(
+            [&](float vv) {
+              if (vbin(vv) != bd) return false;
+              if (sub < 0) return true;
+              const float tt = __fmul_rn(__fsub_rn(x.M, canon(vv)), inv_w);
+              return min(kVBins - 1, static_cast<int>(__fmul_rn(__fsub_rn(tt, static_cast<float>(bd)), 1024.0f))) == sub;
+            },
+            dkeys, dmass, kVGatherCap);
+        if (ng > kVGatherCap) {
+          exact = false;
+        } else {
+          if (threadIdx.x == 0) {
+            unsigned long long cm;
+            int st;
+            const int i = walk(dmass, ng, base, t, &cm, &st);
+            sh.r_found = i >= 0;
+            if (i >= 0) sh.r_key = dkeys[i];
+          }
+          __syncthreads();
+          if (sh.r_found) out_id = static_cast<int>(sh.r_key & idmask);
+          else exact = false;
+          __syncthreads();
+        }
+      }
+    }
+    if (!exact) {
+      // ---- crowded bins (ties, skewed rows): exact mass-weighted radix
+      // selection over the keys
+      cluster_sync_all();  // every CTA is done with the value-path buffers
+      for (int b = threadIdx.x; b < kGBins; b += kThreads)
+        for (int i = 0; i < 4; ++i) {
+          L[i].c[b] = 0;
+          L[i].m[b] = 0;
+        }
+      gbuf = 0;
+      cluster_sync_all();
+      tot_m = tm;
+      keep_c = tc + static_cast<uint32_t>(Z);
+      if (tp) {
+        select_weighted(x, true, tp, nullptr, klim, thr, L, G, gb, gseq, gbuf, cl, sh);
         if (sh.r_found) {
           klim_keep = sh.r_key;
           tot_m = sh.r_cum_m;
           keep_c = sh.r_cum_c;
         }
       }
-    }
-    // ---- the draw (src/sampler.cpp:101-108): first element whose running
-    // mass reaches u * tot
-    double rt = ceil(u * static_cast<double>(tot_m));
-    unsigned long long target = rt < 1.0 ? 1ull : static_cast<unsigned long long>(rt);
-    if (target > tot_m) target = tot_m;
-    select_weighted(x, true, target, A, klim_keep, thr, L, G, gb, gseq, gbuf, cl, sh);
-    if (sh.r_found) {
-      out_id = static_cast<int>(sh.r_key & idmask);
-    } else {
-      out_id = static_cast<int>(klim_keep & idmask);
-      if (threadIdx.x == 0 && crank == 0) raise_status(kErrSelect);
+      const double rt = ceil(u * static_cast<double>(tot_m));
+      unsigned long long target = rt < 1.0 ? 1ull : static_cast<unsigned long long>(rt);
+      if (target > tot_m) target = tot_m;
+      select_weighted(x, true, target, nullptr, klim_keep, thr, L, G, gb, gseq, gbuf, cl, sh);
+      if (sh.r_found) {
+        out_id = static_cast<int>(sh.r_key & idmask);
+      } else {
+        out_id = static_cast<int>(klim_keep & idmask);
+        if (threadIdx.x == 0 && crank == 0) raise_status(kErrSelect);
+      }
     }
     s_sum = static_cast<double>(S) / x.fscale;
     s_tot = static_cast<double>(tot_m) / x.fscale;
@@ -976,11 +949,6 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
 }
 
 // ================================================================ launchers
-size_t greedy_smem(int slice) { return static_cast<size_t>((slice >> 5) + 2) * 4; }
-size_t topk_smem(int slice) {
-  return static_cast<size_t>(3 * kBins) * 4 + static_cast<size_t>(kCandCap) * 8 +
-         static_cast<size_t>((slice >> 5) + 2) * 4;
-}
 size_t general_smem(int slice) {
   const size_t vwords = static_cast<size_t>(((slice + 4 + 3) / 4) * 4);
   const size_t bwords = static_cast<size_t>(((((slice >> 5) + 2) + 3) / 4) * 4);
@@ -991,7 +959,7 @@ static int next_pow2_host(int x) {
   while (p < x) p <<= 1;
   return p;
 }
-size_t merge_smem(int n) { return static_cast<size_t>(next_pow2_host(n < 2 ? 2 : n)) * 8 + 2 * kMaxK * 8; }
+size_t merge_smem(int n) { return static_cast<size_t>(next_pow2_host(n < 2 ? 2 : n)) * 8 + 2 * kSplitMaxK * 8; }
 
 template <class K, class A>
 static cudaError_t launch_cluster(K kernel, const A& args, const DevOpts& o, int grid, int cluster, size_t smem,
@@ -1011,23 +979,6 @@ static cudaError_t launch_cluster(K kernel, const A& args, const DevOpts& o, int
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, args, o);
-}
-
-cudaError_t launch_greedy(const RowArgs& a, const DevOpts& o, cudaStream_t s) {
-  const size_t sm = greedy_smem(a.slice);
-  if (o.penalize) return launch_cluster(greedy_kernel<true>, a, o, a.rows * a.cluster, a.cluster, sm, s);
-  return launch_cluster(greedy_kernel<false>, a, o, a.rows * a.cluster, a.cluster, sm, s);
-}
-
-cudaError_t launch_topk(const RowArgs& a, const DevOpts& o, bool emit, cudaStream_t s) {
-  const size_t sm = topk_smem(a.slice);
-  const int grid = a.rows * a.cluster;
-  if (emit) {
-    if (o.penalize) return launch_cluster(topk_kernel<true, true>, a, o, grid, a.cluster, sm, s);
-    return launch_cluster(topk_kernel<false, true>, a, o, grid, a.cluster, sm, s);
-  }
-  if (o.penalize) return launch_cluster(topk_kernel<true, false>, a, o, grid, a.cluster, sm, s);
-  return launch_cluster(topk_kernel<false, false>, a, o, grid, a.cluster, sm, s);
 }
 
 cudaError_t launch_general(const RowArgs& a, const DevOpts& o, cudaStream_t s) {
@@ -1309,9 +1260,18 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
       const uint32_t ex = block_excl_scan<uint32_t, NT>(mine, sh.ws32, &tot);
       if (tot <= static_cast<uint32_t>(kSliceCap) && tot >= kl) {
         uint32_t at = ex;
-        for_regs(x, n, [&](float v, int j) {
-          if (all || v >= tv) out[at++] = dkey(v, static_cast<uint32_t>(g_lo + j));
-        });
+        if (all) {
+          for_regs(x, n, [&](float v, int j) { out[at++] = dkey(v, static_cast<uint32_t>(g_lo + j)); });
+        } else {  // NaN placeholders beyond n never pass v >= tv
+#pragma unroll
+          for (int i = 0; i < kSplitChunks; ++i) {
+            const int j0 = 4 * (threadIdx.x + i * NT);
+            if (x[i].x >= tv) out[at++] = dkey(x[i].x, static_cast<uint32_t>(g_lo + j0));
+            if (x[i].y >= tv) out[at++] = dkey(x[i].y, static_cast<uint32_t>(g_lo + j0 + 1));
+            if (x[i].z >= tv) out[at++] = dkey(x[i].z, static_cast<uint32_t>(g_lo + j0 + 2));
+            if (x[i].w >= tv) out[at++] = dkey(x[i].w, static_cast<uint32_t>(g_lo + j0 + 3));
+          }
+        }
         count = tot;
       } else {
         // more than kSliceCap candidates (ties, masked rows): exact top-kl
@@ -1342,10 +1302,14 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
     if (threadIdx.x == 0) a.slice_count[slot] = count;
   }
 
-  // publish; the last slice of the row to finish merges
-  __threadfence();
+  // publish; the last slice of the row to finish merges.  The block barrier
+  // orders every thread's partial-result stores before thread 0's fence and
+  // counter increment (the pattern of a grid-wide barrier).
   __syncthreads();
-  if (threadIdx.x == 0) sh.last = atomicAdd(&a.counters[row], 1u) == static_cast<unsigned>(C - 1);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    sh.last = atomicAdd(&a.counters[row], 1u) == static_cast<unsigned>(C - 1);
+  }
   __syncthreads();
   if (!sh.last) return;
   __threadfence();
@@ -1383,51 +1347,65 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
   if (threadIdx.x == 0) sh.ncand = 0;
   __syncthreads();
   const unsigned long long* base = a.slice_keys + static_cast<long long>(row) * C * kSliceCap;
-  uint32_t total;
+  uint64_t* sel = reinterpret_cast<uint64_t*>(H) + 512;  // H bytes [4 KB, 8 KB); the tail uses [0, 4 KB)
   if (utot <= static_cast<uint32_t>(kUnionCap)) {
     for (int e = threadIdx.x; e < C * kSliceCap; e += NT) {
       const int i = e / kSliceCap, j = e - i * kSliceCap;
       if (j < static_cast<int>(scnt[i])) U[soff[i] + j] = __ldcg(base + e);
     }
-    total = utot;
-  } else {
+    __syncthreads();
+  }
+  uint64_t* cand = U;
+  uint32_t total = utot;
+  if (utot > 256u) {
+    // the k best of the union by radix selection, then sort only those
     unsigned long long prefix;
     int shift;
     const int nbits = 32 + a.idxbits;
+    const bool in_smem = utot <= static_cast<uint32_t>(kUnionCap);
     auto each = [&](auto f) {
-      for (int e = threadIdx.x; e < C * kSliceCap; e += NT) {
-        const int i = e / kSliceCap, j = e - i * kSliceCap;
-        if (j < static_cast<int>(scnt[i])) f(to_ckey(__ldcg(base + e), a.idxbits));
+      if (in_smem) {
+        for (int e = threadIdx.x; e < static_cast<int>(utot); e += NT) f(to_ckey(U[e], a.idxbits));
+      } else {
+        for (int e = threadIdx.x; e < C * kSliceCap; e += NT) {
+          const int i = e / kSliceCap, j = e - i * kSliceCap;
+          if (j < static_cast<int>(scnt[i])) f(to_ckey(__ldcg(base + e), a.idxbits));
+        }
       }
     };
     radix_select(each, k, nbits, H, sh, &prefix, &shift);
-    for (int e = threadIdx.x; e < C * kSliceCap; e += NT) {
-      const int i = e / kSliceCap, j = e - i * kSliceCap;
-      if (j < static_cast<int>(scnt[i])) {
-        const unsigned long long d = __ldcg(base + e);
-        if ((to_ckey(d, a.idxbits) >> shift) <= prefix) {
-          const uint32_t p = atomicAdd(&sh.ncand, 1u);
-          if (p < static_cast<uint32_t>(kUnionCap)) U[p] = d;
-        }
+    auto take = [&](unsigned long long d) {
+      if ((to_ckey(d, a.idxbits) >> shift) <= prefix) {
+        const uint32_t p = atomicAdd(&sh.ncand, 1u);
+        if (p < 512u) sel[p] = d;
+      }
+    };
+    if (in_smem) {
+      for (int e = threadIdx.x; e < static_cast<int>(utot); e += NT) take(U[e]);
+    } else {
+      for (int e = threadIdx.x; e < C * kSliceCap; e += NT) {
+        const int i = e / kSliceCap, j = e - i * kSliceCap;
+        if (j < static_cast<int>(scnt[i])) take(__ldcg(base + e));
       }
     }
+    __syncthreads();
+    cand = sel;
     total = k;
   }
-  __syncthreads();
   const int P = next_pow2(max(static_cast<int>(total), 2));
-  for (int i = static_cast<int>(total) + threadIdx.x; i < P; i += NT) U[i] = kNoKey;
+  for (int i = static_cast<int>(total) + threadIdx.x; i < P; i += NT) cand[i] = kNoKey;
   __syncthreads();
-  bitonic_sort_u64(U, P);
+  bitonic_sort_u64(cand, P);
   if (kMode == kSplitEmit) {
     for (int i = threadIdx.x; i < a.cand_k; i += NT) {
       const long long at = static_cast<long long>(row) * a.cand_k + i;
       const bool ok = i < static_cast<int>(k);
-      a.cand_val[at] = ok ? dval(U[i]) : -__int_as_float(0x7f800000);
-      a.cand_id[at] = ok ? static_cast<int>(did(U[i])) : -1;
+      a.cand_val[at] = ok ? dval(cand[i]) : -__int_as_float(0x7f800000);
+      a.cand_id[at] = ok ? static_cast<int>(did(cand[i])) : -1;
     }
   } else {
     double* pr = reinterpret_cast<double*>(H);  // H is free: fp64 scratch of the tail
-    tail_pick(U, static_cast<int>(k), o, a.rng + 2ll * row, a.out_ids + row, a.stats ? a.stats + row : nullptr, pr,
+    tail_pick(cand, static_cast<int>(k), o, a.rng + 2ll * row, a.out_ids + row, a.stats ? a.stats + row : nullptr, pr,
               pr + kSplitMaxK, &sh.tail);
   }
   if (threadIdx.x == 0) a.counters[row] = 0;

@@ -8,8 +8,6 @@
 
 namespace vb {
 
-constexpr int kMaxK = 1024;       // largest top_k handled by the streaming top-k kernel
-constexpr int kCandCap = 2048;    // candidate buffer of that kernel (CTA rank 0)
 constexpr int kMaxSlice = 40960;  // largest per-CTA slice of a row (floats) in the staged kernel
 constexpr int kMaxVocab = kMaxSlice * 8;
 constexpr int kMaxMerge = 4096;   // nshards * k candidates merged per row
@@ -78,12 +76,8 @@ struct MergeArgs {
 };
 
 // Host launchers (kernels.cu).  Return a cudaError_t.
-cudaError_t launch_greedy(const RowArgs& a, const DevOpts& o, cudaStream_t s);
-cudaError_t launch_topk(const RowArgs& a, const DevOpts& o, bool emit, cudaStream_t s);
 cudaError_t launch_general(const RowArgs& a, const DevOpts& o, cudaStream_t s);
 cudaError_t launch_merge(const MergeArgs& a, const DevOpts& o, cudaStream_t s);
-size_t greedy_smem(int slice);
-size_t topk_smem(int slice);
 size_t general_smem(int slice);
 size_t merge_smem(int n);
 cudaError_t read_status(unsigned* st, bool clear, cudaStream_t s);
