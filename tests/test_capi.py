@@ -121,3 +121,23 @@ def test_error_message_is_thread_local_and_cleared(lib):
     assert lib.verbo_cuda_last_error().decode() != ""
     assert _sample(lib, rows=0) == 0
     assert lib.verbo_cuda_last_error().decode() == ""
+
+
+def _build_hpp_kat(tmp_path):
+    exe = tmp_path / "hpp_kat"
+    subprocess.run(["g++", "-std=c++17", "-O1", f"-I{ROOT / 'include'}", str(ROOT / "tests/cpp/hpp_kat.cpp"),
+                    f"-L{build.LIB.parent}", "-lverbo_cuda", f"-Wl,-rpath,{build.LIB.parent}", "-o", str(exe)],
+                   check=True, capture_output=True)
+    return exe
+
+
+def test_cpp_header_compiles_and_reports_errors(lib, tmp_path):
+    """The C++ wrapper builds against the library; without a usable device the
+    constructor throws with the C ABI's message instead of crashing."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("device present: covered by the gpu test")
+    exe = _build_hpp_kat(tmp_path)
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 2 and r.stdout.startswith("error verbo_cuda:"), r.stdout

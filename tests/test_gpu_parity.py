@@ -263,3 +263,13 @@ def test_crowded_bins_use_exact_fallback():
         ora, ost, _ = run_oracle(x, opts, seeds, steps=2)
         compare(ids, ora, ost, str(opts))
         np.testing.assert_allclose(st["sum"], ost[:, -1]["sum"], rtol=1e-9)
+
+
+def test_cpp_header_known_answers(tmp_path):
+    from tests.test_capi import _build_hpp_kat
+
+    exe = _build_hpp_kat(tmp_path)
+    import subprocess
+
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
