@@ -92,6 +92,28 @@ VERBO_CUDA_API int verbo_cuda_sample(const float* logits, int rows, int vocab, l
                                      unsigned long long* rng, int* out_ids, verbo_row_stats* stats,
                                      void* stream);
 
+/* No counterpart in the reference (its sampler never touches the GPU).
+   Same arguments and results as verbo_cuda_sample, for greedy and
+   0 < top_k <= 256, but it allocates nothing: no cudaMalloc, cudaFree or
+   allocating library call.  It is meant for callers that cannot let a library
+   allocate device memory behind their back: a serving engine that reserves
+   almost all of HBM for its KV cache up front and runs its own allocator,
+   or a latency-sensitive decode loop that cannot afford the device-wide
+   synchronisation of cudaMalloc/cudaFree (verbo_cuda_sample allocates its
+   scratch on first use per stream and grows it for larger batches).
+   Its scratch is a fixed 8 MiB array inside the library, held by every device
+   that loads the library until the process exits: up to about 272 rows per
+   call at vocab 151936 (127 at the largest vocab, 327680); larger calls are
+   rejected with an error.  The first call on each device looks up the
+   array's address (cudaGetSymbolAddress); make that first call before any
+   stream capture.  All calls share the array: calls that overlap on the GPU
+   (concurrent streams or host threads) race and must be serialised by the
+   caller. */
+VERBO_CUDA_API int verbo_cuda_sample_noalloc(const float* logits, int rows, int vocab, long long ld,
+                                             const int* hist, const long long* hist_off,
+                                             const verbo_sampling* opts, unsigned long long* rng, int* out_ids,
+                                             verbo_row_stats* stats, void* stream);
+
 /* Vocab-sharded sampling, step 1: for a shard holding global columns
    [col_offset, col_offset + shard_cols) of each row, apply the penalty for
    the history ids that fall in the shard and emit the shard's k best

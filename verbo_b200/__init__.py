@@ -26,7 +26,7 @@ from dataclasses import dataclass
 from pathlib import Path
 from typing import Optional, Sequence
 
-__all__ = ["Sampling", "Sampler", "VerboCudaError", "load_library", "sample", "shard_topk", "merge_sample",
+__all__ = ["Sampling", "Sampler", "VerboCudaError", "load_library", "sample", "sample_noalloc", "shard_topk", "merge_sample",
            "seed_states", "check", "version", "ROW_STATS_FIELDS"]
 __version__ = "0.1.0"
 
@@ -109,6 +109,8 @@ def load_library():
         "verbo_cuda_rng_unit": (ctypes.c_double, [_P]),
         "verbo_cuda_sample": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, _P, _P,
                                              ctypes.POINTER(_Sampling), _P, _P, _P, _P]),
+        "verbo_cuda_sample_noalloc": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, _P, _P,
+                                                     ctypes.POINTER(_Sampling), _P, _P, _P, _P]),
         "verbo_cuda_shard_topk": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, ctypes.c_int,
                                                  ctypes.c_int, _P, _P, ctypes.POINTER(_Sampling), ctypes.c_int,
                                                  _P, _P, _P]),
@@ -200,6 +202,27 @@ def sample(logits, opts: Sampling, rng=None, hist=None, hist_off=None, out=None,
     rc = load_library().verbo_cuda_sample(_dptr(logits, True), rows, vocab, logits.stride(0), _dptr(hist),
                                           _dptr(hist_off),
                                           ctypes.byref(o), _dptr(rng), _dptr(out), _dptr(stats), _stream(stream))
+    _ok(rc)
+    return out
+
+
+def sample_noalloc(logits, opts: Sampling, rng=None, hist=None, hist_off=None, out=None, stats=None, vocab=None,
+                   stream=None):
+    """``sample`` through verbo_cuda_sample_noalloc: for callers that cannot let
+    the library allocate device memory (greedy and 0 < top_k <= 256 only; a
+    fixed 8 MiB scratch inside the library, shared by all calls)."""
+    import torch
+
+    rows, cols = logits.shape
+    vocab = cols if vocab is None else vocab
+    if logits.dtype != torch.float32:
+        raise VerboCudaError("logits must be float32")
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    o = opts._c()
+    rc = load_library().verbo_cuda_sample_noalloc(_dptr(logits, True), rows, vocab, logits.stride(0), _dptr(hist),
+                                                  _dptr(hist_off), ctypes.byref(o), _dptr(rng), _dptr(out),
+                                                  _dptr(stats), _stream(stream))
     _ok(rc)
     return out
 

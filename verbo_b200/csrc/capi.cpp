@@ -291,6 +291,47 @@ VERBO_CUDA_API int verbo_cuda_sample(const float* logits, int rows, int vocab, l
       -1);
 }
 
+// Callers that cannot allocate device memory: see include/verbo_cuda.h.
+// Same arguments and results as verbo_cuda_sample for greedy and
+// 0 < top_k <= 256, without any cudaMalloc / cudaFree.
+VERBO_CUDA_API int verbo_cuda_sample_noalloc(const float* logits, int rows, int vocab, long long ld, const int* hist,
+                                             const long long* hist_off, const verbo_sampling* opts,
+                                             unsigned long long* rng, int* out_ids, verbo_row_stats* stats,
+                                             void* stream) {
+  return guard(
+      [&]() {
+        if (!opts) fail("opts is NULL");
+        if (rows < 0) fail("rows must be >= 0");
+        if (rows == 0) return 0;
+        if (!logits || !out_ids) fail("logits and out_ids must not be NULL");
+        if (vocab < 1 || vocab > vb::kMaxVocab) fail("vocab must be in [1, " + std::to_string(vb::kMaxVocab) + "]");
+        if (ld < vocab) fail("ld must be >= vocab");
+        check_hist(hist, hist_off);
+        const vb::DevOpts o = make_opts(*opts, vocab, hist != nullptr);
+        if (!o.greedy && !rng) fail("rng state is required when temp > 0");
+        if (!o.greedy && !(o.k < vocab && o.k <= vb::kSplitMaxK))
+          fail("the allocation-free entry point needs temp <= 0 or 0 < top_k <= " +
+               std::to_string(vb::kSplitMaxK) + " (and top_k < vocab)");
+        vb::RowArgs a = row_args(logits, rows, vocab, ld, 0, vocab, hist, hist_off);
+        a.rng = rng;
+        a.out_ids = out_ids;
+        a.stats = stats;
+        plan_split(a);
+        bool too_big = false;
+        cuda_ok(vb::launch_split_noalloc(a, o, o.greedy ? vb::kSplitGreedy : vb::kSplitSample,
+                                         static_cast<cudaStream_t>(stream), &too_big),
+                "kernel launch");
+        if (too_big) {
+          const long long per_row = 4 + 4ll * a.cluster + 8ll * a.cluster * vb::kSliceCap;
+          fail("rows x vocab exceed the fixed scratch of " + std::to_string(vb::kNoAllocScratchBytes >> 20) +
+               " MiB: at most about " + std::to_string((vb::kNoAllocScratchBytes - 512) / per_row) +
+               " rows at vocab " + std::to_string(vocab) + " per call");
+        }
+        return 0;
+      },
+      -1);
+}
+
 VERBO_CUDA_API int verbo_cuda_shard_topk(const float* logits, int rows, int shard_cols, long long ld, int col_offset,
                                          int vocab, const int* hist, const long long* hist_off,
                                          const verbo_sampling* opts, int k, float* cand_val, int* cand_id,

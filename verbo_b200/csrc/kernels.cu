@@ -23,6 +23,8 @@
 //                   mass-weighted radix selection over the keys handles rows
 //                   whose bins are too crowded.  No full sort.
 //   merge_kernel    merges per-shard candidates and runs the same tail.
+#include <mutex>
+
 #include "device.cuh"
 #include "kernels.cuh"
 
@@ -1440,6 +1442,53 @@ cudaError_t launch_split(const RowArgs& a, const DevOpts& o, int mode, cudaStrea
     case 4: return launch_split_t<kSplitEmit, false>(a, o, s);
     default: return launch_split_t<kSplitEmit, true>(a, o, s);
   }
+}
+
+// ================================================ allocation-free scratch ==
+// Scratch for verbo_cuda_sample_noalloc: a fixed array in the library's own
+// device image instead of memory from cudaMalloc.  Every device that loads the
+// library holds these kNoAllocScratchBytes until the process exits.  All calls
+// share it and it keeps the last call's contents; calls that overlap on the
+// GPU (different streams, or several host threads) race on it.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// The array's device address on the current device.  Host code cannot use the
+// symbol itself (that is a host-side stand-in, not a device address): the
+// address is looked up once per device with cudaGetSymbolAddress, with that
+// device current.
+static cudaError_t noalloc_scratch_address(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return cudaSuccess;
+}
+
+cudaError_t launch_split_noalloc(RowArgs& a, const DevOpts& o, int mode, cudaStream_t s, bool* too_big) {
+  size_t off_count = 0, off_keys = 0;
+  *too_big = split_scratch_bytes(a.rows, a.cluster, &off_count, &off_keys) > kNoAllocScratchBytes;
+  if (*too_big) return cudaSuccess;
+  void* base = nullptr;
+  cudaError_t e = noalloc_scratch_address(&base);
+  if (e != cudaSuccess) return e;
+  a.counters = static_cast<unsigned*>(base);
+  a.slice_count = reinterpret_cast<unsigned*>(static_cast<char*>(base) + off_count);
+  a.slice_keys = reinterpret_cast<unsigned long long*>(static_cast<char*>(base) + off_keys);
+  // The per-row counters must start at zero.  The kernel leaves them at zero,
+  // but the array also serves calls of other shapes, so clear them here.
+  e = cudaMemsetAsync(a.counters, 0, static_cast<size_t>(a.rows) * sizeof(unsigned), s);
+  if (e != cudaSuccess) return e;
+  return launch_split(a, o, mode, s);
 }
 
 }  // namespace vb

@@ -66,6 +66,12 @@ size_t split_scratch_bytes(long long rows, int slices, size_t* off_count, size_t
 cudaError_t launch_split(const RowArgs& a, const DevOpts& o, int mode, cudaStream_t s);
 enum SplitMode { kSplitGreedy = 0, kSplitSample = 1, kSplitEmit = 2 };
 
+// Allocation-free variant: the split kernel with its scratch in a fixed
+// device array of kNoAllocScratchBytes (kernels.cu).  Sets *too_big (and
+// launches nothing) when rows x slices need more than that.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+cudaError_t launch_split_noalloc(RowArgs& a, const DevOpts& o, int mode, cudaStream_t s, bool* too_big);
+
 struct MergeArgs {
   const float* cand_val;  // [nshards][rows][k]
   const int* cand_id;
