@@ -60,6 +60,7 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-soak", action="store_true", help="skip the 1 s load window kept for the clock record")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
+    p.add_argument("--no-graph", action="store_true", help="launch each timed step from the host instead of a CUDA graph")
     a = p.parse_args()
     if a.warmup < 3:
         p.error("--warmup must be >= 3")
@@ -203,53 +204,69 @@ def bench_rows(a, w: wl.Workload, rank: int, world: int, dev):
     st = np.array(vb.seed_states(seeds.tolist()), dtype=np.uint64)
     rng = torch.from_numpy(st.view(np.int64).copy()).to(dev)
     out = torch.empty(R, dtype=torch.int32, device=dev)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream(device=dev)
 
     def step(i):
         vb.sample(xs[i % copies], opts, rng=rng, hist=h, hist_off=off, out=out, stream=stream)
 
-    for i in range(a.warmup):
-        step(i)
-    vb.check(stream)
-    clocks = Clocks(torch.cuda.current_device()) if rank == 0 else None
-    if clocks:
-        clocks.start()
-    if clocks and not a.no_soak:
-        t_soak = time.perf_counter()
-        i = 0
-        while time.perf_counter() - t_soak < 1.0:   # >= 1 s of load around the timed region for the clock record
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(a.warmup):
             step(i)
-            i += 1
-            if i % 64 == 0:
-                torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    t0.record(stream)
-    for i in range(a.steps):
-        ev[i][0].record(stream)
-        step(i)
-        ev[i][1].record(stream)
-    t1.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    if clocks:
-        clocks.stop()
-    vb.check(stream)
+        vb.check(stream)
+        # Device-resident timing replays each step from a CUDA graph (one per
+        # input copy), so host launch overhead does not gap the device work;
+        # the library's scratch for this stream exists after the warm-up.
+        graphs = []
+        if not a.no_graph:
+            for c in range(copies):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    step(c)
+                graphs.append(g)
+        run = (lambda i: graphs[i % copies].replay()) if graphs else step
+        clocks = Clocks(torch.cuda.current_device()) if rank == 0 else None
+        if clocks:
+            clocks.start()
+        if clocks and not a.no_soak:
+            t_soak = time.perf_counter()
+            i = 0
+            while time.perf_counter() - t_soak < 1.0:   # >= 1 s of load around the timed region for the clock record
+                run(i)
+                i += 1
+                if i % 64 == 0:
+                    torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for i in range(a.steps):
+            ev[i][0].record(stream)
+            run(i)
+            ev[i][1].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        if clocks:
+            clocks.stop()
+        vb.check(stream)
     elapsed = t0.elapsed_time(t1)
-    launch_ms = sum(s.elapsed_time(e) for s, e in ev) / a.steps
+    launch_ms = sum(s_.elapsed_time(e_) for s_, e_ in ev) / a.steps
     red = torch.tensor([elapsed, launch_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(red, op=dist.ReduceOp.MAX)
     elapsed, launch_ms = red.tolist()
+    del graphs
 
     res = dict(R=R, elapsed_ms=elapsed, launch_ms=launch_ms, copies=copies, batch_bytes=batch_bytes,
-               launches=a.steps, clocks=clocks.summary() if clocks else None)
+               launches=a.steps * kernels_per_step(w), clocks=clocks.summary() if clocks else None,
+               graph=not a.no_graph)
     if not a.no_e2e:
-        res.update(e2e_rows(a, w, R, V, xs[0], h, off, opts, rng, out, stream, world, dev))
+        with torch.cuda.stream(stream):  # copies and sampling on one stream
+            res.update(e2e_rows(a, w, R, V, xs[0], h, off, opts, rng, out, stream, world, dev))
     host_sample = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         from oracle import pyoracle as po
@@ -392,7 +409,7 @@ def bench_sharded(a, w: wl.Workload, rank: int, world: int, dev):
         dist.all_reduce(red, op=dist.ReduceOp.MAX)
     elapsed, launch_ms = red.tolist()
     return dict(R=R, cols=cols, elapsed_ms=elapsed, launch_ms=launch_ms, copies=copies, batch_bytes=batch_bytes,
-                launches=3 * a.steps, clocks=clocks.summary() if clocks else None)
+                launches=kernels_per_step(w) * a.steps, clocks=clocks.summary() if clocks else None, graph=False)
 
 
 # ------------------------------------------------------------ reference arm ----
@@ -499,9 +516,10 @@ def main():
             **({"columns_per_gpu": cols} if sharded else {})),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "traffic": None if tr is None else tr * R,
-                     "kernel": "shard_topk_kernel" if sharded else kernel_name(w),
+                     "kernel": "split_kernel<emit> + merge" if sharded else kernel_name(w),
                      "alg_bytes_per_launch": alg_launch, "launch_ms": res["launch_ms"]},
         "clocks": res["clocks"],
+        "timing": "CUDA graph replay per step" if res.get("graph") else "host launch per step",
         "gpu_launches": res["launches"] * world,
     }
     if not sharded and "e2e_ms" in res:
@@ -519,11 +537,18 @@ def main():
     print(json.dumps(line), flush=True)
 
 
+def kernels_per_step(w: wl.Workload) -> int:
+    """Kernels of this library launched by one sampling step."""
+    if w.shards > 1:
+        return 3   # split_kernel<emit> + merge_slices_kernel + merge_kernel
+    return 1 if kernel_name(w) == "general_kernel" else 2
+
+
 def kernel_name(w: wl.Workload) -> str:
     if w.temp <= 0:
-        return "greedy_kernel"
-    if 0 < w.top_k < w.vocab and w.top_k <= 1024:
-        return "topk_kernel"
+        return "split_kernel<greedy> + merge_slices_kernel"
+    if 0 < w.top_k < w.vocab and w.top_k <= 256:
+        return "split_kernel<sample> + merge_slices_kernel"
     return "general_kernel"
 
 

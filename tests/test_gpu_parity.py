@@ -265,6 +265,30 @@ def test_crowded_bins_use_exact_fallback():
         np.testing.assert_allclose(st["sum"], ost[:, -1]["sum"], rtol=1e-9)
 
 
+@pytest.mark.parametrize("k", [1, 2, 31, 33, 50, 64, 128, 255, 256])
+def test_split_topk_bounds(k):
+    # The split top-k kernels bound each slice (and then the union) by the
+    # q-th largest lane maximum of every full warp; rows with ties at the
+    # bound, coarse values (the exact fallbacks), a short last slice and
+    # masked stretches must still give the reference's top-k.
+    g = np.random.default_rng(k)
+    V = 151936
+    x = (g.standard_normal((5, V)) * 2).astype(np.float32)
+    x[1] = np.round(x[1] * 2) / 4                       # ~40 distinct values: every slice overflows
+    x[2, g.integers(0, V, size=3000)] = x[2].max()      # many ties at the top
+    x[3, : V - 5000] = -np.inf                          # only the last slices hold finite values
+    x[4, ::3] = -np.inf
+    hist = g.integers(0, V, size=5 * 64).astype(np.int32)
+    off = np.arange(6, dtype=np.int64) * 64
+    seeds = np.arange(5, dtype=np.uint64) + np.uint64(900 + k)
+    for opts in (dict(temp=0.8, top_k=k, top_p=0.95, repeat=1.1), dict(temp=1.3, top_k=k, top_p=1.0, min_p=0.02)):
+        ids, st, _ = run_gpu(x, opts, seeds, hist, off, steps=2)
+        ora, ost, _ = run_oracle(x, opts, seeds, hist, off, steps=2)
+        compare(ids, ora, ost, f"k={k} {opts}")
+        assert np.array_equal(st["k"], ost[:, -1]["k"])
+        np.testing.assert_allclose(st["sum"], ost[:, -1]["sum"], rtol=1e-9)
+
+
 def test_cpp_header_known_answers(tmp_path):
     from tests.test_capi import _build_hpp_kat
 

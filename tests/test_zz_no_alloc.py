@@ -79,7 +79,7 @@ def test_noalloc_rejects_sizes_beyond_the_scratch(vb):
                                        ids.data_ptr(), None, None)
     assert rc == -1
     msg = lib.verbo_cuda_last_error().decode()
-    assert "fixed scratch" in msg and "272 rows" in msg
+    assert "fixed scratch" in msg and "rows at vocab 151936" in msg
 
 
 def test_noalloc_rejects_options_outside_its_kernel(vb):

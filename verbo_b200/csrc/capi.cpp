@@ -117,15 +117,13 @@ vb::RowArgs row_args(const float* logits, int rows, int ncols, long long ld, int
   return a;
 }
 
-// Scratch of the split-row kernels, one set per (device, stream) so that calls
-// on different streams never share it.  `counters` holds one u32 per row; the
-// kernels leave every counter at zero, so it is zeroed only when it grows.
-// `data` holds the per-slice partial results and needs no initialisation.
+// Scratch of the split-row kernels, one buffer per (device, stream) so that
+// calls on different streams never share it: per-slice counts and candidate
+// keys, written by the streaming kernel and read by the merge kernel of the
+// same call.  Allocated on first use, grown when a larger batch arrives.
 struct Scratch {
-  unsigned* counters = nullptr;
-  long long counter_rows = 0;
   void* data = nullptr;
-  size_t data_bytes = 0;
+  size_t bytes = 0;
 };
 std::mutex g_scratch_mu;
 std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
@@ -133,31 +131,21 @@ std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
 void attach_split_scratch(vb::RowArgs& a, cudaStream_t s) {
   int dev = 0;
   cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
-  size_t off_count = 0, off_keys = 0;
-  const size_t bytes = vb::split_scratch_bytes(a.rows, a.cluster, &off_count, &off_keys) - off_count;
+  size_t off_keys = 0;
+  const size_t bytes = vb::split_scratch_bytes(a.rows, a.cluster, &off_keys);
   std::lock_guard<std::mutex> lk(g_scratch_mu);
   Scratch& sc = g_scratch[{dev, s}];
-  if (sc.counter_rows < a.rows || sc.data_bytes < bytes) cuda_ok(cudaStreamSynchronize(s), "stream");
-  if (sc.counter_rows < a.rows) {
-    const long long n = std::max<long long>(a.rows, 2 * sc.counter_rows);
-    cudaFree(sc.counters);
-    sc.counters = nullptr;
-    sc.counter_rows = 0;
-    cuda_ok(cudaMalloc(&sc.counters, static_cast<size_t>(n) * sizeof(unsigned)), "cudaMalloc scratch");
-    cuda_ok(cudaMemsetAsync(sc.counters, 0, static_cast<size_t>(n) * sizeof(unsigned), s), "cudaMemsetAsync");
-    sc.counter_rows = n;
-  }
-  if (sc.data_bytes < bytes) {
-    const size_t n = std::max(bytes, 2 * sc.data_bytes);
+  if (sc.bytes < bytes) {
+    cuda_ok(cudaStreamSynchronize(s), "stream");  // the old buffer may still be in use
+    const size_t n = std::max(bytes, 2 * sc.bytes);
     cudaFree(sc.data);
     sc.data = nullptr;
-    sc.data_bytes = 0;
+    sc.bytes = 0;
     cuda_ok(cudaMalloc(&sc.data, n), "cudaMalloc scratch");
-    sc.data_bytes = n;
+    sc.bytes = n;
   }
-  a.counters = sc.counters;
   a.slice_count = static_cast<unsigned*>(sc.data);
-  a.slice_keys = reinterpret_cast<unsigned long long*>(static_cast<char*>(sc.data) + (off_keys - off_count));
+  a.slice_keys = reinterpret_cast<unsigned long long*>(static_cast<char*>(sc.data) + off_keys);
 }
 
 // Slices of the split-row kernels: the fewest slices of <= kSplitSlice columns.
@@ -322,7 +310,7 @@ VERBO_CUDA_API int verbo_cuda_sample_noalloc(const float* logits, int rows, int 
                                          static_cast<cudaStream_t>(stream), &too_big),
                 "kernel launch");
         if (too_big) {
-          const long long per_row = 4 + 4ll * a.cluster + 8ll * a.cluster * vb::kSliceCap;
+          const long long per_row = 4ll * a.cluster + 8ll * a.cluster * vb::kSliceCap;
           fail("rows x vocab exceed the fixed scratch of " + std::to_string(vb::kNoAllocScratchBytes >> 20) +
                " MiB: at most about " + std::to_string((vb::kNoAllocScratchBytes - 512) / per_row) +
                " rows at vocab " + std::to_string(vocab) + " per call");

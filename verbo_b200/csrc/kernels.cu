@@ -8,11 +8,13 @@
 //                   per-slice bitmap, and reduces its columns with float
 //                   compares.  Greedy publishes the slice's best key; top-k
 //                   bounds the slice's top-k by a histogram of thread maxima
-//                   and publishes every column above the bound.  The last CTA
-//                   of the row (per-row atomic counter) merges: the best key,
-//                   or a sort of the union of candidates followed by the
-//                   reference's softmax / min-p / top-p / draw in the same
-//                   fp64 order (sampler.cpp:79-108).
+//                   and publishes every column above the bound.  The CTA then
+//                   exits.
+//   merge_slices_kernel  One CTA per row, after split_kernel on the same
+//                   stream: the best key, or a radix selection of the k best
+//                   of the union of candidates followed by the reference's
+//                   softmax / min-p / top-p / draw in the same fp64 order
+//                   (sampler.cpp:79-108).
 //   general_kernel  (top_k == 0, top_k > 256 or top_k >= vocab)  One thread-
 //                   block cluster per row; each CTA stages its slice in shared
 //                   memory with bulk async copies.  Masses exp((v - M) / T) in
@@ -1026,6 +1028,7 @@ constexpr int kUnionCap = 2048;
 
 struct Shared {
   unsigned long long ws64[NW];
+  float offer[NW];  // each full warp's q-th largest lane maximum
   uint32_t ws32[NW];
   Found found;
   uint32_t ncand;
@@ -1110,23 +1113,55 @@ __device__ __forceinline__ unsigned long long regs_best(const float4 (&x)[kSplit
   return dkey(bv, static_cast<uint32_t>(g_lo + bj));
 }
 
-// First bin (of kBinsS counts, 8 per thread) where the running count reaches target >= 1.
+// The largest of the thread's values; NaN (logits and the placeholders beyond
+// n) is ignored, so a thread without a finite or infinite value yields -inf.
+__device__ __forceinline__ float regs_max(const float4 (&x)[kSplitChunks]) {
+  float m = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (int i = 0; i < kSplitChunks; ++i) m = fmaxf(fmaxf(m, fmaxf(x[i].x, x[i].y)), fmaxf(x[i].z, x[i].w));
+  return m;
+}
+
+// Descending bitonic sort of one non-NaN float per lane across the warp.
+__device__ __forceinline__ float warp_sort_desc(float v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const float p = __shfl_xor_sync(0xffffffffu, v, j);
+      v = (((lane & j) == 0) == ((lane & k) == 0)) ? fmaxf(v, p) : fminf(v, p);
+    }
+  }
+  return v;
+}
+
+// First bin (of kBinsS counts, kBinsS / NT per thread) where the running
+// count reaches target >= 1.
 __device__ Found find_bins(const uint32_t* H, uint32_t target, Shared& sh) {
+  constexpr int PER = kBinsS / NT;
+  static_assert(PER % 4 == 0, "bins per thread must be a multiple of 4");
   if (threadIdx.x == 0) sh.found.bin = -1;
-  const uint4 a = reinterpret_cast<const uint4*>(H)[2 * threadIdx.x];
-  const uint4 b = reinterpret_cast<const uint4*>(H)[2 * threadIdx.x + 1];
-  const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t v[PER];
+#pragma unroll
+  for (int i = 0; i < PER / 4; ++i) {
+    const uint4 q = reinterpret_cast<const uint4*>(H)[(PER / 4) * threadIdx.x + i];
+    v[4 * i] = q.x;
+    v[4 * i + 1] = q.y;
+    v[4 * i + 2] = q.z;
+    v[4 * i + 3] = q.w;
+  }
   uint32_t s = 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) s += v[i];
+  for (int i = 0; i < PER; ++i) s += v[i];
   uint32_t total;
   const uint32_t ex = block_excl_scan<uint32_t, NT>(s, sh.ws32, &total);
   if (ex < target && target <= ex + s) {
     uint32_t e = ex;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < PER; ++i) {
       if (target <= e + v[i]) {
-        sh.found.bin = 8 * threadIdx.x + i;
+        sh.found.bin = PER * threadIdx.x + i;
         sh.found.before = e;
         sh.found.cnt = v[i];
         break;
@@ -1198,15 +1233,12 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
   const float* src = a.logits + static_cast<long long>(row) * a.ld + lo;
   const long long g_lo = static_cast<long long>(a.col_off) + lo;
   extern __shared__ __align__(16) unsigned char smem[];
-  uint32_t* H = reinterpret_cast<uint32_t*>(smem);                          // kBinsS counts (top-k modes)
-  uint64_t* U = reinterpret_cast<uint64_t*>(H + kBinsS);  // kUnionCap keys (top-k modes)
-  uint32_t* bm = kMode == kSplitGreedy ? reinterpret_cast<uint32_t*>(smem) : reinterpret_cast<uint32_t*>(U + kUnionCap);
+  uint32_t* H = reinterpret_cast<uint32_t*>(smem);  // kBinsS counts (top-k modes, exact fallback)
+  uint32_t* bm = kMode == kSplitGreedy ? H : H + kBinsS;  // penalty bitmap of the slice
   __shared__ Shared sh;
 
   float4 x[kSplitChunks];
   load_regs(src, n, x);  // all loads in flight before anything else
-  if (kMode != kSplitGreedy)
-    for (int b = threadIdx.x; b < kBinsS; b += NT) H[b] = 0;
   if (threadIdx.x == 0) sh.ncand = 0;
   if (kPen) {
     const int nw = (a.slice >> 5) + 2;
@@ -1233,50 +1265,57 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
   } else {
     const uint32_t k = kMode == kSplitEmit ? static_cast<uint32_t>(min(a.cand_k, a.ncols)) : static_cast<uint32_t>(o.k);
     const uint32_t kl = min(k, static_cast<uint32_t>(n));
-    // Bound from the slice's thread maxima: the first 11-bit key bin where
-    // their count reaches kl has at least kl elements at or above it, so the
-    // slice's top-kl lies in bins <= b*.
-    const unsigned long long tmin = regs_best(x, n, g_lo);
-    if (tmin != kNoKey) atomicAdd(&H[tmin >> 53], 1u);
-    __syncthreads();
     uint32_t count = 0;
     unsigned long long* out = a.slice_keys + slot * kSliceCap;
     if (kl > 0) {
-      const Found fb = find_bins(H, kl, sh);
-      for (int b = threadIdx.x; b < kBinsS; b += NT) H[b] = 0;
-      const uint32_t bstar = fb.bin >= 0 ? static_cast<uint32_t>(fb.bin) : kBinsS - 1u;
-      // bins <= b*  <=>  ord32(v) >= T  <=>  v >= unord32(T) for non-NaN v.
-      // T <= ord32(-inf) means every column is a candidate (-inf and NaN too).
-      const uint32_t T = ~(((bstar + 1u) << 21) - 1u);
-      const bool all = T <= 0x007fffffu;
-      const float tv = unord32(T);
-      uint32_t mine = 0;
-      if (all) {
-        for_regs(x, n, [&](float, int) { ++mine; });
-      } else {
-#pragma unroll
-        for (int i = 0; i < kSplitChunks; ++i)
-          mine += uint32_t(x[i].x >= tv) + uint32_t(x[i].y >= tv) + uint32_t(x[i].z >= tv) + uint32_t(x[i].w >= tv);
+      // Value bound T: every full warp (32 lanes holding columns) offers the
+      // q-th largest of its lanes' maxima, q = ceil(kl / full warps), and T is
+      // the lowest offer.  Each full warp then has q distinct columns >= T, so
+      // the slice has at least kl, and its top-kl by (value desc, column asc)
+      // are all among the columns >= T.
+      const int wfull = min(NW, ((n + 3) >> 2) >> 5);
+      const uint32_t q = wfull > 0 ? (kl + wfull - 1) / static_cast<uint32_t>(wfull) : 33u;
+      bool all = q > 32u;
+      float tv = -__int_as_float(0x7f800000);
+      if (!all) {
+        const float srt = warp_sort_desc(regs_max(x));
+        const float offer = __shfl_sync(0xffffffffu, srt, static_cast<int>(q) - 1);
+        if ((threadIdx.x & 31) == 0 && (threadIdx.x >> 5) < wfull) sh.offer[threadIdx.x >> 5] = offer;
+        __syncthreads();
+        tv = sh.offer[0];
+        for (int w = 1; w < wfull; ++w) tv = fminf(tv, sh.offer[w]);
+        all = !(tv > -__int_as_float(0x7f800000));
       }
-      uint32_t tot;
-      const uint32_t ex = block_excl_scan<uint32_t, NT>(mine, sh.ws32, &tot);
-      if (tot <= static_cast<uint32_t>(kSliceCap) && tot >= kl) {
-        uint32_t at = ex;
-        if (all) {
-          for_regs(x, n, [&](float v, int j) { out[at++] = dkey(v, static_cast<uint32_t>(g_lo + j)); });
-        } else {  // NaN placeholders beyond n never pass v >= tv
-#pragma unroll
-          for (int i = 0; i < kSplitChunks; ++i) {
-            const int j0 = 4 * (threadIdx.x + i * NT);
-            if (x[i].x >= tv) out[at++] = dkey(x[i].x, static_cast<uint32_t>(g_lo + j0));
-            if (x[i].y >= tv) out[at++] = dkey(x[i].y, static_cast<uint32_t>(g_lo + j0 + 1));
-            if (x[i].z >= tv) out[at++] = dkey(x[i].z, static_cast<uint32_t>(g_lo + j0 + 2));
-            if (x[i].w >= tv) out[at++] = dkey(x[i].w, static_cast<uint32_t>(g_lo + j0 + 3));
+      // Candidates in one pass: a shared counter hands out the slots (their
+      // order is immaterial: the merge selects by key).
+      if (all) {
+        if (n <= kSliceCap)
+          for_regs(x, n, [&](float v, int j) { out[atomicAdd(&sh.ncand, 1u)] = dkey(v, static_cast<uint32_t>(g_lo + j)); });
+      } else {  // NaN placeholders beyond n never pass v >= tv
+        auto take = [&](float v, int j) {
+          if (v >= tv) {
+            const uint32_t p = atomicAdd(&sh.ncand, 1u);
+            if (p < static_cast<uint32_t>(kSliceCap)) out[p] = dkey(v, static_cast<uint32_t>(g_lo + j));
           }
+        };
+#pragma unroll
+        for (int i = 0; i < kSplitChunks; ++i) {
+          const int j0 = 4 * (threadIdx.x + i * NT);
+          take(x[i].x, j0);
+          take(x[i].y, j0 + 1);
+          take(x[i].z, j0 + 2);
+          take(x[i].w, j0 + 3);
         }
+      }
+      __syncthreads();
+      const uint32_t tot = (all && n > kSliceCap) ? ~0u : sh.ncand;
+      if (tot <= static_cast<uint32_t>(kSliceCap)) {
         count = tot;
       } else {
         // more than kSliceCap candidates (ties, masked rows): exact top-kl
+        for (int b = threadIdx.x; b < kBinsS; b += NT) H[b] = 0;
+        __syncthreads();
+        if (threadIdx.x == 0) sh.ncand = 0;
         unsigned long long prefix;
         int shift;
         const int nbits = 32 + a.idxbits;
@@ -1304,23 +1343,23 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
     if (threadIdx.x == 0) a.slice_count[slot] = count;
   }
 
-  // publish; the last slice of the row to finish merges.  The block barrier
-  // orders every thread's partial-result stores before thread 0's fence and
-  // counter increment (the pattern of a grid-wide barrier).
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    sh.last = atomicAdd(&a.counters[row], 1u) == static_cast<unsigned>(C - 1);
-  }
-  __syncthreads();
-  if (!sh.last) return;
-  __threadfence();
+}
 
+// Per-row merge of the slices' partial results, launched after split_kernel
+// on the same stream (so it sees every slice's stores; nothing waits).
+template <int kMode>
+__global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const DevOpts o) {
+  const int C = a.cluster;
+  const int row = blockIdx.x;
+  extern __shared__ __align__(16) unsigned char smem[];
+  uint32_t* H = reinterpret_cast<uint32_t*>(smem);        // kBinsS counts / fp64 tail scratch
+  uint64_t* U = reinterpret_cast<uint64_t*>(H + kBinsS);  // kUnionCap keys
+  __shared__ Shared sh;
   if (kMode == kSplitGreedy) {
     if (threadIdx.x < 32) {
       unsigned long long m = kNoKey;
       for (int i = threadIdx.x; i < C; i += 32) {
-        const unsigned long long v = __ldcg(&a.slice_keys[static_cast<long long>(row) * C + i]);
+        const unsigned long long v = a.slice_keys[static_cast<long long>(row) * C + i];
         m = v < m ? v : m;
       }
       m = warp_min(m);
@@ -1329,12 +1368,10 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
         a.out_ids[row] = id;
         if (a.stats) write_stats(a.stats + row, 0.0, 0.0, 0.0, __longlong_as_double(0x7ff0000000000000ll),
                                  __longlong_as_double(0x7ff0000000000000ll), o.vocab, 1, id, 1);
-        a.counters[row] = 0;
       }
     }
     return;
   }
-
   const uint32_t k = kMode == kSplitEmit ? static_cast<uint32_t>(min(a.cand_k, a.ncols)) : static_cast<uint32_t>(o.k);
   __shared__ uint32_t soff[kMaxSlices + 1];
   const uint32_t ci = threadIdx.x < static_cast<unsigned>(C) ? __ldcg(&a.slice_count[static_cast<long long>(row) * C + threadIdx.x]) : 0u;
@@ -1350,21 +1387,68 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
   __syncthreads();
   const unsigned long long* base = a.slice_keys + static_cast<long long>(row) * C * kSliceCap;
   uint64_t* sel = reinterpret_cast<uint64_t*>(H) + 512;  // H bytes [4 KB, 8 KB); the tail uses [0, 4 KB)
-  if (utot <= static_cast<uint32_t>(kUnionCap)) {
-    for (int e = threadIdx.x; e < C * kSliceCap; e += NT) {
-      const int i = e / kSliceCap, j = e - i * kSliceCap;
-      if (j < static_cast<int>(scnt[i])) U[soff[i] + j] = __ldcg(base + e);
-    }
+  const bool in_smem = utot <= static_cast<uint32_t>(kUnionCap);
+  if (in_smem) {  // a slice publishes at most kSliceCap == NT keys
+    for (int i = 0; i < C; ++i)
+      if (threadIdx.x < scnt[i]) U[soff[i] + threadIdx.x] = __ldcg(base + static_cast<long long>(i) * kSliceCap + threadIdx.x);
     __syncthreads();
   }
-  uint64_t* cand = U;
-  uint32_t total = utot;
-  if (utot > 256u) {
-    // the k best of the union by radix selection, then sort only those
+  uint64_t* cand = sel + kSliceCap;  // the k best, sorted (sel[kSliceCap, 2 kSliceCap))
+  bool done = false;
+  if (in_smem) {
+    // The slices' bound once more, over the union: every full warp offers the
+    // q-th largest of its lanes' best values, and the lowest offer bounds the
+    // union's top-k from below.  Lanes own U[t], U[t + NT], ...
+    float bv = -__int_as_float(0x7f800000);
+    for (uint32_t e = threadIdx.x; e < utot; e += NT) bv = fmaxf(bv, dval(U[e]));
+    const int wfull = min(NW, static_cast<int>(utot >> 5));
+    const uint32_t q = wfull > 0 ? (k + wfull - 1) / static_cast<uint32_t>(wfull) : 33u;
+    bool all = q > 32u;
+    float tv = -__int_as_float(0x7f800000);
+    if (!all) {
+      const float srt = warp_sort_desc(bv);
+      const float offer = __shfl_sync(0xffffffffu, srt, static_cast<int>(q) - 1);
+      if ((threadIdx.x & 31) == 0 && (threadIdx.x >> 5) < wfull) sh.offer[threadIdx.x >> 5] = offer;
+      __syncthreads();
+      tv = sh.offer[0];
+      for (int w = 1; w < wfull; ++w) tv = fminf(tv, sh.offer[w]);
+      all = !(tv > -__int_as_float(0x7f800000));
+    }
+    const uint64_t* F = U;
+    uint32_t m = utot;
+    if (!all) {
+      for (uint32_t e = threadIdx.x; e < utot; e += NT) {
+        const uint64_t d = U[e];
+        if (dval(d) >= tv) {
+          const uint32_t p = atomicAdd(&sh.ncand, 1u);
+          if (p < static_cast<uint32_t>(kSliceCap)) sel[p] = d;
+        }
+      }
+      __syncthreads();
+      F = sel;
+      m = sh.ncand;
+    }
+    if (m <= static_cast<uint32_t>(NT)) {
+      // rank by counting: keys are distinct, so each of the k best lands at its place
+      if (threadIdx.x < m) {
+        const uint64_t d = F[threadIdx.x];
+        uint32_t r = 0;
+        for (uint32_t j = 0; j < m; ++j) r += F[j] < d ? 1u : 0u;
+        if (r < k) cand[r] = d;
+      }
+      __syncthreads();
+      done = true;
+    }
+  }
+  if (!done) {
+    // rare: the k best of the union by radix selection, then sort only those
     unsigned long long prefix;
     int shift;
     const int nbits = 32 + a.idxbits;
-    const bool in_smem = utot <= static_cast<uint32_t>(kUnionCap);
+    __syncthreads();  // everyone has read sh.ncand
+    for (int b = threadIdx.x; b < kBinsS; b += NT) H[b] = 0;
+    if (threadIdx.x == 0) sh.ncand = 0;
+    __syncthreads();
     auto each = [&](auto f) {
       if (in_smem) {
         for (int e = threadIdx.x; e < static_cast<int>(utot); e += NT) f(to_ckey(U[e], a.idxbits));
@@ -1379,7 +1463,7 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
     auto take = [&](unsigned long long d) {
       if ((to_ckey(d, a.idxbits) >> shift) <= prefix) {
         const uint32_t p = atomicAdd(&sh.ncand, 1u);
-        if (p < 512u) sel[p] = d;
+        if (p < static_cast<uint32_t>(kSliceCap)) sel[p] = d;
       }
     };
     if (in_smem) {
@@ -1391,13 +1475,13 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
       }
     }
     __syncthreads();
-    cand = sel;
-    total = k;
+    const int P = next_pow2(max(static_cast<int>(k), 2));
+    for (int i = static_cast<int>(k) + threadIdx.x; i < P; i += NT) sel[i] = kNoKey;
+    __syncthreads();
+    bitonic_sort_u64(sel, P);
+    for (int i = threadIdx.x; i < static_cast<int>(k); i += NT) cand[i] = sel[i];
+    __syncthreads();
   }
-  const int P = next_pow2(max(static_cast<int>(total), 2));
-  for (int i = static_cast<int>(total) + threadIdx.x; i < P; i += NT) cand[i] = kNoKey;
-  __syncthreads();
-  bitonic_sort_u64(cand, P);
   if (kMode == kSplitEmit) {
     for (int i = threadIdx.x; i < a.cand_k; i += NT) {
       const long long at = static_cast<long long>(row) * a.cand_k + i;
@@ -1410,29 +1494,31 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
     tail_pick(cand, static_cast<int>(k), o, a.rng + 2ll * row, a.out_ids + row, a.stats ? a.stats + row : nullptr, pr,
               pr + kSplitMaxK, &sh.tail);
   }
-  if (threadIdx.x == 0) a.counters[row] = 0;
 }
+
 
 }  // namespace split
 
-size_t split_scratch_bytes(long long rows, int slices, size_t* off_count, size_t* off_keys) {
-  auto up = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
-  const size_t counters = up(static_cast<size_t>(rows) * 4);
-  const size_t counts = up(static_cast<size_t>(rows) * slices * 4);
-  const size_t keys = static_cast<size_t>(rows) * slices * kSliceCap * 8;
-  *off_count = counters;
-  *off_keys = counters + counts;
-  return counters + counts + keys;
+size_t split_scratch_bytes(long long rows, int slices, size_t* off_keys) {
+  const size_t counts = (static_cast<size_t>(rows) * slices * 4 + 255) & ~static_cast<size_t>(255);
+  *off_keys = counts;
+  return counts + static_cast<size_t>(rows) * slices * kSliceCap * 8;
 }
-
 template <int kMode, bool kPen>
 static cudaError_t launch_split_t(const RowArgs& a, const DevOpts& o, cudaStream_t s) {
   const size_t bmb = static_cast<size_t>((a.slice >> 5) + 2) * 4;
-  const size_t sm = kMode == kSplitGreedy ? bmb : split::kBinsS * 4 + split::kUnionCap * 8 + bmb;
+  const size_t sm = kMode == kSplitGreedy ? bmb : split::kBinsS * 4 + bmb;
   split::split_kernel<kMode, kPen><<<a.rows * a.cluster, split::NT, sm, s>>>(a, o);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // the per-row merge runs after every slice of the batch (same stream)
+  if (kMode == kSplitGreedy) {
+    split::merge_slices_kernel<kMode><<<a.rows, 32, 0, s>>>(a, o);
+  } else {
+    split::merge_slices_kernel<kMode><<<a.rows, split::NT, split::kBinsS * 4 + split::kUnionCap * 8, s>>>(a, o);
+  }
   return cudaGetLastError();
 }
-
 cudaError_t launch_split(const RowArgs& a, const DevOpts& o, int mode, cudaStream_t s) {
   switch (mode * 2 + (o.penalize ? 1 : 0)) {
     case 0: return launch_split_t<kSplitGreedy, false>(a, o, s);
@@ -1475,20 +1561,17 @@ static cudaError_t noalloc_scratch_address(void** out) {
 }
 
 cudaError_t launch_split_noalloc(RowArgs& a, const DevOpts& o, int mode, cudaStream_t s, bool* too_big) {
-  size_t off_count = 0, off_keys = 0;
-  *too_big = split_scratch_bytes(a.rows, a.cluster, &off_count, &off_keys) > kNoAllocScratchBytes;
+  size_t off_keys = 0;
+  *too_big = split_scratch_bytes(a.rows, a.cluster, &off_keys) > kNoAllocScratchBytes;
   if (*too_big) return cudaSuccess;
   void* base = nullptr;
   cudaError_t e = noalloc_scratch_address(&base);
   if (e != cudaSuccess) return e;
-  a.counters = static_cast<unsigned*>(base);
-  a.slice_count = reinterpret_cast<unsigned*>(static_cast<char*>(base) + off_count);
+  // Nothing in the scratch has to start at zero: each slice writes its count
+  // and candidates before the merge kernel reads them, so the previous call's
+  // contents are simply overwritten.
+  a.slice_count = static_cast<unsigned*>(base);
   a.slice_keys = reinterpret_cast<unsigned long long*>(static_cast<char*>(base) + off_keys);
-  // The per-row counters must start at zero.  The kernel leaves them at zero,
-  // but the array also serves calls of other shapes, so clear them here.
-  e = cudaMemsetAsync(a.counters, 0, static_cast<size_t>(a.rows) * sizeof(unsigned), s);
-  if (e != cudaSuccess) return e;
   return launch_split(a, o, mode, s);
 }
-
 }  // namespace vb

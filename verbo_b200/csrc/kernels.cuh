@@ -46,13 +46,13 @@ struct RowArgs {
   int idxbits;  // bits of the largest global id
   int fixbits;  // fixed-point fraction bits of the staged kernel's masses
   // Scratch of the split-row kernels (global memory, see split_scratch_bytes):
-  unsigned* counters;              // [rows]: slices done; zero between launches
   unsigned* slice_count;           // [rows * cluster]: candidates each slice published
   unsigned long long* slice_keys;  // [rows * cluster * kSliceCap]: candidate keys (greedy: 1 per slice)
 };
 
 // Split-row kernels: one CTA of kSplitThreads per (row, slice of <= kSplitSlice
-// columns); the last CTA of a row to finish merges the slices' partial results.
+// columns) publishes a partial result; a per-row merge kernel follows on the
+// same stream.
 constexpr int kSplitThreads = 256;
 constexpr int kSplitChunks = 10;                                  // 16-byte chunks per thread, in registers
 constexpr int kSplitSlice = kSplitThreads * kSplitChunks * 4;     // 10240 columns
@@ -60,9 +60,9 @@ constexpr int kSliceCap = 256;                                    // candidates 
 constexpr int kSplitMaxK = kSliceCap;                             // largest top_k of the split top-k kernel
 constexpr int kMaxSlices = 32;
 
-// Bytes of split-kernel scratch for `rows` rows of `slices` slices, and the
-// offsets of its three parts (counters first; they must start zeroed).
-size_t split_scratch_bytes(long long rows, int slices, size_t* off_count, size_t* off_keys);
+// Bytes of split-kernel scratch for `rows` rows of `slices` slices (per-slice
+// counts at offset 0, candidate keys at *off_keys).  Nothing needs zeroing.
+size_t split_scratch_bytes(long long rows, int slices, size_t* off_keys);
 cudaError_t launch_split(const RowArgs& a, const DevOpts& o, int mode, cudaStream_t s);
 enum SplitMode { kSplitGreedy = 0, kSplitSample = 1, kSplitEmit = 2 };
 
