@@ -102,9 +102,9 @@ VERBO_CUDA_API int verbo_cuda_sample(const float* logits, int rows, int vocab, l
    synchronisation of cudaMalloc/cudaFree (verbo_cuda_sample allocates its
    scratch on first use per stream and grows it for larger batches).
    Its scratch is a fixed 8 MiB array inside the library, held by every device
-   that loads the library until the process exits: up to about 272 rows per
-   call at vocab 151936 (127 at the largest vocab, 327680); larger calls are
-   rejected with an error.  The first call on each device looks up the
+   that loads the library until the process exits: up to about 272 top-k rows
+   per call at vocab 151936 (127 at the largest vocab, 327680) and about
+   46,000 greedy rows; larger calls are rejected with an error.  The first call on each device looks up the
    array's address (cudaGetSymbolAddress); make that first call before any
    stream capture.  All calls share the array: calls that overlap on the GPU
    (concurrent streams or host threads) race and must be serialised by the

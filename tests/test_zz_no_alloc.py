@@ -74,12 +74,13 @@ def test_noalloc_rejects_sizes_beyond_the_scratch(vb):
     one = torch.zeros(1, device="cuda")
     ids = torch.zeros(1, dtype=torch.int32, device="cuda")
     lib = vb.load_library()
-    o = vb.Sampling(temp=0.0)._c()
-    rc = lib.verbo_cuda_sample_noalloc(one.data_ptr(), 4096, 151936, 151936, None, None, ctypes.byref(o), None,
-                                       ids.data_ptr(), None, None)
-    assert rc == -1
-    msg = lib.verbo_cuda_last_error().decode()
-    assert "fixed scratch" in msg and "rows at vocab 151936" in msg
+    # greedy keeps one key per item, top-k up to 256: their limits differ
+    for rows, o in ((100000, vb.Sampling(temp=0.0)._c()), (4096, vb.Sampling(temp=0.8, top_k=50)._c())):
+        rc = lib.verbo_cuda_sample_noalloc(one.data_ptr(), rows, 151936, 151936, None, None, ctypes.byref(o),
+                                           ids.data_ptr(), ids.data_ptr(), None, None)
+        assert rc == -1
+        msg = lib.verbo_cuda_last_error().decode()
+        assert "fixed scratch" in msg and "rows at vocab 151936" in msg
 
 
 def test_noalloc_rejects_options_outside_its_kernel(vb):

@@ -1044,11 +1044,12 @@ __device__ __forceinline__ void load_regs(const float* src, int n, float4 (&x)[k
   const bool vec = (reinterpret_cast<uintptr_t>(src) & 15) == 0;
   const float4* s4 = reinterpret_cast<const float4*>(src);
   const float nan = __int_as_float(0x7fc00000);
+  const int nfull = vec ? n / (4 * NT) : 0;  // chunks that are whole for every thread (block-uniform)
 #pragma unroll
   for (int i = 0; i < kSplitChunks; ++i) {
     const int q = threadIdx.x + i * NT;
     const int j0 = 4 * q;
-    if (vec && j0 + 3 < n) {
+    if (i < nfull || (vec && j0 + 3 < n)) {
       x[i] = ld_stream(s4 + q);
     } else {
       x[i].x = j0 < n ? ld_stream1(src + j0) : nan;
@@ -1059,18 +1060,28 @@ __device__ __forceinline__ void load_regs(const float* src, int n, float4 (&x)[k
   }
 }
 
-__device__ __forceinline__ void penalize_regs(float4 (&x)[kSplitChunks], const uint32_t* bm, float rep, int n) {
+// The penalty mask of a thread: bit 4*i + c stands for slice column
+// 4*(thread + i*NT) + c, the c-th value of the thread's chunk i.  One 64-bit
+// word per thread, so most threads (no penalised column) test one word.
+static_assert(4 * kSplitChunks <= 64, "penalty mask holds 4 bits per chunk");
+__device__ __forceinline__ void mask_set(unsigned long long* pm, int j) {
+  const int q = j >> 2;
+  atomicOr(&pm[q % NT], 1ull << (4 * (q / NT) + (j & 3)));
+}
+__device__ __forceinline__ bool mask_test(const unsigned long long* pm, int j) {
+  const int q = j >> 2;
+  return (pm[q % NT] >> (4 * (q / NT) + (j & 3))) & 1ull;
+}
+__device__ __forceinline__ void penalize_regs(float4 (&x)[kSplitChunks], unsigned long long m, float rep) {
+  if (m == 0) return;
 #pragma unroll
   for (int i = 0; i < kSplitChunks; ++i) {
-    const int j0 = 4 * (threadIdx.x + i * NT);
-    if (j0 < n) {
-      const uint32_t nib = (bm[j0 >> 5] >> (j0 & 31)) & 15u;
-      if (nib) {
-        if (nib & 1u) x[i].x = penalize(x[i].x, rep);
-        if (nib & 2u) x[i].y = penalize(x[i].y, rep);
-        if (nib & 4u) x[i].z = penalize(x[i].z, rep);
-        if (nib & 8u) x[i].w = penalize(x[i].w, rep);
-      }
+    const uint32_t nib = static_cast<uint32_t>(m >> (4 * i)) & 15u;
+    if (nib) {
+      if (nib & 1u) x[i].x = penalize(x[i].x, rep);
+      if (nib & 2u) x[i].y = penalize(x[i].y, rep);
+      if (nib & 4u) x[i].z = penalize(x[i].z, rep);
+      if (nib & 8u) x[i].w = penalize(x[i].w, rep);
     }
   }
 }
@@ -1233,27 +1244,27 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
   const float* src = a.logits + static_cast<long long>(row) * a.ld + lo;
   const long long g_lo = static_cast<long long>(a.col_off) + lo;
   extern __shared__ __align__(16) unsigned char smem[];
-  uint32_t* H = reinterpret_cast<uint32_t*>(smem);  // kBinsS counts (top-k modes, exact fallback)
-  uint32_t* bm = kMode == kSplitGreedy ? H : H + kBinsS;  // penalty bitmap of the slice
+  uint32_t* H = reinterpret_cast<uint32_t*>(smem);  // kBinsS counts (top-k exact fallback)
   __shared__ Shared sh;
+  __shared__ unsigned long long pm[kPen ? NT : 1];  // penalty masks, one per thread
 
   float4 x[kSplitChunks];
   load_regs(src, n, x);  // all loads in flight before anything else
   if (threadIdx.x == 0) sh.ncand = 0;
   if (kPen) {
-    const int nw = (a.slice >> 5) + 2;
-    for (int i = threadIdx.x; i < nw; i += NT) bm[i] = 0;
+    pm[threadIdx.x] = 0;
     __syncthreads();
+    // the last repeat_last ids of the row's history (src/sampler.cpp:58-64)
     const long long h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
     const long long len = h1 - h0;
     const long long from = (o.repeat_last > 0 && len > o.repeat_last) ? len - o.repeat_last : 0;
     for (long long j = h0 + from + threadIdx.x; j < h1; j += NT) {
       const long long t = static_cast<long long>(a.hist[j]) - g_lo;
-      if (t >= 0 && t < n) atomicOr(&bm[t >> 5], 1u << (t & 31));
+      if (t >= 0 && t < n) mask_set(pm, static_cast<int>(t));
     }
   }
   __syncthreads();
-  if (kPen) penalize_regs(x, bm, o.repeat, n);
+  if (kPen) penalize_regs(x, pm[threadIdx.x], o.repeat);
   const long long slot = static_cast<long long>(row) * C + s;
 
   if (kMode == kSplitGreedy) {
@@ -1323,7 +1334,7 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
         auto each_col = [&](auto f) {
           for (int j = threadIdx.x; j < n; j += NT) {
             float v = ld_stream1(src + j);
-            if (kPen && ((bm[j >> 5] >> (j & 31)) & 1u)) v = penalize(v, o.repeat);
+            if (kPen && mask_test(pm, j)) v = penalize(v, o.repeat);
             f(v, j);
           }
         };
@@ -1499,15 +1510,14 @@ __global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const
 
 }  // namespace split
 
-size_t split_scratch_bytes(long long rows, int slices, size_t* off_keys) {
+size_t split_scratch_bytes(long long rows, int slices, bool greedy, size_t* off_keys) {
   const size_t counts = (static_cast<size_t>(rows) * slices * 4 + 255) & ~static_cast<size_t>(255);
   *off_keys = counts;
-  return counts + static_cast<size_t>(rows) * slices * kSliceCap * 8;
+  return counts + static_cast<size_t>(rows) * slices * (greedy ? 1 : kSliceCap) * 8;
 }
 template <int kMode, bool kPen>
 static cudaError_t launch_split_t(const RowArgs& a, const DevOpts& o, cudaStream_t s) {
-  const size_t bmb = static_cast<size_t>((a.slice >> 5) + 2) * 4;
-  const size_t sm = kMode == kSplitGreedy ? bmb : split::kBinsS * 4 + bmb;
+  const size_t sm = kMode == kSplitGreedy ? 0 : split::kBinsS * 4;
   split::split_kernel<kMode, kPen><<<a.rows * a.cluster, split::NT, sm, s>>>(a, o);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -1562,7 +1572,7 @@ static cudaError_t noalloc_scratch_address(void** out) {
 
 cudaError_t launch_split_noalloc(RowArgs& a, const DevOpts& o, int mode, cudaStream_t s, bool* too_big) {
   size_t off_keys = 0;
-  *too_big = split_scratch_bytes(a.rows, a.cluster, &off_keys) > kNoAllocScratchBytes;
+  *too_big = split_scratch_bytes(a.rows, a.cluster, mode == kSplitGreedy, &off_keys) > kNoAllocScratchBytes;
   if (*too_big) return cudaSuccess;
   void* base = nullptr;
   cudaError_t e = noalloc_scratch_address(&base);

@@ -61,8 +61,9 @@ constexpr int kSplitMaxK = kSliceCap;                             // largest top
 constexpr int kMaxSlices = 32;
 
 // Bytes of split-kernel scratch for `rows` rows of `slices` slices (per-slice
-// counts at offset 0, candidate keys at *off_keys).  Nothing needs zeroing.
-size_t split_scratch_bytes(long long rows, int slices, size_t* off_keys);
+// counts at offset 0, keys at *off_keys: one per slice for greedy, kSliceCap
+// for top-k).  Nothing needs zeroing.
+size_t split_scratch_bytes(long long rows, int slices, bool greedy, size_t* off_keys);
 cudaError_t launch_split(const RowArgs& a, const DevOpts& o, int mode, cudaStream_t s);
 enum SplitMode { kSplitGreedy = 0, kSplitSample = 1, kSplitEmit = 2 };
 
