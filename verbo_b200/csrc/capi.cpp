@@ -128,11 +128,12 @@ struct Scratch {
 std::mutex g_scratch_mu;
 std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
 
-void attach_split_scratch(vb::RowArgs& a, bool greedy, cudaStream_t s) {
+void attach_split_scratch(vb::RowArgs& a, const vb::DevOpts& o, bool greedy, cudaStream_t s) {
   int dev = 0;
   cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
-  size_t off_keys = 0;
-  const size_t bytes = vb::split_scratch_bytes(a.rows, a.cluster, greedy, &off_keys);
+  const int win_w = vb::split_window_width(o);
+  const vb::SplitScratch l = vb::split_scratch_layout(a.rows, a.cluster, greedy, win_w);
+  const size_t bytes = l.bytes;
   std::lock_guard<std::mutex> lk(g_scratch_mu);
   Scratch& sc = g_scratch[{dev, s}];
   if (sc.bytes < bytes) {
@@ -144,8 +145,7 @@ void attach_split_scratch(vb::RowArgs& a, bool greedy, cudaStream_t s) {
     cuda_ok(cudaMalloc(&sc.data, n), "cudaMalloc scratch");
     sc.bytes = n;
   }
-  a.slice_count = static_cast<unsigned*>(sc.data);
-  a.slice_keys = reinterpret_cast<unsigned long long*>(static_cast<char*>(sc.data) + off_keys);
+  vb::split_scratch_attach(a, sc.data, l, win_w);
 }
 
 // Slices of the split-row kernels: the fewest slices of <= kSplitSlice columns.
@@ -178,7 +178,7 @@ int sample_impl(const float* logits, int rows, int vocab, long long ld, const in
   cudaError_t e;
   if (o.greedy || (o.k < vocab && o.k <= vb::kSplitMaxK)) {
     plan_split(a);
-    attach_split_scratch(a, o.greedy != 0, s);
+    attach_split_scratch(a, o, o.greedy != 0, s);
     e = vb::launch_split(a, o, o.greedy ? vb::kSplitGreedy : vb::kSplitSample, s);
   } else {
     e = vb::launch_general(a, o, s);
@@ -310,7 +310,8 @@ VERBO_CUDA_API int verbo_cuda_sample_noalloc(const float* logits, int rows, int 
                                          static_cast<cudaStream_t>(stream), &too_big),
                 "kernel launch");
         if (too_big) {
-          const long long per_row = 4ll * a.cluster + 8ll * a.cluster * (o.greedy ? 1 : vb::kSliceCap);
+          const long long per_row = 4ll * a.cluster + 8ll * a.cluster * (o.greedy ? 1 : vb::kSliceCap) +
+                                    4ll * vb::split_window_width(o);
           fail("rows x vocab exceed the fixed scratch of " + std::to_string(vb::kNoAllocScratchBytes >> 20) +
                " MiB: at most about " + std::to_string((vb::kNoAllocScratchBytes - 512) / per_row) +
                " rows at vocab " + std::to_string(vocab) + " per call");
@@ -342,7 +343,7 @@ VERBO_CUDA_API int verbo_cuda_shard_topk(const float* logits, int rows, int shar
         a.cand_id = cand_id;
         a.cand_k = k;
         plan_split(a);
-        attach_split_scratch(a, false, static_cast<cudaStream_t>(stream));
+        attach_split_scratch(a, o, false, static_cast<cudaStream_t>(stream));
         cuda_ok(vb::launch_split(a, o, vb::kSplitEmit, static_cast<cudaStream_t>(stream)), "kernel launch");
         return 0;
       },

@@ -110,6 +110,14 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
+// 16-byte asynchronous copy global -> shared (both 16-byte aligned), L1
+// bypassed; completion by cp_async_wait_all in the issuing thread.
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src_gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src_gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Streaming 16-byte load: read-only path, no L1 allocation, 256-byte L2 prefetch.
 __device__ __forceinline__ float4 ld_stream(const float4* p) {
   float4 v;

@@ -1234,6 +1234,39 @@ __device__ __forceinline__ unsigned long long to_ckey(unsigned long long d, int 
   return ((d >> 32) << idxbits) | (d & 0xffffffffull);
 }
 
+// The exact top-kl of a slice by radix selection, for slices whose bound
+// admits more than kSliceCap candidates (ties, masked rows).  Rare, so it
+// re-reads the slice from L2 and stays out of line: the caller's register
+// copy of the slice is dead by then and its budget is not shared.
+template <bool kPen>
+__device__ __noinline__ void slice_exact_topk(const RowArgs& a, const DevOpts& o, const float* src, int n,
+                                              long long g_lo, uint32_t kl, const unsigned long long* pm,
+                                              uint32_t* H, Shared& sh, unsigned long long* out) {
+  for (int b = threadIdx.x; b < kBinsS; b += NT) H[b] = 0;
+  __syncthreads();
+  if (threadIdx.x == 0) sh.ncand = 0;
+  unsigned long long prefix;
+  int shift;
+  const int nbits = 32 + a.idxbits;
+  auto each_col = [&](auto f) {
+    for (int j = threadIdx.x; j < n; j += NT) {
+      float v = ld_stream1(src + j);
+      if (kPen && mask_test(pm, j)) v = penalize(v, o.repeat);
+      f(v, j);
+    }
+  };
+  radix_select(
+      [&](auto f) { each_col([&](float v, int j) { f(ckey(v, static_cast<uint32_t>(g_lo + j), a.idxbits)); }); },
+      kl, nbits, H, sh, &prefix, &shift);
+  each_col([&](float v, int j) {
+    const uint32_t gid = static_cast<uint32_t>(g_lo + j);
+    if ((ckey(v, gid, a.idxbits) >> shift) <= prefix) {
+      const uint32_t p = atomicAdd(&sh.ncand, 1u);
+      if (p < static_cast<uint32_t>(kSliceCap)) out[p] = dkey(v, gid);
+    }
+  });
+}
+
 template <int kMode, bool kPen>
 __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const DevOpts o) {
   const int C = a.cluster;
@@ -1245,22 +1278,38 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
   const long long g_lo = static_cast<long long>(a.col_off) + lo;
   extern __shared__ __align__(16) unsigned char smem[];
   uint32_t* H = reinterpret_cast<uint32_t*>(smem);  // kBinsS counts (top-k exact fallback)
+  int* wids = reinterpret_cast<int*>(smem + (kMode == kSplitGreedy ? 0 : kBinsS * 4));  // the row's window
   __shared__ Shared sh;
   __shared__ unsigned long long pm[kPen ? NT : 1];  // penalty masks, one per thread
 
+  // A dense window goes out before the logits, so it is back when they are.
+  if (kPen && a.win_w > 0) {
+    const int* g = a.win + static_cast<long long>(row) * a.win_w;
+    for (int c = threadIdx.x; c < (a.win_w >> 2); c += NT) cp_async16(wids + 4 * c, g + 4 * c);
+    cp_async_commit();
+  }
   float4 x[kSplitChunks];
-  load_regs(src, n, x);  // all loads in flight before anything else
+  load_regs(src, n, x);  // all logits loads in flight before anything else
   if (threadIdx.x == 0) sh.ncand = 0;
   if (kPen) {
     pm[threadIdx.x] = 0;
+    if (a.win_w > 0) cp_async_wait_all();
     __syncthreads();
-    // the last repeat_last ids of the row's history (src/sampler.cpp:58-64)
-    const long long h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
-    const long long len = h1 - h0;
-    const long long from = (o.repeat_last > 0 && len > o.repeat_last) ? len - o.repeat_last : 0;
-    for (long long j = h0 + from + threadIdx.x; j < h1; j += NT) {
-      const long long t = static_cast<long long>(a.hist[j]) - g_lo;
-      if (t >= 0 && t < n) mask_set(pm, static_cast<int>(t));
+    // the last repeat_last ids of the row's history (src/sampler.cpp:58-64);
+    // ids outside [0, vocab) and the -1 padding mark nothing
+    if (a.win_w > 0) {
+      for (int j = threadIdx.x; j < a.win_w; j += NT) {
+        const long long t = static_cast<long long>(wids[j]) - g_lo;
+        if (wids[j] >= 0 && t >= 0 && t < n) mask_set(pm, static_cast<int>(t));
+      }
+    } else {
+      const long long h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
+      const long long len = h1 - h0;
+      const long long from = (o.repeat_last > 0 && len > o.repeat_last) ? len - o.repeat_last : 0;
+      for (long long j = h0 + from + threadIdx.x; j < h1; j += NT) {
+        const long long t = static_cast<long long>(a.hist[j]) - g_lo;
+        if (t >= 0 && t < n) mask_set(pm, static_cast<int>(t));
+      }
     }
   }
   __syncthreads();
@@ -1324,30 +1373,7 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
         count = tot;
       } else {
         // more than kSliceCap candidates (ties, masked rows): exact top-kl
-        for (int b = threadIdx.x; b < kBinsS; b += NT) H[b] = 0;
-        __syncthreads();
-        if (threadIdx.x == 0) sh.ncand = 0;
-        unsigned long long prefix;
-        int shift;
-        const int nbits = 32 + a.idxbits;
-        // (rare path: re-read the slice from L2 so the register copy can die)
-        auto each_col = [&](auto f) {
-          for (int j = threadIdx.x; j < n; j += NT) {
-            float v = ld_stream1(src + j);
-            if (kPen && mask_test(pm, j)) v = penalize(v, o.repeat);
-            f(v, j);
-          }
-        };
-        radix_select(
-            [&](auto f) { each_col([&](float v, int j) { f(ckey(v, static_cast<uint32_t>(g_lo + j), a.idxbits)); }); },
-            kl, nbits, H, sh, &prefix, &shift);
-        each_col([&](float v, int j) {
-          const uint32_t gid = static_cast<uint32_t>(g_lo + j);
-          if ((ckey(v, gid, a.idxbits) >> shift) <= prefix) {
-            const uint32_t p = atomicAdd(&sh.ncand, 1u);
-            if (p < static_cast<uint32_t>(kSliceCap)) out[p] = dkey(v, gid);
-          }
-        });
+        slice_exact_topk<kPen>(a, o, src, n, g_lo, kl, pm, H, sh, out);
         count = kl;
       }
     }
@@ -1510,16 +1536,50 @@ __global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const
 
 }  // namespace split
 
-size_t split_scratch_bytes(long long rows, int slices, bool greedy, size_t* off_keys) {
-  const size_t counts = (static_cast<size_t>(rows) * slices * 4 + 255) & ~static_cast<size_t>(255);
-  *off_keys = counts;
-  return counts + static_cast<size_t>(rows) * slices * (greedy ? 1 : kSliceCap) * 8;
+static size_t round256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+SplitScratch split_scratch_layout(long long rows, int slices, bool greedy, int win_w) {
+  SplitScratch l;
+  l.off_keys = round256(static_cast<size_t>(rows) * slices * 4);
+  l.off_win = l.off_keys + round256(static_cast<size_t>(rows) * slices * (greedy ? 1 : kSliceCap) * 8);
+  l.bytes = l.off_win + static_cast<size_t>(rows) * win_w * 4;
+  return l;
 }
+void split_scratch_attach(RowArgs& a, void* base, const SplitScratch& l, int win_w) {
+  char* b = static_cast<char*>(base);
+  a.slice_count = reinterpret_cast<unsigned*>(b);
+  a.slice_keys = reinterpret_cast<unsigned long long*>(b + l.off_keys);
+  a.win = win_w > 0 ? reinterpret_cast<int*>(b + l.off_win) : nullptr;
+  a.win_w = win_w;
+}
+int split_window_width(const DevOpts& o) {
+  if (!o.penalize || o.repeat_last <= 0 || o.repeat_last > kWinMax) return 0;
+  return (o.repeat_last + 3) & ~3;
+}
+namespace split {
+// Copies each row's penalty window (its last repeat_last history ids,
+// src/sampler.cpp:58-64) into win[row][0, win_w), padded with -1.
+__global__ void __launch_bounds__(256) window_kernel(const RowArgs a, const DevOpts o) {
+  const int row = blockIdx.x;
+  const long long h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
+  const long long len = h1 - h0;
+  const long long from = (o.repeat_last > 0 && len > o.repeat_last) ? len - o.repeat_last : 0;
+  const long long st = h0 + from, wl = len - from;  // wl <= repeat_last <= win_w
+  int* d = a.win + static_cast<long long>(row) * a.win_w;
+  for (int j = threadIdx.x; j < a.win_w; j += 256) d[j] = j < wl ? a.hist[st + j] : -1;
+}
+}  // namespace split
+
 template <int kMode, bool kPen>
 static cudaError_t launch_split_t(const RowArgs& a, const DevOpts& o, cudaStream_t s) {
-  const size_t sm = kMode == kSplitGreedy ? 0 : split::kBinsS * 4;
+  cudaError_t e;
+  if (kPen && a.win_w > 0) {
+    split::window_kernel<<<a.rows, 256, 0, s>>>(a, o);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  const size_t sm = (kMode == kSplitGreedy ? 0 : split::kBinsS * 4) + (kPen && a.win_w > 0 ? a.win_w * 4 : 0);
   split::split_kernel<kMode, kPen><<<a.rows * a.cluster, split::NT, sm, s>>>(a, o);
-  cudaError_t e = cudaGetLastError();
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // the per-row merge runs after every slice of the batch (same stream)
   if (kMode == kSplitGreedy) {
@@ -1571,17 +1631,17 @@ static cudaError_t noalloc_scratch_address(void** out) {
 }
 
 cudaError_t launch_split_noalloc(RowArgs& a, const DevOpts& o, int mode, cudaStream_t s, bool* too_big) {
-  size_t off_keys = 0;
-  *too_big = split_scratch_bytes(a.rows, a.cluster, mode == kSplitGreedy, &off_keys) > kNoAllocScratchBytes;
+  const int win_w = split_window_width(o);
+  const SplitScratch l = split_scratch_layout(a.rows, a.cluster, mode == kSplitGreedy, win_w);
+  *too_big = l.bytes > kNoAllocScratchBytes;
   if (*too_big) return cudaSuccess;
   void* base = nullptr;
   cudaError_t e = noalloc_scratch_address(&base);
   if (e != cudaSuccess) return e;
-  // Nothing in the scratch has to start at zero: each slice writes its count
-  // and candidates before the merge kernel reads them, so the previous call's
-  // contents are simply overwritten.
-  a.slice_count = static_cast<unsigned*>(base);
-  a.slice_keys = reinterpret_cast<unsigned long long*>(static_cast<char*>(base) + off_keys);
+  // Nothing in the scratch has to start at zero: the window kernel and each
+  // slice write what the later kernels of the same call read, so the previous
+  // call's contents are simply overwritten.
+  split_scratch_attach(a, base, l, win_w);
   return launch_split(a, o, mode, s);
 }
 }  // namespace vb

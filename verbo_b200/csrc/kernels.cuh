@@ -45,9 +45,11 @@ struct RowArgs {
   int slice;    // columns per CTA (multiple of 4)
   int idxbits;  // bits of the largest global id
   int fixbits;  // fixed-point fraction bits of the staged kernel's masses
-  // Scratch of the split-row kernels (global memory, see split_scratch_bytes):
+  // Scratch of the split-row kernels (global memory, see split_scratch_layout):
   unsigned* slice_count;           // [rows * cluster]: candidates each slice published
   unsigned long long* slice_keys;  // [rows * cluster * kSliceCap]: candidate keys (greedy: 1 per slice)
+  int* win;                        // [rows][win_w]: dense penalty windows, -1 padded (win_w > 0)
+  int win_w;
 };
 
 // Split-row kernels: one CTA of kSplitThreads per (row, slice of <= kSplitSlice
@@ -60,10 +62,21 @@ constexpr int kSliceCap = 256;                                    // candidates 
 constexpr int kSplitMaxK = kSliceCap;                             // largest top_k of the split top-k kernel
 constexpr int kMaxSlices = 32;
 
-// Bytes of split-kernel scratch for `rows` rows of `slices` slices (per-slice
-// counts at offset 0, keys at *off_keys: one per slice for greedy, kSliceCap
-// for top-k).  Nothing needs zeroing.
-size_t split_scratch_bytes(long long rows, int slices, bool greedy, size_t* off_keys);
+// Dense penalty windows: when every row's window (its last repeat_last ids)
+// is at most kWinMax long, a small kernel copies the windows into
+// [rows][win_w] ahead of the split kernel, whose CTAs then fetch their row's
+// window before their logits instead of after them.
+constexpr int kWinMax = 2048;
+int split_window_width(const DevOpts& o);  // 0: the kernels read the CSR histories directly
+
+// Layout of the split kernels' scratch (nothing in it needs zeroing): per-slice
+// counts at offset 0, keys at off_keys (one per slice for greedy, kSliceCap
+// for top-k), windows at off_win.
+struct SplitScratch {
+  size_t off_keys, off_win, bytes;
+};
+SplitScratch split_scratch_layout(long long rows, int slices, bool greedy, int win_w);
+void split_scratch_attach(RowArgs& a, void* base, const SplitScratch& l, int win_w);
 cudaError_t launch_split(const RowArgs& a, const DevOpts& o, int mode, cudaStream_t s);
 enum SplitMode { kSplitGreedy = 0, kSplitSample = 1, kSplitEmit = 2 };
 
