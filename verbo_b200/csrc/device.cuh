@@ -57,6 +57,14 @@ __device__ __forceinline__ void cluster_sync_all() {
   cluster_wait();
 }
 
+// ------------------------------------- programmatic dependent launch ------
+// Without the launch attribute both are no-ops.  grid_wait blocks until the
+// grids this one depends on have completed and their writes are visible (they
+// contain no waits of their own); grid_release lets the dependent grid be
+// scheduled before this one finishes.
+__device__ __forceinline__ void grid_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------ timers ------
 __device__ __forceinline__ uint64_t gtimer() {
   uint64_t t;

@@ -26,6 +26,7 @@
 //                   whose bins are too crowded.  No full sort.
 //   merge_kernel    merges per-shard candidates and runs the same tail.
 #include <mutex>
+#include <utility>
 
 #include "device.cuh"
 #include "kernels.cuh"
@@ -1282,14 +1283,32 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
   __shared__ Shared sh;
   __shared__ unsigned long long pm[kPen ? NT : 1];  // penalty masks, one per thread
 
-  // A dense window goes out before the logits, so it is back when they are.
-  if (kPen && a.win_w > 0) {
+  // The merge grid may be scheduled once every CTA of this grid has started
+  // or finished: released by the last wave only, so that its CTAs fill slots
+  // no split CTA is waiting for.
+  if (static_cast<int>(blockIdx.x) + a.first_wave >= static_cast<int>(gridDim.x)) grid_release();
+  // The dense windows come from window_kernel, which this grid may overlap
+  // (programmatic launch).  CTAs of the first wave put their logits loads in
+  // flight first and then wait for it; later CTAs find it finished and send
+  // the window out before the logits, so it is back when they are.
+  float4 x[kSplitChunks];
+  auto fetch_window = [&]() {
+    grid_wait();
     const int* g = a.win + static_cast<long long>(row) * a.win_w;
     for (int c = threadIdx.x; c < (a.win_w >> 2); c += NT) cp_async16(wids + 4 * c, g + 4 * c);
     cp_async_commit();
+  };
+  if (kPen && a.win_w > 0) {
+    if (static_cast<int>(blockIdx.x) < a.first_wave) {
+      load_regs(src, n, x);
+      fetch_window();
+    } else {
+      fetch_window();
+      load_regs(src, n, x);
+    }
+  } else {
+    load_regs(src, n, x);  // all logits loads in flight before anything else
   }
-  float4 x[kSplitChunks];
-  load_regs(src, n, x);  // all logits loads in flight before anything else
   if (threadIdx.x == 0) sh.ncand = 0;
   if (kPen) {
     pm[threadIdx.x] = 0;
@@ -1392,6 +1411,7 @@ __global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const
   uint32_t* H = reinterpret_cast<uint32_t*>(smem);        // kBinsS counts / fp64 tail scratch
   uint64_t* U = reinterpret_cast<uint64_t*>(H + kBinsS);  // kUnionCap keys
   __shared__ Shared sh;
+  grid_wait();  // the split grid's partials (programmatic launch)
   if (kMode == kSplitGreedy) {
     if (threadIdx.x < 32) {
       unsigned long long m = kNoKey;
@@ -1559,6 +1579,7 @@ namespace split {
 // Copies each row's penalty window (its last repeat_last history ids,
 // src/sampler.cpp:58-64) into win[row][0, win_w), padded with -1.
 __global__ void __launch_bounds__(256) window_kernel(const RowArgs a, const DevOpts o) {
+  grid_release();  // the split grid may start its logits loads meanwhile
   const int row = blockIdx.x;
   const long long h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
   const long long len = h1 - h0;
@@ -1569,25 +1590,70 @@ __global__ void __launch_bounds__(256) window_kernel(const RowArgs a, const DevO
 }
 }  // namespace split
 
+// CTAs of the split kernel resident at once (SM count x CTAs per SM), looked
+// up once per device and instantiation.
 template <int kMode, bool kPen>
-static cudaError_t launch_split_t(const RowArgs& a, const DevOpts& o, cudaStream_t s) {
-  cudaError_t e;
-  if (kPen && a.win_w > 0) {
+static cudaError_t split_first_wave(size_t smem, int* out) {
+  static std::mutex mu;
+  static int cache[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!cache[dev]) {
+    int sms = 0, occ = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, split::split_kernel<kMode, kPen>, split::NT, smem);
+    if (e != cudaSuccess) return e;
+    cache[dev] = sms * (occ > 0 ? occ : 1);
+  }
+  *out = cache[dev];
+  return cudaSuccess;
+}
+
+// Launch with programmatic stream serialisation: the kernel may start while
+// the previous kernel on the stream (one of ours, released by it) still runs,
+// and waits for it with grid_wait where it needs its results.
+template <class... P, class... A>
+static cudaError_t launch_after(void (*k)(P...), int grid, int block, size_t smem, cudaStream_t s, A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...);
+}
+
+template <int kMode, bool kPen>
+static cudaError_t launch_split_t(const RowArgs& a0, const DevOpts& o, cudaStream_t s) {
+  RowArgs a = a0;
+  const bool windows = kPen && a.win_w > 0;
+  const size_t sm = (kMode == kSplitGreedy ? 0 : split::kBinsS * 4) + (windows ? a.win_w * 4 : 0);
+  cudaError_t e = split_first_wave<kMode, kPen>(sm, &a.first_wave);
+  if (e != cudaSuccess) return e;
+  const int grid = a.rows * a.cluster;
+  if (windows) {
+    // launched normally: it starts after everything before it on the stream
     split::window_kernel<<<a.rows, 256, 0, s>>>(a, o);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    e = launch_after(split::split_kernel<kMode, kPen>, grid, split::NT, sm, s, a, o);
+  } else {
+    split::split_kernel<kMode, kPen><<<grid, split::NT, sm, s>>>(a, o);
+    e = cudaGetLastError();
   }
-  const size_t sm = (kMode == kSplitGreedy ? 0 : split::kBinsS * 4) + (kPen && a.win_w > 0 ? a.win_w * 4 : 0);
-  split::split_kernel<kMode, kPen><<<a.rows * a.cluster, split::NT, sm, s>>>(a, o);
-  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // the per-row merge runs after every slice of the batch (same stream)
-  if (kMode == kSplitGreedy) {
-    split::merge_slices_kernel<kMode><<<a.rows, 32, 0, s>>>(a, o);
-  } else {
-    split::merge_slices_kernel<kMode><<<a.rows, split::NT, split::kBinsS * 4 + split::kUnionCap * 8, s>>>(a, o);
-  }
-  return cudaGetLastError();
+  if (kMode == kSplitGreedy) return launch_after(split::merge_slices_kernel<kMode>, a.rows, 32, 0, s, a, o);
+  return launch_after(split::merge_slices_kernel<kMode>, a.rows, split::NT,
+                      static_cast<size_t>(split::kBinsS * 4 + split::kUnionCap * 8), s, a, o);
 }
 cudaError_t launch_split(const RowArgs& a, const DevOpts& o, int mode, cudaStream_t s) {
   switch (mode * 2 + (o.penalize ? 1 : 0)) {

@@ -50,6 +50,7 @@ struct RowArgs {
   unsigned long long* slice_keys;  // [rows * cluster * kSliceCap]: candidate keys (greedy: 1 per slice)
   int* win;                        // [rows][win_w]: dense penalty windows, -1 padded (win_w > 0)
   int win_w;
+  int first_wave;  // split kernel: CTAs resident at launch (SMs x CTAs per SM), set by the launcher
 };
 
 // Split-row kernels: one CTA of kSplitThreads per (row, slice of <= kSplitSlice
