@@ -265,6 +265,27 @@ def test_crowded_bins_use_exact_fallback():
         np.testing.assert_allclose(st["sum"], ost[:, -1]["sum"], rtol=1e-9)
 
 
+@pytest.mark.parametrize("temp", [0.05, 0.4, 1.0, 1.5, 6.0])
+def test_full_vocab_weights_match_reference_sums(temp):
+    # The full-vocabulary kernel computes exp((v - M) / temp) with its own
+    # table-driven exponential and sums fixed-point masses; the reference sums
+    # glibc exp() values one by one in sorted order, whose own rounding is
+    # bounded by about N * eps = 151936 * 2^-53 = 1.7e-11 relative.  The
+    # normalisers agree within 5e-11 across exponent ranges from nearly
+    # all-underflow (temp 0.05 over N(0, 3^2)) to a narrow band (temp 6); an
+    # error in the exponential would show at 1e-3, not 1e-11.  Sampled ids
+    # agree away from boundaries.
+    g = np.random.default_rng(int(temp * 100))
+    V = 151936
+    x = np.stack([g.standard_normal(V) * 3, g.standard_normal(V) * 0.5, g.uniform(-20, 0, V)]).astype(np.float32)
+    seeds = np.arange(3, dtype=np.uint64) + np.uint64(4000 + int(temp * 100))
+    for opts in (dict(temp=temp, top_k=0, top_p=0.99), dict(temp=temp, top_k=0, top_p=1.0, min_p=0.01)):
+        ids, st, _ = run_gpu(x, opts, seeds, steps=2)
+        ora, ost, _ = run_oracle(x, opts, seeds, steps=2)
+        compare(ids, ora, ost, f"temp={temp} {opts}")
+        np.testing.assert_allclose(st["sum"], ost[:, -1]["sum"], rtol=5e-11)
+
+
 @pytest.mark.parametrize("k", [1, 2, 31, 33, 50, 64, 128, 255, 256])
 def test_split_topk_bounds(k):
     # The split top-k kernels bound each slice (and then the union) by the

@@ -348,7 +348,10 @@ struct GenCtx {
   int idxbits, nbits;
   float M;
   double inv_temp;
-  double fscale;  // 2^fixbits
+  int fixbits;      // F: masses are round(w * 2^F)
+  double xcut;      // exponents below it give a fixed-point mass of 0
+  bool need_w;      // min-p compares the weights themselves
+  const double* T;  // T[j] = 2^(j/256), j < 256 (shared memory)
   int C, crank;
   unsigned long long kc0;  // key of the row's first element in sorted order (always kept by min-p)
 };
@@ -359,10 +362,31 @@ __device__ __forceinline__ bool in_pset(const GenCtx& x, double m, double thr, u
   return !(thr > 0.0) || m >= thr || kc == x.kc0;
 }
 
+// The weight w = exp((double)(v - M) / temp) of src/sampler.cpp:79-85 (with
+// the division taken as a product by 1/temp) and its fixed-point mass
+// round(w * 2^F).  The exponential is table driven, after P. T. P. Tang,
+// "Table-driven implementation of the exponential function in IEEE
+// floating-point arithmetic", ACM TOMS 15(2), 1989: x = (256 e + j) ln2/256 + r
+// with |r| <= ln2/512, exp(x) = 2^e * 2^(j/256) * p(r), p the degree-4 Taylor
+// polynomial (truncation below 4e-17 relative), ln2/256 split so that k * hi
+// is exact.  Within a few ulp of a correctly rounded exp (tested against
+// CUDA's), so sums and decisions differ from the reference's only next to a
+// boundary.  Exponents below xcut (w * 2^F < 1/2) give mass 0.
 __device__ __forceinline__ unsigned long long fixed_mass(const GenCtx& x, float v, double* m_out) {
-  const double m = exp(static_cast<double>(__fsub_rn(canon(v), x.M)) * x.inv_temp);
-  *m_out = m;
-  return __double2ull_rn(m * x.fscale);
+  const double xx = static_cast<double>(__fsub_rn(canon(v), x.M)) * x.inv_temp;  // <= 0, -inf for NaN/-inf
+  if (!(xx >= x.xcut)) {
+    *m_out = x.need_w ? exp(xx) : 0.0;  // min-p may still compare tiny weights
+    return 0ull;
+  }
+  const int k = __double2int_rn(xx * 369.3299304675746);  // 256 / ln2
+  const double kd = static_cast<double>(k);
+  double r = fma(-kd, 0x1.62e42ff000000p-9, xx);  // ln2/256, high part (exact product)
+  r = fma(-kd, -0x1.718432a1b0e26p-43, r);        // low part
+  const double p = fma(fma(fma(fma(r, 1.0 / 24.0, 1.0 / 6.0), r, 0.5), r, 1.0), r, 1.0);
+  const double y = x.T[k & 255] * p;  // in [0.9986, 1.9973]
+  const int e = k >> 8;               // floor(k / 256) >= -(F + 2)
+  *m_out = y * __longlong_as_double(static_cast<long long>(1023 + e) << 52);
+  return __double2ull_rn(y * __longlong_as_double(static_cast<long long>(1023 + x.fixbits + e) << 52));
 }
 
 // Mass- or count-weighted selection: the first element, in the reference's
@@ -491,7 +515,9 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
   Hist* G = L + 1;   // two buffers
   // L[0..3]: radix histograms of the exact selection; the value path reuses the same bytes
   Gath* gb = reinterpret_cast<Gath*>(L + 4);  // two buffers
+  double* etab = reinterpret_cast<double*>(gb + 2);  // 2^(j/256), the exponential's table
   __shared__ GenShared sh;
+  for (int j = threadIdx.x; j < 256; j += kThreads) etab[j] = exp2(j * (1.0 / 256.0));
 
   cluster_arrive();
   // ---- stage the slice: bulk async copy of the 16-byte aligned body
@@ -555,14 +581,21 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
     __syncthreads();
   }
   // ---- row maximum (smallest key) across the cluster
-  uint64_t best = kNoKey;
+  // (float compares: `vj > bv` keeps the lowest column on ties and never
+  // takes a NaN; a thread whose columns are all -inf/NaN keeps its first)
+  float bv = -__int_as_float(0x7f800000);
+  int bj = -1;
   float lo_f = __int_as_float(0x7f800000);  // smallest finite value
   for (int j = threadIdx.x; j < n; j += kThreads) {
     const float vj = v[j];
-    const uint64_t d = dkey(vj, static_cast<uint32_t>(g_lo + j));
-    best = d < best ? d : best;
-    if (isfinite(vj)) lo_f = fminf(lo_f, vj);
+    if (vj > bv) {
+      bv = vj;
+      bj = j;
+    }
+    if (vj > -__int_as_float(0x7f800000)) lo_f = fminf(lo_f, vj);  // NaN and -inf fail; +inf kept
   }
+  if (bj < 0 && static_cast<int>(threadIdx.x) < n) bj = threadIdx.x;
+  uint64_t best = bj >= 0 ? dkey(bv, static_cast<uint32_t>(g_lo + bj)) : kNoKey;
   best = block_min<unsigned long long>(best, sh.ws64);
   lo_f = block_min<float>(lo_f, reinterpret_cast<float*>(sh.ws64));
   cluster_wait();
@@ -590,7 +623,10 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
   x.nbits = 32 + a.idxbits;
   x.M = dval(dmin);
   x.inv_temp = o.inv_temp;
-  x.fscale = ldexp(1.0, a.fixbits);
+  x.fixbits = a.fixbits;
+  x.xcut = -(a.fixbits + 1) * 0.6931471805599453;
+  x.need_w = o.min_p > 0.0f;
+  x.T = etab;
   x.C = C;
   x.crank = crank;
   x.kc0 = ((dmin >> 32) << a.idxbits) | (dmin & 0xffffffffull);
@@ -640,21 +676,38 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
     };
     // ---- mass pass: S over the k-set; (mass, count) of the min-p set per value bin
     unsigned long long s_local = 0, z_local = 0;
-    for (int j = threadIdx.x; j < n; j += kThreads) {
-      const float vv = v[j];
-      const unsigned long long kc = ckey(vv, static_cast<uint32_t>(g_lo + j), a.idxbits);
-      if (kc > klim) continue;
-      double m;
-      const unsigned long long qm = fixed_mass(x, vv, &m);
-      s_local += qm;
-      if (!in_pset(x, m, thr, kc)) continue;
-      if (qm == 0) {  // below the fixed-point resolution: counted, never drawn
-        ++z_local;
-        continue;
+    if (klim == kAll && !(thr > 0.0)) {
+      // every column is in the k-set and the min-p set: no keys needed
+      for (int j = threadIdx.x; j < n; j += kThreads) {
+        const float vv = v[j];
+        double m;
+        const unsigned long long qm = fixed_mass(x, vv, &m);
+        if (qm == 0) {  // below the fixed-point resolution: counted, never drawn
+          ++z_local;
+          continue;
+        }
+        s_local += qm;
+        const int bi = vbin(vv);
+        atomicAdd(&Lv->c[bi], 1u);
+        atomicAdd(&Lv->m[bi], qm);
       }
-      const int bi = vbin(vv);
-      atomicAdd(&Lv->c[bi], 1u);
-      atomicAdd(&Lv->m[bi], qm);
+    } else {
+      for (int j = threadIdx.x; j < n; j += kThreads) {
+        const float vv = v[j];
+        const unsigned long long kc = ckey(vv, static_cast<uint32_t>(g_lo + j), a.idxbits);
+        if (kc > klim) continue;
+        double m;
+        const unsigned long long qm = fixed_mass(x, vv, &m);
+        s_local += qm;
+        if (!in_pset(x, m, thr, kc)) continue;
+        if (qm == 0) {  // below the fixed-point resolution: counted, never drawn
+          ++z_local;
+          continue;
+        }
+        const int bi = vbin(vv);
+        atomicAdd(&Lv->c[bi], 1u);
+        atomicAdd(&Lv->m[bi], qm);
+      }
     }
     s_local = block_sum(s_local, sh.ws64);
     z_local = block_sum(z_local, sh.ws64);
@@ -937,8 +990,8 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
         if (threadIdx.x == 0 && crank == 0) raise_status(kErrSelect);
       }
     }
-    s_sum = static_cast<double>(S) / x.fscale;
-    s_tot = static_cast<double>(tot_m) / x.fscale;
+    s_sum = ldexp(static_cast<double>(S), -x.fixbits);
+    s_tot = ldexp(static_cast<double>(tot_m), -x.fixbits);
     s_keep = static_cast<int>(keep_c);
   }
   if (crank == 0 && threadIdx.x == 0) {
@@ -957,7 +1010,7 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
 size_t general_smem(int slice) {
   const size_t vwords = static_cast<size_t>(((slice + 4 + 3) / 4) * 4);
   const size_t bwords = static_cast<size_t>(((((slice >> 5) + 2) + 3) / 4) * 4);
-  return (vwords + bwords) * 4 + 4 * sizeof(Hist) + 2 * sizeof(Gath);
+  return (vwords + bwords) * 4 + 4 * sizeof(Hist) + 2 * sizeof(Gath) + 256 * sizeof(double);
 }
 static int next_pow2_host(int x) {
   int p = 1;
