@@ -157,6 +157,34 @@ VERBO_CUDA_API int verbo_cuda_sampler_reset(verbo_cuda_sampler* s);
 /* Sampler::cfg (include/verbo/verbo.hpp:123). */
 VERBO_CUDA_API int verbo_cuda_sampler_cfg(const verbo_cuda_sampler* s, verbo_sampling* out);
 
+/* ---- batched generation streams ------------------------------------------
+   The loop of verbo::generate (src/sampler.cpp:111-181) for B streams at
+   once, with each stream's Sampler state on the device: its xoroshiro128+
+   state and its penalty window (the last repeat_last accepted ids, which is
+   all Sampler::pick reads of the history).  A step samples one id per stream
+   from B device rows and accepts it into the stream's window on the device,
+   so the caller's decode loop moves only the ids it wants to inspect (stop
+   checks and detokenisation stay on the host, as in generate).  The reference
+   has one Sampler per generation and no batched form.
+   With a penalty (repeat != 1) the options need 1 <= repeat_last <= 2048;
+   every stream starts as verbo::Sampler(cfg) does (seeded from cfg.seed) and
+   is re-seeded with verbo_cuda_batch_reset.  Calls on one batch are ordered by
+   the CUDA stream they are given: use one stream per batch, or synchronise. */
+typedef struct verbo_cuda_batch verbo_cuda_batch;
+VERBO_CUDA_API verbo_cuda_batch* verbo_cuda_batch_new(const verbo_sampling* cfg, int streams, int device);
+VERBO_CUDA_API void verbo_cuda_batch_free(verbo_cuda_batch* b);
+/* Sampler::reset for stream `stream` (src/sampler.cpp:26-31) with `seed`
+   (0: the clock, as in the reference): new RNG state, empty window. */
+VERBO_CUDA_API int verbo_cuda_batch_reset(verbo_cuda_batch* b, int stream, unsigned long long seed,
+                                          void* cuda_stream);
+/* Sampler::accept of n host ids (src/sampler.cpp:43-48), e.g. the prompt. */
+VERBO_CUDA_API int verbo_cuda_batch_accept(verbo_cuda_batch* b, int stream, const int* ids, int n,
+                                           void* cuda_stream);
+/* One pick + accept per stream: `logits` holds B device rows of `ld` floats
+   (vocab used); out_ids (device, B ints) receives the ids; stats optional. */
+VERBO_CUDA_API int verbo_cuda_batch_step(verbo_cuda_batch* b, const float* logits, int vocab, long long ld,
+                                         int* out_ids, verbo_row_stats* stats, void* cuda_stream);
+
 #ifdef __cplusplus
 }
 #endif

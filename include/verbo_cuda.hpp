@@ -70,5 +70,35 @@ class Sampler {
   verbo_cuda_sampler* h_ = nullptr;
 };
 
+// B generation streams whose Sampler state (RNG, penalty window) lives on the
+// device: the batched form of the loop in verbo::generate.  step() samples
+// one id per stream from B device rows and accepts it on the device.
+class Batch {
+ public:
+  Batch(Sampling cfg, int streams, int device = 0) : cfg_(cfg) {
+    const verbo_sampling c = cfg.c();
+    h_ = verbo_cuda_batch_new(&c, streams, device);
+    if (!h_) throw std::runtime_error(verbo_cuda_last_error());
+  }
+  ~Batch() { verbo_cuda_batch_free(h_); }
+  Batch(const Batch&) = delete;
+  Batch& operator=(const Batch&) = delete;
+
+  void reset(int stream, std::uint64_t seed, void* cuda_stream = nullptr) {
+    check(verbo_cuda_batch_reset(h_, stream, seed, cuda_stream));
+  }
+  void accept(int stream, const int* ids, int n, void* cuda_stream = nullptr) {
+    check(verbo_cuda_batch_accept(h_, stream, ids, n, cuda_stream));
+  }
+  void step(const float* d_logits, int vocab, long long ld, int* d_out_ids, void* cuda_stream = nullptr) {
+    check(verbo_cuda_batch_step(h_, d_logits, vocab, ld, d_out_ids, nullptr, cuda_stream));
+  }
+  const Sampling& cfg() const { return cfg_; }
+
+ private:
+  Sampling cfg_;
+  verbo_cuda_batch* h_ = nullptr;
+};
+
 }  // namespace cuda
 }  // namespace verbo

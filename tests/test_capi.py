@@ -37,7 +37,7 @@ def declared_functions():
 
 def test_exports_match_header(lib):
     declared = declared_functions()
-    assert len(declared) == 16
+    assert len(declared) == 21
     out = subprocess.run(["nm", "-D", "--defined-only", str(build.LIB)], capture_output=True, text=True,
                          check=True).stdout
     exported = sorted(ln.split()[-1] for ln in out.splitlines() if ln.split()[-1].startswith("verbo_cuda_"))
@@ -114,6 +114,23 @@ def test_shard_and_merge_validation(lib):
     big = vb.Sampling(top_k=10)._c()
     assert lib.verbo_cuda_merge_sample(1, 1, 2, 8, 1024, 1000, ctypes.byref(big), 1, 1, None, None) == -1
     assert "nshards * k" in lib.verbo_cuda_last_error().decode()
+
+
+def test_batch_validation(lib):
+    """Arguments are checked before any device is touched."""
+    assert lib.verbo_cuda_batch_new(None, 4, 0) is None
+    assert "cfg is NULL" in lib.verbo_cuda_last_error().decode()
+    o = vb.Sampling()._c()
+    assert lib.verbo_cuda_batch_new(ctypes.byref(o), 0, 0) is None
+    assert "streams" in lib.verbo_cuda_last_error().decode()
+    for rl in (0, 4096):
+        bad = vb.Sampling(repeat=1.1, repeat_last=rl)._c()
+        assert lib.verbo_cuda_batch_new(ctypes.byref(bad), 4, 0) is None
+        assert "repeat_last" in lib.verbo_cuda_last_error().decode()
+    assert lib.verbo_cuda_batch_step(None, 1, 10, 10, 1, None, None) == -1
+    assert "batch is NULL" in lib.verbo_cuda_last_error().decode()
+    assert lib.verbo_cuda_batch_reset(None, 0, 1, None) == -1
+    assert lib.verbo_cuda_batch_accept(None, 0, None, 0, None) == -1
 
 
 def test_error_message_is_thread_local_and_cleared(lib):

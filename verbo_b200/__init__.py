@@ -123,6 +123,11 @@ def load_library():
         "verbo_cuda_sampler_accept": (ctypes.c_int, [_P, ctypes.c_int]),
         "verbo_cuda_sampler_reset": (ctypes.c_int, [_P]),
         "verbo_cuda_sampler_cfg": (ctypes.c_int, [_P, ctypes.POINTER(_Sampling)]),
+        "verbo_cuda_batch_new": (_P, [ctypes.POINTER(_Sampling), ctypes.c_int, ctypes.c_int]),
+        "verbo_cuda_batch_free": (None, [_P]),
+        "verbo_cuda_batch_reset": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_ulonglong, _P]),
+        "verbo_cuda_batch_accept": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_int, _P]),
+        "verbo_cuda_batch_step": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_longlong, _P, _P, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -311,3 +316,55 @@ class Sampler:
         c = _Sampling()
         _ok(self._lib.verbo_cuda_sampler_cfg(self._h, ctypes.byref(c)))
         return Sampling(c.temp, c.top_k, c.top_p, c.min_p, c.repeat, c.repeat_last, c.seed)
+
+
+class Batch:
+    """B generation streams sampled together, their RNG states and penalty
+    windows kept on the device (the batched form of verbo::generate's loop,
+    src/sampler.cpp:111-181).  ``step`` takes CUDA float32 rows [B, ld]."""
+
+    def __init__(self, cfg: Optional[Sampling], streams: int, device: int = 0):
+        self._lib = load_library()
+        self._cfg = cfg if cfg is not None else Sampling()
+        c = self._cfg._c()
+        h = self._lib.verbo_cuda_batch_new(ctypes.byref(c), int(streams), device)
+        if not h:
+            raise _err()
+        self._h = h
+        self.streams = int(streams)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.verbo_cuda_batch_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self, stream: int, seed: int, cuda_stream=None) -> None:
+        _ok(self._lib.verbo_cuda_batch_reset(self._h, int(stream), int(seed), _stream(cuda_stream)))
+
+    def accept(self, stream: int, ids, cuda_stream=None) -> None:
+        import numpy as np
+
+        arr = np.ascontiguousarray(ids, dtype=np.int32)
+        _ok(self._lib.verbo_cuda_batch_accept(self._h, int(stream), arr.ctypes.data if arr.size else None, arr.size,
+                                              _stream(cuda_stream)))
+
+    def step(self, logits, out=None, stats=None, vocab=None, cuda_stream=None):
+        import torch
+
+        rows, cols = logits.shape
+        if rows != self.streams:
+            raise VerboCudaError("logits must have one row per stream")
+        if logits.dtype != torch.float32:
+            raise VerboCudaError("logits must be float32")
+        if out is None:
+            out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+        _ok(self._lib.verbo_cuda_batch_step(self._h, _dptr(logits, True), cols if vocab is None else vocab,
+                                            logits.stride(0), _dptr(out), _dptr(stats), _stream(cuda_stream)))
+        return out
+

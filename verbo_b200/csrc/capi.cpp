@@ -128,10 +128,10 @@ struct Scratch {
 std::mutex g_scratch_mu;
 std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
 
-void attach_split_scratch(vb::RowArgs& a, const vb::DevOpts& o, bool greedy, cudaStream_t s) {
+void attach_split_scratch(vb::RowArgs& a, const vb::DevOpts& o, bool greedy, cudaStream_t s, bool windows = true) {
   int dev = 0;
   cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
-  const int win_w = vb::split_window_width(o);
+  const int win_w = windows ? vb::split_window_width(o) : 0;
   const vb::SplitScratch l = vb::split_scratch_layout(a.rows, a.cluster, greedy, win_w);
   const size_t bytes = l.bytes;
   std::lock_guard<std::mutex> lk(g_scratch_mu);
@@ -155,6 +155,29 @@ void plan_split(vb::RowArgs& a) {
   a.slice = (a.slice + 3) & ~3;
 }
 
+// Picks the kernel for the options: the split-row kernels for greedy and
+// 0 < top_k <= 256, the full-vocabulary kernel otherwise.  `ring` (batched
+// streams) replaces the split kernels' scratch windows by the streams' own.
+void dispatch_rows(vb::RowArgs& a, const vb::DevOpts& o, int vocab, cudaStream_t s, int* ring, int ring_w) {
+  cudaError_t e;
+  if (o.greedy || (o.k < vocab && o.k <= vb::kSplitMaxK)) {
+    plan_split(a);
+    attach_split_scratch(a, o, o.greedy != 0, s, ring == nullptr);
+    if (ring) {
+      a.win = ring;
+      a.win_w = ring_w;
+    }
+    e = vb::launch_split(a, o, o.greedy ? vb::kSplitGreedy : vb::kSplitSample, s);
+  } else {
+    if (ring) {  // read through the CSR view; the ring is where the sampled ids go
+      a.win = ring;
+      a.win_w = ring_w;
+    }
+    e = vb::launch_general(a, o, s);
+  }
+  cuda_ok(e, "kernel launch");
+}
+
 void check_hist(const int* hist, const long long* hist_off) {
   if ((hist == nullptr) != (hist_off == nullptr)) fail("hist and hist_off must both be given or both be NULL");
 }
@@ -175,15 +198,7 @@ int sample_impl(const float* logits, int rows, int vocab, long long ld, const in
   a.rng = rng;
   a.out_ids = out_ids;
   a.stats = stats;
-  cudaError_t e;
-  if (o.greedy || (o.k < vocab && o.k <= vb::kSplitMaxK)) {
-    plan_split(a);
-    attach_split_scratch(a, o, o.greedy != 0, s);
-    e = vb::launch_split(a, o, o.greedy ? vb::kSplitGreedy : vb::kSplitSample, s);
-  } else {
-    e = vb::launch_general(a, o, s);
-  }
-  cuda_ok(e, "kernel launch");
+  dispatch_rows(a, o, vocab, s, nullptr, 0);
   return 0;
 }
 
@@ -508,6 +523,189 @@ VERBO_CUDA_API int verbo_cuda_sampler_cfg(const verbo_cuda_sampler* s, verbo_sam
       [&]() {
         if (!s || !out) fail("sampler and out must not be NULL");
         *out = s->cfg;
+        return 0;
+      },
+      -1);
+}
+
+// ------------------------------------------------------- batched streams --
+// B generation streams whose RNG states and penalty windows stay on the device
+// (the batched form of the loop in verbo::generate, src/sampler.cpp:111-181).
+// Each stream's window is a ring of its last repeat_last accepted ids; the
+// kernel that finishes a row appends the id it sampled, so a step is the
+// sampling launch and nothing else.
+
+}  // extern "C"
+
+struct verbo_cuda_batch {
+  verbo_sampling cfg{};
+  int device = 0;
+  int streams = 0;
+  bool pen = false;   // repeat != 1: the streams keep windows
+  int ring_len = 0;   // repeat_last
+  int win_w = 0;      // ring row stride (ring_len rounded up to 4, the tail -1)
+  int* d_win = nullptr;
+  long long* d_pos = nullptr;
+  long long* d_off = nullptr;  // CSR view of the rings for the full-vocabulary kernel
+  unsigned long long* d_rng = nullptr;
+  int* d_stage = nullptr;
+  long long stage_cap = 0;
+};
+
+namespace {
+
+void batch_release(verbo_cuda_batch* b) {
+  if (!b) return;
+  cudaSetDevice(b->device);
+  cudaDeviceSynchronize();
+  cudaFree(b->d_win);
+  cudaFree(b->d_pos);
+  cudaFree(b->d_off);
+  cudaFree(b->d_rng);
+  cudaFree(b->d_stage);
+}
+
+void batch_check_stream(const verbo_cuda_batch* b, int i) {
+  if (!b) fail("batch is NULL");
+  if (i < 0 || i >= b->streams) fail("stream index out of range");
+}
+
+// Sampler::reset of one stream (src/sampler.cpp:26-31): seed 0 takes the clock.
+void batch_reset_one(verbo_cuda_batch* b, int i, unsigned long long seed, cudaStream_t s) {
+  unsigned long long st[2];
+  seed_state(seed, st);
+  cuda_ok(cudaMemcpyAsync(b->d_rng + 2ll * i, st, sizeof(st), cudaMemcpyHostToDevice, s), "upload rng");
+  if (b->pen) {
+    cuda_ok(cudaMemsetAsync(b->d_win + static_cast<long long>(i) * b->win_w, 0xff, b->win_w * sizeof(int), s),
+            "clear window");
+    cuda_ok(cudaMemsetAsync(b->d_pos + i, 0, sizeof(long long), s), "clear count");
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+VERBO_CUDA_API verbo_cuda_batch* verbo_cuda_batch_new(const verbo_sampling* cfg, int streams, int device) {
+  return guard(
+      [&]() -> verbo_cuda_batch* {
+        if (!cfg) fail("cfg is NULL");
+        if (streams < 1 || streams > (1 << 24)) fail("streams must be in [1, 16777216]");
+        if (std::isnan(cfg->temp) || cfg->temp == INFINITY) fail("temp must not be NaN or +inf");
+        const bool pen = cfg->repeat != 1.0f;
+        if (pen && (cfg->repeat_last < 1 || cfg->repeat_last > vb::kWinMax))
+          fail("batched streams with a repetition penalty need 1 <= repeat_last <= " + std::to_string(vb::kWinMax));
+        int n = 0;
+        cuda_ok(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+        if (device < 0 || device >= n) fail("no CUDA device " + std::to_string(device));
+        cuda_ok(cudaSetDevice(device), "cudaSetDevice");
+        auto* b = new verbo_cuda_batch();
+        b->cfg = *cfg;
+        b->device = device;
+        b->streams = streams;
+        b->pen = pen;
+        try {
+          cuda_ok(cudaMalloc(&b->d_rng, 16ull * streams), "cudaMalloc rng");
+          if (pen) {
+            b->ring_len = cfg->repeat_last;
+            b->win_w = (cfg->repeat_last + 3) & ~3;
+            cuda_ok(cudaMalloc(&b->d_win, 4ull * b->win_w * streams), "cudaMalloc windows");
+            cuda_ok(cudaMalloc(&b->d_pos, 8ull * streams), "cudaMalloc counts");
+            cuda_ok(cudaMalloc(&b->d_off, 8ull * (streams + 1)), "cudaMalloc offsets");
+            std::vector<long long> off(static_cast<size_t>(streams) + 1);
+            for (int i = 0; i <= streams; ++i) off[i] = static_cast<long long>(i) * b->win_w;
+            cuda_ok(cudaMemcpy(b->d_off, off.data(), off.size() * 8, cudaMemcpyHostToDevice), "upload offsets");
+            cuda_ok(cudaMemset(b->d_win, 0xff, 4ull * b->win_w * streams), "clear windows");
+            cuda_ok(cudaMemset(b->d_pos, 0, 8ull * streams), "clear counts");
+          }
+          // every stream starts as verbo::Sampler(cfg) does: seeded from cfg.seed
+          unsigned long long st[2];
+          seed_state(cfg->seed, st);
+          std::vector<unsigned long long> all(2ull * streams);
+          for (int i = 0; i < streams; ++i) {
+            all[2ull * i] = st[0];
+            all[2ull * i + 1] = st[1];
+          }
+          cuda_ok(cudaMemcpy(b->d_rng, all.data(), all.size() * 8, cudaMemcpyHostToDevice), "upload rng");
+        } catch (...) {
+          batch_release(b);
+          delete b;
+          throw;
+        }
+        return b;
+      },
+      nullptr);
+}
+
+VERBO_CUDA_API void verbo_cuda_batch_free(verbo_cuda_batch* b) {
+  batch_release(b);
+  delete b;
+}
+
+VERBO_CUDA_API int verbo_cuda_batch_reset(verbo_cuda_batch* b, int stream, unsigned long long seed, void* cuda_stream) {
+  return guard(
+      [&]() {
+        batch_check_stream(b, stream);
+        cuda_ok(cudaSetDevice(b->device), "cudaSetDevice");
+        batch_reset_one(b, stream, seed, static_cast<cudaStream_t>(cuda_stream));
+        return 0;
+      },
+      -1);
+}
+
+VERBO_CUDA_API int verbo_cuda_batch_accept(verbo_cuda_batch* b, int stream, const int* ids, int n, void* cuda_stream) {
+  return guard(
+      [&]() {
+        batch_check_stream(b, stream);
+        if (n < 0) fail("n must be >= 0");
+        if (n > 0 && !ids) fail("ids is NULL");
+        if (!b->pen || n == 0) return 0;  // without a penalty nothing reads the history
+        cuda_ok(cudaSetDevice(b->device), "cudaSetDevice");
+        const cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+        // only the last ring_len ids can reach the window
+        const int skip = n > b->ring_len ? n - b->ring_len : 0;
+        const int m = n - skip;
+        if (b->stage_cap < m) {
+          cuda_ok(cudaStreamSynchronize(s), "stream");  // the old staging may still be read
+          cudaFree(b->d_stage);
+          b->d_stage = nullptr;
+          b->stage_cap = 0;
+          cuda_ok(cudaMalloc(&b->d_stage, 4ull * b->ring_len), "cudaMalloc staging");
+          b->stage_cap = b->ring_len;
+        }
+        cuda_ok(cudaMemcpyAsync(b->d_stage, ids + skip, 4ull * m, cudaMemcpyHostToDevice, s), "upload ids");
+        // the skipped ids still count: they advance the stream's ring position
+        cuda_ok(vb::launch_ring_accept(b->d_win, b->win_w, b->ring_len, b->d_pos, stream, b->d_stage, m, skip, s),
+                "kernel launch");
+        return 0;
+      },
+      -1);
+}
+
+VERBO_CUDA_API int verbo_cuda_batch_step(verbo_cuda_batch* b, const float* logits, int vocab, long long ld,
+                                         int* out_ids, verbo_row_stats* stats, void* cuda_stream) {
+  return guard(
+      [&]() {
+        if (!b) fail("batch is NULL");
+        if (!logits || !out_ids) fail("logits and out_ids must not be NULL");
+        if (vocab < 1 || vocab > vb::kMaxVocab) fail("vocab must be in [1, " + std::to_string(vb::kMaxVocab) + "]");
+        if (ld < vocab) fail("ld must be >= vocab");
+        cuda_ok(cudaSetDevice(b->device), "cudaSetDevice");
+        const cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+        vb::DevOpts o = make_opts(b->cfg, vocab, b->pen);
+        // the rings hold exactly the windows: the CSR view (full-vocabulary
+        // kernel) reads each whole ring row, -1 slots marking nothing
+        if (b->pen) o.repeat_last = b->win_w;
+        vb::RowArgs a = row_args(logits, b->streams, vocab, ld, 0, vocab, b->pen ? b->d_win : nullptr,
+                                 b->pen ? b->d_off : nullptr);
+        a.rng = b->d_rng;
+        a.out_ids = out_ids;
+        a.stats = stats;
+        if (b->pen) {
+          a.ring_pos = b->d_pos;
+          a.ring_len = b->ring_len;
+        }
+        dispatch_rows(a, o, vocab, s, b->pen ? b->d_win : nullptr, b->win_w);
         return 0;
       },
       -1);

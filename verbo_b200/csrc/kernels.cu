@@ -37,6 +37,15 @@ __device__ unsigned int g_status;
 
 __device__ __forceinline__ void raise_status(unsigned bits) { atomicOr(&g_status, bits); }
 
+// Sampler::accept (src/sampler.cpp:43-48) of a batched stream on the device:
+// the ring keeps the last ring_len ids, which is all the penalty window reads.
+__device__ __forceinline__ void ring_append(const RowArgs& a, int row, int id) {
+  if (!a.ring_pos) return;
+  const long long p = a.ring_pos[row];
+  a.win[static_cast<long long>(row) * a.win_w + p % a.ring_len] = id;
+  a.ring_pos[row] = p + 1;
+}
+
 // xoroshiro128+ draw, Sampler::unit (src/sampler.cpp:33-41).
 __device__ __forceinline__ double rng_unit(unsigned long long& s1_io, unsigned long long& s0_io) {
   unsigned long long s1 = s1_io;
@@ -996,6 +1005,7 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
   }
   if (crank == 0 && threadIdx.x == 0) {
     a.out_ids[row] = out_id;
+    ring_append(a, row, out_id);  // the cluster's CTAs read the ring only at the start
     if (a.stats) {
       const double nan = __longlong_as_double(0x7ff8000000000000ll);
       write_stats(a.stats + row, s_sum, s_tot, u, nan, nan, o.k, s_keep, out_id, 0);
@@ -1476,6 +1486,7 @@ __global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const
       if (threadIdx.x == 0) {
         const int id = static_cast<int>(did(m));
         a.out_ids[row] = id;
+        ring_append(a, row, id);
         if (a.stats) write_stats(a.stats + row, 0.0, 0.0, 0.0, __longlong_as_double(0x7ff0000000000000ll),
                                  __longlong_as_double(0x7ff0000000000000ll), o.vocab, 1, id, 1);
       }
@@ -1603,6 +1614,7 @@ __global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const
     double* pr = reinterpret_cast<double*>(H);  // H is free: fp64 scratch of the tail
     tail_pick(cand, static_cast<int>(k), o, a.rng + 2ll * row, a.out_ids + row, a.stats ? a.stats + row : nullptr, pr,
               pr + kSplitMaxK, &sh.tail);
+    if (threadIdx.x == 0) ring_append(a, row, a.out_ids[row]);  // written by this thread in tail_pick
   }
 }
 
@@ -1628,6 +1640,23 @@ int split_window_width(const DevOpts& o) {
   if (!o.penalize || o.repeat_last <= 0 || o.repeat_last > kWinMax) return 0;
   return (o.repeat_last + 3) & ~3;
 }
+// Accepts skip + n ids into one stream's ring, of which only the last n
+// (ids[0, n), n <= ring_len) are stored: the j-th id accepted by the stream
+// occupies slot j mod ring_len, so the ring always holds the last ring_len.
+__global__ void __launch_bounds__(256) ring_accept_kernel(int* win, int win_w, int ring_len, long long* pos, int row,
+                                                          const int* ids, int n, int skip) {
+  const long long p = pos[row] + skip;
+  int* w = win + static_cast<long long>(row) * win_w;
+  for (int i = threadIdx.x; i < n; i += 256) w[(p + i) % ring_len] = ids[i];
+  __syncthreads();
+  if (threadIdx.x == 0) pos[row] = p + n;
+}
+cudaError_t launch_ring_accept(int* win, int win_w, int ring_len, long long* pos, int row, const int* ids, int n,
+                               int skip, cudaStream_t s) {
+  ring_accept_kernel<<<1, 256, 0, s>>>(win, win_w, ring_len, pos, row, ids, n, skip);
+  return cudaGetLastError();
+}
+
 namespace split {
 // Copies each row's penalty window (its last repeat_last history ids,
 // src/sampler.cpp:58-64) into win[row][0, win_w), padded with -1.
@@ -1692,7 +1721,7 @@ static cudaError_t launch_split_t(const RowArgs& a0, const DevOpts& o, cudaStrea
   cudaError_t e = split_first_wave<kMode, kPen>(sm, &a.first_wave);
   if (e != cudaSuccess) return e;
   const int grid = a.rows * a.cluster;
-  if (windows) {
+  if (windows && !a.ring_pos) {  // batched streams keep their windows in place
     // launched normally: it starts after everything before it on the stream
     split::window_kernel<<<a.rows, 256, 0, s>>>(a, o);
     e = cudaGetLastError();

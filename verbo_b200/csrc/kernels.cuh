@@ -51,7 +51,18 @@ struct RowArgs {
   int* win;                        // [rows][win_w]: dense penalty windows, -1 padded (win_w > 0)
   int win_w;
   int first_wave;  // split kernel: CTAs resident at launch (SMs x CTAs per SM), set by the launcher
+  // Batched streams (verbo_cuda_batch_*): `win` is then each stream's ring of
+  // its last ring_len accepted ids (slot = count mod ring_len, -1 = empty),
+  // read as the dense window, and the kernel that finishes a row appends the
+  // sampled id to it.  ring_pos == nullptr otherwise.
+  long long* ring_pos;  // [rows]: ids accepted so far
+  int ring_len;
 };
+
+// Accepts skip + n ids into row `row`'s ring (batched streams), storing the
+// last n = ids[0, n) (n <= ring_len): one CTA.
+cudaError_t launch_ring_accept(int* win, int win_w, int ring_len, long long* pos, int row, const int* ids, int n,
+                               int skip, cudaStream_t s);
 
 // Split-row kernels: one CTA of kSplitThreads per (row, slice of <= kSplitSlice
 // columns) publishes a partial result; a per-row merge kernel follows on the
