@@ -458,11 +458,14 @@ def bench_reference(a, w: wl.Workload, world: int):
 METRIC = "sampled rows/s at V=151936, 1/2/4/8 B200; HBM GB/s vs ~8 TB/s peak"
 
 
-def workload_config(w: wl.Workload, rows_per_gpu: int, world: int, **extra):
+def workload_config(w: wl.Workload, rows_per_gpu: int, world: int, ranks=None, **extra):
+    """world: rank count the rows multiply by (1 for vocab shards, which share
+    rows); ranks: GPUs of the job, for the parallelism label (default world)."""
+    ranks = world if ranks is None else ranks
     d = {"workload": (f"{w.name}: {w.rows} x {w.vocab} fp32 logits ({w.dist}, scale {w.scale}), temp {w.temp}, "
                       f"top_k {w.top_k}, top_p {w.top_p}, min_p {w.min_p}, repeat {w.repeat} over {w.hist_len} ids"),
          "vocab": w.vocab, "rows_per_gpu": rows_per_gpu, "global_rows": rows_per_gpu * world,
-         "history": w.hist_len, "parallelism": f"rows x{world}" if w.shards == 1 else f"vocab shards x{world}"}
+         "history": w.hist_len, "parallelism": f"rows x{ranks}" if w.shards == 1 else f"vocab shards x{ranks}"}
     d.update(extra)
     return d
 
@@ -514,12 +517,14 @@ def main():
         "ms_per_step": res["elapsed_ms"] / a.steps, "higher_is_better": True,
         "scaling": "strong" if sharded else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(
-            w, R, 1 if sharded else world,
+            w, R, 1 if sharded else world, ranks=world,
             l2=("inputs larger than L2" if res["copies"] == 1 else
                 f"{res['copies']} rotating input copies ({res['copies'] * res['batch_bytes'] >> 20} MiB) > L2"),
             **({"columns_per_gpu": cols} if sharded else {})),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "traffic": None if tr is None else tr * R,
+                     "peak_kind": peak_kind,
+                     # per-row traffic was captured on all columns: a rank's shard reads its share
+                     "traffic": None if tr is None else tr * R * cols / w.vocab,
                      "kernel": (("window_kernel + " if uses_window(w) else "") + "split_kernel<emit> + merge")
                      if sharded else kernel_name(w),
                      "alg_bytes_per_launch": alg_launch, "launch_ms": res["launch_ms"]},

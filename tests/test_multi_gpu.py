@@ -1,0 +1,40 @@
+"""Vocab-sharded sampling over real NCCL ranks (one process per GPU).
+
+Runs tests/mgpu_worker.py under torch.distributed.run on 2 GPUs (skipped
+with fewer): the sharded ids must equal the unsharded CUDA path's and agree
+on every rank.  The CPU tests of the same host logic (gloo) are in
+tests/test_distributed.py.
+"""
+from __future__ import annotations
+
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_vocab_sharded_over_two_gpus_matches_unsharded(cuda_lib):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           str(ROOT / "tests" / "mgpu_worker.py")]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "== unsharded: True" in r.stdout
