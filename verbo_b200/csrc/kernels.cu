@@ -264,7 +264,8 @@ struct GenShared {
   float xlo[kMaxCluster];
   unsigned long long xs[kMaxCluster];
   unsigned long long xz[kMaxCluster];
-  unsigned long long my_s, my_z;  // this CTA's mass-pass totals, pulled by the others
+  alignas(16) unsigned long long my_sz[2];  // this CTA's mass-pass totals (S, Z), pulled by the others
+  unsigned long long all_sz[2];              // the cluster's totals
   // value-path decisions (identical in every CTA)
   int v_gather;      // 1: resolve by one gather of bins [vb_lo, vb_hi]
   int vb_lo, vb_hi;
@@ -283,6 +284,8 @@ struct GenShared {
   unsigned long long r_key, r_cum_m;
   uint32_t r_cum_c;
   int r_found;
+  uint32_t r_steps;  // resolve: rank + 1 of the member found among the gathered ones
+  uint32_t ncrowd;   // resolve: members of the target sub-bin collected
 };
 
 __device__ HFound find_hist(const Hist* H, bool by_mass, unsigned long long target, GenShared& sh) {
@@ -505,7 +508,7 @@ __device__ void select_weighted(const GenCtx& x, bool by_mass, unsigned long lon
   }
 }
 
-__global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, const DevOpts o) {
+__global__ void __launch_bounds__(kThreads, 2) general_kernel(const RowArgs a, const DevOpts o) {
   cg::cluster_group cl = cg::this_cluster();
   const int C = a.cluster;
   const int crank = static_cast<int>(cl.block_rank());
@@ -721,28 +724,57 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
     s_local = block_sum(s_local, sh.ws64);
     z_local = block_sum(z_local, sh.ws64);
     if (threadIdx.x == 0) {
-      sh.my_s = s_local;
-      sh.my_z = z_local;
+      sh.my_sz[0] = s_local;
+      sh.my_sz[1] = z_local;
     }
     // Pull model: every CTA reads all local histograms with plain DSMEM loads
     // (no remote atomics).  Lv stays untouched until every CTA has pulled it.
     cluster_sync_all();
+    // all remote loads are issued before any is used (16-byte vectors; bins
+    // b0, b0 + 1 are adjacent)
     const int b0 = 2 * threadIdx.x;
     unsigned long long m0 = 0, m1 = 0, S = 0, Z = 0;
     uint32_t c0 = 0, c1 = 0;
-    for (int r = 0; r < C; ++r) {
-      const VHist* Lr = cl.map_shared_rank(Lv, r);
-      m0 += Lr->m[b0];
-      m1 += Lr->m[b0 + 1];
-      c0 += Lr->c[b0];
-      c1 += Lr->c[b0 + 1];
-      S += *cl.map_shared_rank(&sh.my_s, r);
-      Z += *cl.map_shared_rank(&sh.my_z, r);
+    // (S, Z): thread r pulls rank r's totals, warp 0 adds them up
+    if (threadIdx.x < 32) {
+      ulonglong2 sz = make_ulonglong2(0ull, 0ull);
+      if (threadIdx.x < static_cast<unsigned>(C))
+        sz = *reinterpret_cast<const ulonglong2*>(cl.map_shared_rank(sh.my_sz, threadIdx.x));
+      sz.x = warp_sum(sz.x);
+      sz.y = warp_sum(sz.y);
+      if (threadIdx.x == 0) {
+        sh.all_sz[0] = sz.x;
+        sh.all_sz[1] = sz.y;
+      }
+    }
+#pragma unroll
+    for (int r0 = 0; r0 < kMaxCluster; r0 += 4) {
+      ulonglong2 pm[4];
+      uint2 pc[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (r0 + q < C) {
+          const VHist* Lr = cl.map_shared_rank(Lv, r0 + q);
+          pm[q] = *reinterpret_cast<const ulonglong2*>(&Lr->m[b0]);
+          pc[q] = *reinterpret_cast<const uint2*>(&Lr->c[b0]);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (r0 + q < C) {
+          m0 += pm[q].x;
+          m1 += pm[q].y;
+          c0 += pc[q].x;
+          c1 += pc[q].y;
+        }
+      }
     }
     unsigned long long tm;
     uint32_t tc;
     const unsigned long long em = block_excl_scan(m0 + m1, sh.ws64, &tm);
     const uint32_t ec = block_excl_scan(c0 + c1, sh.ws32, &tc);
+    S = sh.all_sz[0];  // written before the scans' barriers
+    Z = sh.all_sz[1];
     // First bin whose running mass reaches t (>= 1, <= tm): bin, mass and count before it.
     auto vfind = [&](unsigned long long t, int* bin, unsigned long long* bm_, uint32_t* bc_, uint32_t* cnt,
                      unsigned long long* mass) {
@@ -781,8 +813,9 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
       uint32_t* cnt0 = cl.map_shared_rank(&sh.gcount[gseq++], 0);
       for (int j = threadIdx.x; j < n; j += kThreads) {
         const float vv = v[j];
+        if (!pick(vv)) continue;  // (cheap test first; the key only for members)
         const unsigned long long kc = ckey(vv, static_cast<uint32_t>(g_lo + j), a.idxbits);
-        if (kc > klim || !pick(vv)) continue;
+        if (kc > klim) continue;
         double m;
         const unsigned long long qm = fixed_mass(x, vv, &m);
         if (!in_pset(x, m, thr, kc) || qm == 0) continue;
@@ -799,15 +832,7 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
       const uint32_t got = sh.ng;
       __syncthreads();
       if (got > static_cast<uint32_t>(cap)) return cap + 1;
-      const int ng = static_cast<int>(got);
-      const int P = next_pow2(max(ng, 2));
-      for (int i = ng + threadIdx.x; i < P; i += kThreads) {
-        gkey[i] = kNoKey;
-        gmass[i] = 0;
-      }
-      __syncthreads();
-      sort_pairs(gkey, gmass, P);
-      return ng;
+      return static_cast<int>(got);  // unsorted: resolve() orders what it needs
     };
     // Walks sorted members from running mass `cm`: index of the first whose
     // running mass reaches t, or -1.  Run by thread 0 only.
@@ -822,6 +847,121 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
         }
       }
       return -1;
+    };
+    // Among the gathered members (gkey, gmass)[0, ng) (unsorted) of value bin
+    // `bin` (its refined sub-bin `sub` when >= 0), the first in key order at
+    // which base + running mass reaches t (> base): sets sh.r_found, r_key,
+    // r_cum_m (running mass including it) and r_steps (its rank + 1).  The
+    // members go into kThreads sub-bins by value, monotone in key order (ties
+    // share a sub-bin), by a histogram and one scan in Gv; only the target
+    // sub-bin's members (at most 32) are sorted, by one warp.  A crowded
+    // sub-bin (ties) sorts all members and walks them instead.
+    auto resolve = [&](unsigned long long* gkey, unsigned long long* gmass, int ng, int bin, int sub,
+                       unsigned long long base, unsigned long long t) {
+      constexpr int NS = kThreads;
+      unsigned long long* sm = Gv->m;  // [NS] masses
+      uint32_t* sc = Gv->c;            // [NS] counts
+      uint32_t* lst = Gv->c + NS;      // [32] members of the target sub-bin
+      auto sbin = [&](unsigned long long kc) -> int {
+        const float vv = unord32(~static_cast<uint32_t>(kc >> a.idxbits));
+        float u = __fsub_rn(__fmul_rn(__fsub_rn(x.M, vv), inv_w), static_cast<float>(bin));
+        if (sub >= 0) u = __fsub_rn(__fmul_rn(u, 1024.0f), static_cast<float>(sub));
+        return min(NS - 1, max(0, static_cast<int>(__fmul_rn(u, static_cast<float>(NS)))));
+      };
+      sm[threadIdx.x] = 0;
+      sc[threadIdx.x] = 0;
+      if (threadIdx.x == 0) sh.ncrowd = 0;
+      __syncthreads();
+      for (int i = threadIdx.x; i < ng; i += kThreads) {
+        const int b = sbin(gkey[i]);
+        atomicAdd(&sc[b], 1u);
+        atomicAdd(&sm[b], gmass[i]);
+      }
+      __syncthreads();
+      const unsigned long long mm = sm[threadIdx.x];
+      const uint32_t cc = sc[threadIdx.x];
+      unsigned long long mt;
+      uint32_t ct;
+      const unsigned long long em = block_excl_scan(mm, sh.ws64, &mt);
+      const uint32_t ec = block_excl_scan(cc, sh.ws32, &ct);
+      const unsigned long long tt = t - base;
+      if (threadIdx.x == 0) sh.hf.bin = -1;
+      __syncthreads();
+      if (em < tt && tt <= em + mm) {
+        sh.hf.bin = threadIdx.x;
+        sh.hf.before_m = em;
+        sh.hf.before_c = ec;
+        sh.hf.c = cc;
+      }
+      __syncthreads();
+      const int sb = sh.hf.bin;
+      const unsigned long long bm = sh.hf.before_m;
+      const uint32_t bcnt = sh.hf.before_c, ns = sh.hf.c;
+      __syncthreads();
+      if (sb < 0) {  // the members' mass does not reach t
+        if (threadIdx.x == 0) sh.r_found = 0;
+        __syncthreads();
+        return;
+      }
+      if (ns <= 32u) {
+        for (int i = threadIdx.x; i < ng; i += kThreads)
+          if (sbin(gkey[i]) == sb) {
+            const uint32_t q = atomicAdd(&sh.ncrowd, 1u);
+            if (q < 32u) lst[q] = static_cast<uint32_t>(i);
+          }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+          const int lane = threadIdx.x;
+          const bool have = lane < static_cast<int>(ns);
+          unsigned long long k = have ? gkey[lst[lane]] : kNoKey;
+          unsigned long long m = have ? gmass[lst[lane]] : 0ull;
+#pragma unroll
+          for (int kk = 2; kk <= 32; kk <<= 1) {
+#pragma unroll
+            for (int j = kk >> 1; j > 0; j >>= 1) {  // ascending bitonic sort by key, mass alongside
+              const unsigned long long pk = __shfl_xor_sync(0xffffffffu, k, j);
+              const unsigned long long pm = __shfl_xor_sync(0xffffffffu, m, j);
+              const bool take_min = ((lane & j) == 0) == ((lane & kk) == 0);
+              if (take_min ? (pk < k) : (pk > k)) {
+                k = pk;
+                m = pm;
+              }
+            }
+          }
+          const unsigned long long inc = warp_incl_scan(m);
+          const unsigned hits = __ballot_sync(0xffffffffu, lane < static_cast<int>(ns) && bm + inc >= tt);
+          const int L = hits ? __ffs(hits) - 1 : 0;
+          const unsigned long long kL = __shfl_sync(0xffffffffu, k, L);
+          const unsigned long long iL = __shfl_sync(0xffffffffu, inc, L);
+          if (lane == 0) {
+            sh.r_found = hits != 0;
+            sh.r_key = kL;
+            sh.r_cum_m = base + bm + iL;
+            sh.r_steps = bcnt + static_cast<uint32_t>(L) + 1u;
+          }
+        }
+        __syncthreads();
+        return;
+      }
+      const int P = next_pow2(max(ng, 2));
+      for (int i = ng + threadIdx.x; i < P; i += kThreads) {
+        gkey[i] = kNoKey;
+        gmass[i] = 0;
+      }
+      __syncthreads();
+      sort_pairs(gkey, gmass, P);
+      if (threadIdx.x == 0) {
+        unsigned long long cm = 0;
+        int st = 0;
+        const int i = walk(gmass, ng, base, t, &cm, &st);
+        sh.r_found = i >= 0;
+        if (i >= 0) {
+          sh.r_key = gkey[i];
+          sh.r_cum_m = cm;
+          sh.r_steps = static_cast<uint32_t>(st);
+        }
+      }
+      __syncthreads();
     };
     // the cutoff gather lands in the local histogram's space (free after the push)
     // Buffers: the cutoff gather goes to vg (nobody pulls it); the draw gather
@@ -847,18 +987,10 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
       if (ng > kCutCap) {
         exact = false;
       } else {
-        if (threadIdx.x == 0) {
-          unsigned long long cm;
-          int st = 0;
-          const int i = walk(cmass, ng, Bc, tp, &cm, &st);
-          sh.r_found = i >= 0;
-          sh.r_cum_m = i >= 0 ? cm : 0;
-          sh.r_cum_c = Cc + static_cast<uint32_t>(st);
-        }
-        __syncthreads();
+        resolve(ckeys, cmass, ng, bc, -1, Bc, tp);
         if (!sh.r_found) exact = false;
-        tot_m = sh.r_cum_m;
-        keep_c = sh.r_cum_c;
+        tot_m = sh.r_found ? sh.r_cum_m : 0;
+        keep_c = Cc + (sh.r_found ? sh.r_steps : 0u);
         __syncthreads();
       }
     }
@@ -897,8 +1029,9 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
         __syncthreads();
         for (int j = threadIdx.x; j < n; j += kThreads) {
           const float vv = v[j];
+          if (vbin(vv) != bd) continue;
           const unsigned long long kc = ckey(vv, static_cast<uint32_t>(g_lo + j), a.idxbits);
-          if (kc > klim || vbin(vv) != bd) continue;
+          if (kc > klim) continue;
           double m;
           const unsigned long long qm = fixed_mass(x, vv, &m);
           if (!in_pset(x, m, thr, kc) || qm == 0) continue;
@@ -953,14 +1086,7 @@ __global__ void __launch_bounds__(kThreads) general_kernel(const RowArgs a, cons
         if (ng > kVGatherCap) {
           exact = false;
         } else {
-          if (threadIdx.x == 0) {
-            unsigned long long cm;
-            int st;
-            const int i = walk(dmass, ng, base, t, &cm, &st);
-            sh.r_found = i >= 0;
-            if (i >= 0) sh.r_key = dkeys[i];
-          }
-          __syncthreads();
+          resolve(dkeys, dmass, ng, bd, sub, base, t);
           if (sh.r_found) out_id = static_cast<int>(sh.r_key & idmask);
           else exact = false;
           __syncthreads();
