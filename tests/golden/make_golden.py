@@ -16,7 +16,12 @@ Writes, next to this script:
 * ``configs.json`` - the five benchmark configurations at a few rows each:
                      the ids of 2 picks per row from the reference, plus a
                      SHA-256 of the regenerated logits so a test can tell a
-                     changed generator from a wrong sampler.
+                     changed generator from a wrong sampler;
+* ``tiny_qwen2.f32`` - all 38 real rows of that fixture in the reference's
+                     logits dump layout (cli/main.cpp:174-190: raw fp32 rows),
+                     read back through verbo_b200.logits_dump;
+* ``dump_ids.json``  - the ids the reference's Sampler picks from those rows
+                     (2 picks per row) under three option sets.
 
 The reference's Sampler has no golden vectors of its own for seeded draws
 (its tests check determinism and ranges only, tests/test_core.cpp:454-496),
@@ -36,7 +41,14 @@ ROOT = HERE.parent.parent
 sys.path.insert(0, str(ROOT))
 
 from oracle import pyoracle as po  # noqa: E402
+from verbo_b200 import logits_dump  # noqa: E402
 from verbo_b200 import workloads as wl  # noqa: E402
+
+DUMP_OPTS = {
+    "greedy": dict(temp=0.0, top_k=40, top_p=0.9, min_p=0.0, repeat=1.0, repeat_last=64),
+    "default": dict(temp=0.7, top_k=40, top_p=0.9, min_p=0.0, repeat=1.0, repeat_last=64),
+    "nucleus": dict(temp=1.0, top_k=0, top_p=0.95, min_p=0.02, repeat=1.0, repeat_last=64),
+}
 
 STEPS_SMALL = 3
 STEPS_CFG = 2
@@ -142,7 +154,17 @@ def main(ref_dir: str) -> None:
             "ids": ids.tolist(),
         }
     (HERE / "configs.json").write_text(json.dumps(cfg, indent=1) + "\n")
-    print("wrote", HERE / "small.npz", HERE / "configs.json")
+
+    rows = np.fromfile(ref_dir / "tests/data/tiny-qwen2/ref_logits.bin", dtype=np.float32).reshape(-1, 400)
+    logits_dump.write_dump(HERE / "tiny_qwen2.f32", rows)
+    back = logits_dump.read_dump(HERE / "tiny_qwen2.f32", 400)
+    seeds = np.arange(back.shape[0], dtype=np.uint64) + np.uint64(9001)
+    dump = {"vocab": 400, "rows": int(back.shape[0]), "seed0": 9001, "steps": STEPS_CFG, "cases": {}}
+    for name, opts in DUMP_OPTS.items():
+        ids = po.ref_sample_rows(back, po.sampling(**opts), seeds, None, None, steps=STEPS_CFG)
+        dump["cases"][name] = {"opts": opts, "ids": ids.tolist()}
+    (HERE / "dump_ids.json").write_text(json.dumps(dump, indent=1) + "\n")
+    print("wrote", HERE / "small.npz", HERE / "configs.json", HERE / "tiny_qwen2.f32", HERE / "dump_ids.json")
 
 
 if __name__ == "__main__":
