@@ -286,6 +286,36 @@ def test_full_vocab_weights_match_reference_sums(temp):
         np.testing.assert_allclose(st["sum"], ost[:, -1]["sum"], rtol=5e-11)
 
 
+@pytest.mark.parametrize("k", [32, 50, 64])
+def test_topk_concentrated_in_few_slices(k):
+    # For 32 <= k <= 64 a slice emits only its top-m (m = 24 at V = 151936)
+    # and the merge checks each slice's threshold against the k-th value
+    # found.  Rows whose k best sit in one or two slices (slices are 10240
+    # columns) fail that check for those slices, which the merge then
+    # resolves exactly; the ids must not notice.
+    g = np.random.default_rng(k + 7)
+    V, S = 151936, 10240
+    x = g.standard_normal((6, V)).astype(np.float32)
+    x[0, :S] += 6.0                                   # all in slice 0
+    x[1, V - 3000:] += 6.0                            # all in the last (short) slice
+    x[2, 3 * S:4 * S] += 6.0
+    x[2, 9 * S:10 * S] += 6.0                         # split over two slices
+    x[3] = np.sort(x[3])                              # ascending: the k best at the end
+    x[4, S:S + 40] = 9.0                              # a block of equal values across the k-th
+    # row 5: no concentration
+    hist = np.concatenate([g.integers(0, S, size=48), g.integers(V - 3000, V, size=48)] * 6).astype(np.int32)
+    off = np.arange(7, dtype=np.int64) * 96
+    seeds = np.arange(6, dtype=np.uint64) + np.uint64(700 + k)
+    for opts in (dict(temp=0.8, top_k=k, top_p=0.95, repeat=1.2, repeat_last=64),
+                 dict(temp=1.0, top_k=k, top_p=1.0, min_p=0.01, repeat=1.3, repeat_last=0),  # whole history (CSR)
+                 dict(temp=0.7, top_k=k, top_p=0.9)):
+        ids, st, _ = run_gpu(x, opts, seeds, hist, off, steps=2)
+        ora, ost, _ = run_oracle(x, opts, seeds, hist, off, steps=2)
+        compare(ids, ora, ost, f"k={k} {opts}")
+        np.testing.assert_allclose(st["sum"], ost[:, -1]["sum"], rtol=1e-9)
+        assert np.array_equal(st["k"], ost[:, -1]["k"])
+
+
 @pytest.mark.parametrize("k", [1, 2, 31, 33, 50, 64, 128, 255, 256])
 def test_split_topk_bounds(k):
     # The split top-k kernels bound each slice (and then the union) by the

@@ -326,7 +326,7 @@ VERBO_CUDA_API int verbo_cuda_sample_noalloc(const float* logits, int rows, int 
                 "kernel launch");
         if (too_big) {
           const long long per_row = 4ll * a.cluster + 8ll * a.cluster * (o.greedy ? 1 : vb::kSliceCap) +
-                                    4ll * vb::split_window_width(o);
+                                    (o.greedy ? 0ll : 4ll * a.cluster) + 4ll * vb::split_window_width(o);
           fail("rows x vocab exceed the fixed scratch of " + std::to_string(vb::kNoAllocScratchBytes >> 20) +
                " MiB: at most about " + std::to_string((vb::kNoAllocScratchBytes - 512) / per_row) +
                " rows at vocab " + std::to_string(vocab) + " per call");

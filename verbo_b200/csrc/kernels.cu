@@ -1214,7 +1214,8 @@ namespace split {
 constexpr int NT = kSplitThreads;
 constexpr int NW = NT / 32;
 constexpr int kBinsS = 2048;  // 11-bit digits of the candidate key
-constexpr int kUnionCap = 2048;
+constexpr int kUnionCap = 2048;  // union of a row's candidates staged in the merge kernel
+constexpr int kAugCap = 256;     // exact keys of slices whose certificate failed
 
 struct Shared {
   unsigned long long ws64[NW];
@@ -1424,6 +1425,18 @@ __device__ __forceinline__ unsigned long long to_ckey(unsigned long long d, int 
   return ((d >> 32) << idxbits) | (d & 0xffffffffull);
 }
 
+// Candidates a top-k slice must certainly hold: its whole top-kl, except in
+// rows of C >= 2 slices with 32 <= k <= 64, where the top-m with
+// m = max(kTopM, ceil(k / (C - 1))) suffices: C - 1 full slices give the
+// union at least k keys, and a slice whose threshold is above the union's
+// k-th value (it then holds m of the k best, so at most (k - 1) / m slices
+// can) is resolved exactly by the merge.
+__device__ __forceinline__ uint32_t split_top_m(uint32_t k, int C, uint32_t kl) {
+  if (C < 2 || k < 32u || k > 64u) return kl;
+  const uint32_t per = (k + static_cast<uint32_t>(C) - 2u) / static_cast<uint32_t>(C - 1);
+  return min(kl, max(static_cast<uint32_t>(kTopM), per));
+}
+
 // The exact top-kl of a slice by radix selection, for slices whose bound
 // admits more than kSliceCap candidates (ties, masked rows).  Rare, so it
 // re-reads the slice from L2 and stays out of line: the caller's register
@@ -1533,6 +1546,8 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
   } else {
     const uint32_t k = kMode == kSplitEmit ? static_cast<uint32_t>(min(a.cand_k, a.ncols)) : static_cast<uint32_t>(o.k);
     const uint32_t kl = min(k, static_cast<uint32_t>(n));
+    const uint32_t m = split_top_m(k, C, kl);  // the slice bounds its top-m (m == kl: its whole top-k)
+    float thr = -__int_as_float(0x7f800000);   // published certificate; -inf: the full top-kl was emitted
     uint32_t count = 0;
     unsigned long long* out = a.slice_keys + slot * kSliceCap;
     if (kl > 0) {
@@ -1542,7 +1557,7 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
       // the slice has at least kl, and its top-kl by (value desc, column asc)
       // are all among the columns >= T.
       const int wfull = min(NW, ((n + 3) >> 2) >> 5);
-      const uint32_t q = wfull > 0 ? (kl + wfull - 1) / static_cast<uint32_t>(wfull) : 33u;
+      const uint32_t q = wfull > 0 ? (m + wfull - 1) / static_cast<uint32_t>(wfull) : 33u;
       bool all = q > 32u;
       float tv = -__int_as_float(0x7f800000);
       if (!all) {
@@ -1579,13 +1594,17 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
       const uint32_t tot = (all && n > kSliceCap) ? ~0u : sh.ncand;
       if (tot <= static_cast<uint32_t>(kSliceCap)) {
         count = tot;
+        if (m < kl && !all) thr = tv;  // only the top-m is certain: the merge checks thr
       } else {
         // more than kSliceCap candidates (ties, masked rows): exact top-kl
         slice_exact_topk<kPen>(a, o, src, n, g_lo, kl, pm, H, sh, out);
         count = kl;
       }
     }
-    if (threadIdx.x == 0) a.slice_count[slot] = count;
+    if (threadIdx.x == 0) {
+      a.slice_count[slot] = count;
+      if (kMode != kSplitGreedy) a.slice_thr[slot] = thr;
+    }
   }
 
 }
@@ -1729,6 +1748,100 @@ __global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const
     for (int i = threadIdx.x; i < static_cast<int>(k); i += NT) cand[i] = sel[i];
     __syncthreads();
   }
+  // ---- certificates (split_top_m): a slice that emitted only its top-m is
+  // settled when its threshold is at or below the k-th value found; else it
+  // holds m of the k best and may hold more: its exact top-kl replaces its
+  // partial (at most (k - 1) / m slices, at most kAugCap keys in all), and
+  // the k best are selected again.
+  __shared__ uint32_t nbad;
+  __shared__ unsigned char isbad[kMaxSlices];
+  const float vk = utot >= k ? dval(cand[k - 1]) : -__int_as_float(0x7f800000);
+  if (threadIdx.x == 0) nbad = 0;
+  if (threadIdx.x < static_cast<unsigned>(C)) isbad[threadIdx.x] = 0;
+  __syncthreads();
+  if (threadIdx.x < static_cast<unsigned>(C) &&
+      __ldcg(&a.slice_thr[static_cast<long long>(row) * C + threadIdx.x]) > vk) {
+    isbad[threadIdx.x] = 1;
+    atomicAdd(&nbad, 1u);
+  }
+  __syncthreads();
+  if (nbad > 0) {
+    uint64_t* aug = U + kUnionCap;
+    __shared__ unsigned long long pmk[NT];  // the bad slice's penalty masks
+    uint32_t naug = 0;
+    for (int sl = 0; sl < C; ++sl) {
+      if (!isbad[sl]) continue;
+      const int lo = sl * a.slice;
+      const int n = max(0, min(a.ncols - lo, a.slice));
+      const long long g_lo = static_cast<long long>(a.col_off) + lo;
+      const uint32_t kl = min(k, static_cast<uint32_t>(n));
+      if (naug + kl > static_cast<uint32_t>(kAugCap)) {  // unreachable by the bound on bad slices
+        if (threadIdx.x == 0) raise_status(kErrSelect);
+        break;
+      }
+      pmk[threadIdx.x] = 0;
+      __syncthreads();
+      if (o.penalize) {  // the window, as the split kernels read it
+        if (a.win_w > 0) {
+          for (int j = threadIdx.x; j < a.win_w; j += NT) {
+            const int id = a.win[static_cast<long long>(row) * a.win_w + j];
+            const long long t = static_cast<long long>(id) - g_lo;
+            if (id >= 0 && t >= 0 && t < n) mask_set(pmk, static_cast<int>(t));
+          }
+        } else {
+          const long long h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
+          const long long len = h1 - h0;
+          const long long from = (o.repeat_last > 0 && len > o.repeat_last) ? len - o.repeat_last : 0;
+          for (long long j = h0 + from + threadIdx.x; j < h1; j += NT) {
+            const long long t = static_cast<long long>(a.hist[j]) - g_lo;
+            if (t >= 0 && t < n) mask_set(pmk, static_cast<int>(t));
+          }
+        }
+      }
+      __syncthreads();
+      const float* src = a.logits + static_cast<long long>(row) * a.ld + lo;
+      unsigned long long* dst = reinterpret_cast<unsigned long long*>(aug + naug);
+      if (o.penalize) slice_exact_topk<true>(a, o, src, n, g_lo, kl, pmk, H, sh, dst);
+      else slice_exact_topk<false>(a, o, src, n, g_lo, kl, pmk, H, sh, dst);
+      __syncthreads();
+      naug += kl;
+    }
+    // the k best of the settled slices' partials and the exact lists
+    unsigned long long prefix;
+    int shift;
+    const int nbits = 32 + a.idxbits;
+    for (int b = threadIdx.x; b < kBinsS; b += NT) H[b] = 0;
+    if (threadIdx.x == 0) sh.ncand = 0;
+    __syncthreads();
+    auto each2 = [&](auto f) {
+      for (int i = 0; i < C; ++i) {
+        if (isbad[i]) continue;
+        for (int j = threadIdx.x; j < static_cast<int>(scnt[i]); j += NT)
+          f(to_ckey(in_smem ? U[soff[i] + j] : __ldcg(base + static_cast<long long>(i) * kSliceCap + j), a.idxbits));
+      }
+      for (int e = threadIdx.x; e < static_cast<int>(naug); e += NT) f(to_ckey(aug[e], a.idxbits));
+    };
+    radix_select(each2, k, nbits, H, sh, &prefix, &shift);
+    auto take2 = [&](unsigned long long d) {
+      if ((to_ckey(d, a.idxbits) >> shift) <= prefix) {
+        const uint32_t p = atomicAdd(&sh.ncand, 1u);
+        if (p < static_cast<uint32_t>(kSliceCap)) sel[p] = d;
+      }
+    };
+    for (int i = 0; i < C; ++i) {
+      if (isbad[i]) continue;
+      for (int j = threadIdx.x; j < static_cast<int>(scnt[i]); j += NT)
+        take2(in_smem ? U[soff[i] + j] : __ldcg(base + static_cast<long long>(i) * kSliceCap + j));
+    }
+    for (int e = threadIdx.x; e < static_cast<int>(naug); e += NT) take2(aug[e]);
+    __syncthreads();
+    const int P = next_pow2(max(static_cast<int>(k), 2));
+    for (int i = static_cast<int>(k) + threadIdx.x; i < P; i += NT) sel[i] = kNoKey;
+    __syncthreads();
+    bitonic_sort_u64(sel, P);
+    for (int i = threadIdx.x; i < static_cast<int>(k); i += NT) cand[i] = sel[i];
+    __syncthreads();
+  }
   if (kMode == kSplitEmit) {
     for (int i = threadIdx.x; i < a.cand_k; i += NT) {
       const long long at = static_cast<long long>(row) * a.cand_k + i;
@@ -1751,7 +1864,8 @@ static size_t round256(size_t b) { return (b + 255) & ~static_cast<size_t>(255);
 SplitScratch split_scratch_layout(long long rows, int slices, bool greedy, int win_w) {
   SplitScratch l;
   l.off_keys = round256(static_cast<size_t>(rows) * slices * 4);
-  l.off_win = l.off_keys + round256(static_cast<size_t>(rows) * slices * (greedy ? 1 : kSliceCap) * 8);
+  l.off_thr = l.off_keys + round256(static_cast<size_t>(rows) * slices * (greedy ? 1 : kSliceCap) * 8);
+  l.off_win = l.off_thr + (greedy ? 0 : round256(static_cast<size_t>(rows) * slices * 4));
   l.bytes = l.off_win + static_cast<size_t>(rows) * win_w * 4;
   return l;
 }
@@ -1759,6 +1873,7 @@ void split_scratch_attach(RowArgs& a, void* base, const SplitScratch& l, int win
   char* b = static_cast<char*>(base);
   a.slice_count = reinterpret_cast<unsigned*>(b);
   a.slice_keys = reinterpret_cast<unsigned long long*>(b + l.off_keys);
+  a.slice_thr = reinterpret_cast<float*>(b + l.off_thr);
   a.win = win_w > 0 ? reinterpret_cast<int*>(b + l.off_win) : nullptr;
   a.win_w = win_w;
 }
@@ -1861,7 +1976,7 @@ static cudaError_t launch_split_t(const RowArgs& a0, const DevOpts& o, cudaStrea
   // the per-row merge runs after every slice of the batch (same stream)
   if (kMode == kSplitGreedy) return launch_after(split::merge_slices_kernel<kMode>, a.rows, 32, 0, s, a, o);
   return launch_after(split::merge_slices_kernel<kMode>, a.rows, split::NT,
-                      static_cast<size_t>(split::kBinsS * 4 + split::kUnionCap * 8), s, a, o);
+                      static_cast<size_t>(split::kBinsS * 4 + (split::kUnionCap + split::kAugCap) * 8), s, a, o);
 }
 cudaError_t launch_split(const RowArgs& a, const DevOpts& o, int mode, cudaStream_t s) {
   switch (mode * 2 + (o.penalize ? 1 : 0)) {

@@ -48,6 +48,7 @@ struct RowArgs {
   // Scratch of the split-row kernels (global memory, see split_scratch_layout):
   unsigned* slice_count;           // [rows * cluster]: candidates each slice published
   unsigned long long* slice_keys;  // [rows * cluster * kSliceCap]: candidate keys (greedy: 1 per slice)
+  float* slice_thr;                // [rows * cluster]: top-k slices' emission thresholds (-inf: full top-k)
   int* win;                        // [rows][win_w]: dense penalty windows, -1 padded (win_w > 0)
   int win_w;
   int first_wave;  // split kernel: CTAs resident at launch (SMs x CTAs per SM), set by the launcher
@@ -73,6 +74,10 @@ constexpr int kSplitSlice = kSplitThreads * kSplitChunks * 4;     // 10240 colum
 constexpr int kSliceCap = 256;                                    // candidates a slice may publish
 constexpr int kSplitMaxK = kSliceCap;                             // largest top_k of the split top-k kernel
 constexpr int kMaxSlices = 32;
+// Top-k slices of rows with >= 2 slices and 32 <= k <= 64 emit only their
+// top-m, m = max(kTopM, ceil(k / (slices - 1))), with their threshold as a
+// certificate the merge checks (kernels.cu, merge_slices_kernel).
+constexpr int kTopM = 24;
 
 // Dense penalty windows: when every row's window (its last repeat_last ids)
 // is at most kWinMax long, a small kernel copies the windows into
@@ -85,7 +90,7 @@ int split_window_width(const DevOpts& o);  // 0: the kernels read the CSR histor
 // counts at offset 0, keys at off_keys (one per slice for greedy, kSliceCap
 // for top-k), windows at off_win.
 struct SplitScratch {
-  size_t off_keys, off_win, bytes;
+  size_t off_keys, off_thr, off_win, bytes;
 };
 SplitScratch split_scratch_layout(long long rows, int slices, bool greedy, int win_w);
 void split_scratch_attach(RowArgs& a, void* base, const SplitScratch& l, int win_w);
