@@ -1338,6 +1338,22 @@ __device__ __forceinline__ float warp_sort_desc(float v) {
   return v;
 }
 
+// The q-th largest (1 <= q <= 32, duplicates counted) of one non-NaN value
+// per lane.  Small q: q rounds of warp max reductions, each retiring the lanes
+// that hold the maximum; larger q: a full 32-lane sort.
+__device__ __forceinline__ float warp_qth_max(float v, uint32_t q) {
+  if (q > 4u) return __shfl_sync(0xffffffffu, warp_sort_desc(v), static_cast<int>(q) - 1);
+  uint32_t u = ord32(canon(v));  // > 0 for every non-NaN value; 0 marks a retired lane
+  uint32_t seen = 0, mx;
+  while (true) {
+    mx = __reduce_max_sync(0xffffffffu, u);
+    seen += __popc(__ballot_sync(0xffffffffu, u == mx));
+    if (seen >= q) break;
+    if (u == mx) u = 0;
+  }
+  return unord32(mx);
+}
+
 // First bin (of kBinsS counts, kBinsS / NT per thread) where the running
 // count reaches target >= 1.
 __device__ Found find_bins(const uint32_t* H, uint32_t target, Shared& sh) {
@@ -1552,17 +1568,16 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
     unsigned long long* out = a.slice_keys + slot * kSliceCap;
     if (kl > 0) {
       // Value bound T: every full warp (32 lanes holding columns) offers the
-      // q-th largest of its lanes' maxima, q = ceil(kl / full warps), and T is
+      // q-th largest of its lanes' maxima, q = ceil(m / full warps), and T is
       // the lowest offer.  Each full warp then has q distinct columns >= T, so
-      // the slice has at least kl, and its top-kl by (value desc, column asc)
+      // the slice has at least m, and its top-m by (value desc, column asc)
       // are all among the columns >= T.
       const int wfull = min(NW, ((n + 3) >> 2) >> 5);
       const uint32_t q = wfull > 0 ? (m + wfull - 1) / static_cast<uint32_t>(wfull) : 33u;
       bool all = q > 32u;
       float tv = -__int_as_float(0x7f800000);
       if (!all) {
-        const float srt = warp_sort_desc(regs_max(x));
-        const float offer = __shfl_sync(0xffffffffu, srt, static_cast<int>(q) - 1);
+        const float offer = warp_qth_max(regs_max(x), q);
         if ((threadIdx.x & 31) == 0 && (threadIdx.x >> 5) < wfull) sh.offer[threadIdx.x >> 5] = offer;
         __syncthreads();
         tv = sh.offer[0];

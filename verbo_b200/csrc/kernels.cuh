@@ -77,7 +77,7 @@ constexpr int kMaxSlices = 32;
 // Top-k slices of rows with >= 2 slices and 32 <= k <= 64 emit only their
 // top-m, m = max(kTopM, ceil(k / (slices - 1))), with their threshold as a
 // certificate the merge checks (kernels.cu, merge_slices_kernel).
-constexpr int kTopM = 24;
+constexpr int kTopM = 16;
 
 // Dense penalty windows: when every row's window (its last repeat_last ids)
 // is at most kWinMax long, a small kernel copies the windows into
