@@ -169,6 +169,21 @@ def test_greedy_nan_first_element():
     ids, _, _ = run_gpu(x, dict(temp=0.0))
     ora, _, _ = run_oracle(x, dict(temp=0.0))
     assert ids[:, 0].tolist() == ora[:, 0].tolist() == [0, 2]
+    # ... also when element 0 (or the maximum) is in the penalty window, for
+    # short rows and for rows long enough for several slices
+    for V in (16, 151936):
+        g = np.random.default_rng(V)
+        x = (g.standard_normal((4, V)) * 2).astype(np.float32)
+        x[0, 0] = np.nan
+        x[1, 0] = np.nan
+        x[2, 7] = 40.0
+        x[3, 0] = 40.0
+        hist = np.array([0, 3, 0, 1, 7, 2, 0, 2], dtype=np.int32)
+        off = np.array([0, 2, 4, 6, 8], dtype=np.int64)
+        for opts in (dict(temp=0.0, repeat=1.5, repeat_last=8), dict(temp=0.0, repeat=0.5, repeat_last=2)):
+            ids, _, _ = run_gpu(x, opts, hist=hist, off=off)
+            ora, _, _ = run_oracle(x, opts, hist=hist, off=off)
+            assert ids[:, 0].tolist() == ora[:, 0].tolist(), (V, opts)
 
 
 def test_history_windows():

@@ -1259,6 +1259,29 @@ __device__ __forceinline__ void mask_set(unsigned long long* pm, int j) {
   const int q = j >> 2;
   atomicOr(&pm[q % NT], 1ull << (4 * (q / NT) + (j & 3)));
 }
+// As mask_set; true for the one call that set the bit (a window may name a
+// column twice).
+__device__ __forceinline__ bool mask_set_first(unsigned long long* pm, int j) {
+  const int q = j >> 2;
+  const unsigned long long bit = 1ull << (4 * (q / NT) + (j & 3));
+  return (atomicOr(&pm[q % NT], bit) & bit) == 0ull;
+}
+// Penalised columns left out of the thread's registers (set to -inf): their
+// penalised values come from the threads that marked them.  Selects only.
+__device__ __forceinline__ void exclude_regs(float4 (&x)[kSplitChunks], unsigned long long m) {
+  if (m == 0) return;
+  const float ninf = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (int i = 0; i < kSplitChunks; ++i) {
+    const uint32_t nib = static_cast<uint32_t>(m >> (4 * i)) & 15u;
+    if (nib) {
+      if (nib & 1u) x[i].x = ninf;
+      if (nib & 2u) x[i].y = ninf;
+      if (nib & 4u) x[i].z = ninf;
+      if (nib & 8u) x[i].w = ninf;
+    }
+  }
+}
 __device__ __forceinline__ bool mask_test(const unsigned long long* pm, int j) {
   const int q = j >> 2;
   return (pm[q % NT] >> (4 * (q / NT) + (j & 3))) & 1ull;
@@ -1441,6 +1464,21 @@ __device__ __forceinline__ unsigned long long to_ckey(unsigned long long d, int 
   return ((d >> 32) << idxbits) | (d & 0xffffffffull);
 }
 
+// Marks in `pm` the columns [g_lo, g_lo + n) named by the row's penalty window
+// read from the CSR history (the last repeat_last ids, src/sampler.cpp:58-64;
+// ids outside the slice mark nothing).  Out of line: the dense-window path is
+// the common one, and this one's 64-bit indexing stays out of its registers.
+__device__ __noinline__ void mark_csr_window(const RowArgs& a, const DevOpts& o, int row, long long g_lo, int n,
+                                             unsigned long long* pm) {
+  const long long h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
+  const long long len = h1 - h0;
+  const long long from = (o.repeat_last > 0 && len > o.repeat_last) ? len - o.repeat_last : 0;
+  for (long long j = h0 + from + threadIdx.x; j < h1; j += NT) {
+    const long long t = static_cast<long long>(a.hist[j]) - g_lo;
+    if (t >= 0 && t < n) mask_set(pm, static_cast<int>(t));
+  }
+}
+
 // Candidates a top-k slice must certainly hold: its whole top-kl, except in
 // rows of C >= 2 slices with 32 <= k <= 64, where the top-m with
 // m = max(kTopM, ceil(k / (C - 1))) suffices: C - 1 full slices give the
@@ -1486,7 +1524,7 @@ __device__ __noinline__ void slice_exact_topk(const RowArgs& a, const DevOpts& o
   });
 }
 
-template <int kMode, bool kPen>
+template <int kMode, bool kPen, int kLZ>
 __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const DevOpts o) {
   const int C = a.cluster;
   const int row = blockIdx.x / C;
@@ -1528,6 +1566,23 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
     load_regs(src, n, x);  // all logits loads in flight before anything else
   }
   if (threadIdx.x == 0) sh.ncand = 0;
+  // Lazy penalty (top-k modes, dense windows of <= NT ids, one per thread):
+  // the thread that marks a column first loads that column's value itself (its
+  // line is already on its way for the owner), penalises it once and supplies
+  // its key; owners only leave their marked columns out, so a warp no longer
+  // runs the penalty's divisions for the few lanes that need them.  The top-k
+  // kernels are issue bound and gain; greedy is bound by memory latency, and
+  // the extra dependent load would lengthen it, so greedy, larger windows and
+  // the CSR path penalise in the owners' registers.
+  constexpr int LZ = kLZ;  // window ids a thread may own on the lazy path (windows of <= LZ * NT)
+  const bool lazy = kPen && kMode != kSplitGreedy && a.win_w > 0 && a.win_w <= LZ * NT;
+  int pj[LZ];       // the columns this thread penalises (lazy), slice-relative, or -1
+  float pv[LZ];     // their values as loaded, then penalised
+#pragma unroll
+  for (int e = 0; e < LZ; ++e) {
+    pj[e] = -1;
+    pv[e] = 0.0f;
+  }
   if (kPen) {
     pm[threadIdx.x] = 0;
     if (a.win_w > 0) cp_async_wait_all();
@@ -1535,22 +1590,38 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
     // the last repeat_last ids of the row's history (src/sampler.cpp:58-64);
     // ids outside [0, vocab) and the -1 padding mark nothing
     if (a.win_w > 0) {
-      for (int j = threadIdx.x; j < a.win_w; j += NT) {
-        const long long t = static_cast<long long>(wids[j]) - g_lo;
-        if (wids[j] >= 0 && t >= 0 && t < n) mask_set(pm, static_cast<int>(t));
+      const int g = static_cast<int>(g_lo);  // global ids fit in int (vocab <= kMaxVocab)
+      if (lazy) {
+#pragma unroll
+        for (int e = 0; e < LZ; ++e) {
+          const int j = threadIdx.x + e * NT;
+          const int id = j < a.win_w ? wids[j] : -1;
+          if (id >= g && id - g < n && mask_set_first(pm, id - g)) {  // -1 padding and ids outside fail
+            pj[e] = id - g;
+            pv[e] = ld_stream1(src + pj[e]);
+          }
+        }
+      } else {
+        for (int j = threadIdx.x; j < a.win_w; j += NT) {
+          const int id = wids[j];
+          if (id >= g && id - g < n) mask_set(pm, id - g);
+        }
       }
     } else {
-      const long long h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
-      const long long len = h1 - h0;
-      const long long from = (o.repeat_last > 0 && len > o.repeat_last) ? len - o.repeat_last : 0;
-      for (long long j = h0 + from + threadIdx.x; j < h1; j += NT) {
-        const long long t = static_cast<long long>(a.hist[j]) - g_lo;
-        if (t >= 0 && t < n) mask_set(pm, static_cast<int>(t));
-      }
+      mark_csr_window(a, o, row, g_lo, n, pm);
     }
   }
   __syncthreads();
-  if (kPen) penalize_regs(x, pm[threadIdx.x], o.repeat);
+  if (kPen) {
+    if (lazy) {
+      exclude_regs(x, pm[threadIdx.x]);
+    } else {
+      penalize_regs(x, pm[threadIdx.x], o.repeat);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < LZ; ++e)
+    if (pj[e] >= 0) pv[e] = penalize(pv[e], o.repeat);
   const long long slot = static_cast<long long>(row) * C + s;
 
   if (kMode == kSplitGreedy) {
@@ -1587,9 +1658,25 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
       // Candidates in one pass: a shared counter hands out the slots (their
       // order is immaterial: the merge selects by key).
       if (all) {
-        if (n <= kSliceCap)
-          for_regs(x, n, [&](float v, int j) { out[atomicAdd(&sh.ncand, 1u)] = dkey(v, static_cast<uint32_t>(g_lo + j)); });
+        if (n <= kSliceCap) {
+          const unsigned long long mine = lazy ? pm[threadIdx.x] : 0ull;
+          for_regs(x, n, [&](float v, int j) {
+            const int q4 = j >> 2;  // owners skip the columns the lazy penalty supplies
+            if (!((mine >> (4 * (q4 / NT) + (j & 3))) & 1ull))
+              out[atomicAdd(&sh.ncand, 1u)] = dkey(v, static_cast<uint32_t>(g_lo + j));
+          });
+#pragma unroll
+          for (int e = 0; e < LZ; ++e)
+            if (pj[e] >= 0) out[atomicAdd(&sh.ncand, 1u)] = dkey(pv[e], static_cast<uint32_t>(g_lo + pj[e]));
+        }
       } else {  // NaN placeholders beyond n never pass v >= tv
+#pragma unroll
+        for (int e = 0; e < LZ; ++e) {
+          if (pj[e] >= 0 && canon(pv[e]) >= tv) {  // (excluded from the owner's registers)
+            const uint32_t p = atomicAdd(&sh.ncand, 1u);
+            if (p < static_cast<uint32_t>(kSliceCap)) out[p] = dkey(pv[e], static_cast<uint32_t>(g_lo + pj[e]));
+          }
+        }
         auto take = [&](float v, int j) {
           if (v >= tv) {
             const uint32_t p = atomicAdd(&sh.ncand, 1u);
@@ -1804,13 +1891,7 @@ __global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const
             if (id >= 0 && t >= 0 && t < n) mask_set(pmk, static_cast<int>(t));
           }
         } else {
-          const long long h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
-          const long long len = h1 - h0;
-          const long long from = (o.repeat_last > 0 && len > o.repeat_last) ? len - o.repeat_last : 0;
-          for (long long j = h0 + from + threadIdx.x; j < h1; j += NT) {
-            const long long t = static_cast<long long>(a.hist[j]) - g_lo;
-            if (t >= 0 && t < n) mask_set(pmk, static_cast<int>(t));
-          }
+          mark_csr_window(a, o, row, g_lo, n, pmk);
         }
       }
       __syncthreads();
@@ -1930,7 +2011,7 @@ __global__ void __launch_bounds__(256) window_kernel(const RowArgs a, const DevO
 
 // CTAs of the split kernel resident at once (SM count x CTAs per SM), looked
 // up once per device and instantiation.
-template <int kMode, bool kPen>
+template <int kMode, bool kPen, int kLZ>
 static cudaError_t split_first_wave(size_t smem, int* out) {
   static std::mutex mu;
   static int cache[64] = {};
@@ -1943,7 +2024,7 @@ static cudaError_t split_first_wave(size_t smem, int* out) {
     int sms = 0, occ = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, split::split_kernel<kMode, kPen>, split::NT, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, split::split_kernel<kMode, kPen, kLZ>, split::NT, smem);
     if (e != cudaSuccess) return e;
     cache[dev] = sms * (occ > 0 ? occ : 1);
   }
@@ -1969,12 +2050,13 @@ static cudaError_t launch_after(void (*k)(P...), int grid, int block, size_t sme
   return cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...);
 }
 
-template <int kMode, bool kPen>
-static cudaError_t launch_split_t(const RowArgs& a0, const DevOpts& o, cudaStream_t s) {
+// kLZ: window ids each thread may penalise lazily (top-k modes; see split_kernel)
+template <int kMode, bool kPen, int kLZ>
+static cudaError_t launch_split_lz(const RowArgs& a0, const DevOpts& o, cudaStream_t s) {
   RowArgs a = a0;
   const bool windows = kPen && a.win_w > 0;
   const size_t sm = (kMode == kSplitGreedy ? 0 : split::kBinsS * 4) + (windows ? a.win_w * 4 : 0);
-  cudaError_t e = split_first_wave<kMode, kPen>(sm, &a.first_wave);
+  cudaError_t e = split_first_wave<kMode, kPen, kLZ>(sm, &a.first_wave);
   if (e != cudaSuccess) return e;
   const int grid = a.rows * a.cluster;
   if (windows && !a.ring_pos) {  // batched streams keep their windows in place
@@ -1982,9 +2064,9 @@ static cudaError_t launch_split_t(const RowArgs& a0, const DevOpts& o, cudaStrea
     split::window_kernel<<<a.rows, 256, 0, s>>>(a, o);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    e = launch_after(split::split_kernel<kMode, kPen>, grid, split::NT, sm, s, a, o);
+    e = launch_after(split::split_kernel<kMode, kPen, kLZ>, grid, split::NT, sm, s, a, o);
   } else {
-    split::split_kernel<kMode, kPen><<<grid, split::NT, sm, s>>>(a, o);
+    split::split_kernel<kMode, kPen, kLZ><<<grid, split::NT, sm, s>>>(a, o);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) return e;
@@ -1992,6 +2074,15 @@ static cudaError_t launch_split_t(const RowArgs& a0, const DevOpts& o, cudaStrea
   if (kMode == kSplitGreedy) return launch_after(split::merge_slices_kernel<kMode>, a.rows, 32, 0, s, a, o);
   return launch_after(split::merge_slices_kernel<kMode>, a.rows, split::NT,
                       static_cast<size_t>(split::kBinsS * 4 + (split::kUnionCap + split::kAugCap) * 8), s, a, o);
+}
+template <int kMode, bool kPen>
+static cudaError_t launch_split_t(const RowArgs& a, const DevOpts& o, cudaStream_t s) {
+  // windows of 257..1024 ids: four per thread on the lazy path (their register
+  // cost would slow the common windows of <= 256 ids)
+  if constexpr (kPen && kMode != kSplitGreedy) {
+    if (a.win_w > split::NT && a.win_w <= 4 * split::NT) return launch_split_lz<kMode, kPen, 4>(a, o, s);
+  }
+  return launch_split_lz<kMode, kPen, 1>(a, o, s);
 }
 cudaError_t launch_split(const RowArgs& a, const DevOpts& o, int mode, cudaStream_t s) {
   switch (mode * 2 + (o.penalize ? 1 : 0)) {
