@@ -1742,7 +1742,11 @@ __global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const
   }
   const uint32_t k = kMode == kSplitEmit ? static_cast<uint32_t>(min(a.cand_k, a.ncols)) : static_cast<uint32_t>(o.k);
   __shared__ uint32_t soff[kMaxSlices + 1];
+  // counts and certificates of the row's slices, loaded together
   const uint32_t ci = threadIdx.x < static_cast<unsigned>(C) ? __ldcg(&a.slice_count[static_cast<long long>(row) * C + threadIdx.x]) : 0u;
+  const float my_thr = threadIdx.x < static_cast<unsigned>(C)
+                           ? __ldcg(&a.slice_thr[static_cast<long long>(row) * C + threadIdx.x])
+                           : -__int_as_float(0x7f800000);
   uint32_t utot;
   const uint32_t cex = block_excl_scan<uint32_t, NT>(ci, sh.ws32, &utot);
   if (threadIdx.x < static_cast<unsigned>(C)) {
@@ -1756,9 +1760,17 @@ __global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const
   const unsigned long long* base = a.slice_keys + static_cast<long long>(row) * C * kSliceCap;
   uint64_t* sel = reinterpret_cast<uint64_t*>(H) + 512;  // H bytes [4 KB, 8 KB); the tail uses [0, 4 KB)
   const bool in_smem = utot <= static_cast<uint32_t>(kUnionCap);
-  if (in_smem) {  // a slice publishes at most kSliceCap == NT keys
-    for (int i = 0; i < C; ++i)
-      if (threadIdx.x < scnt[i]) U[soff[i] + threadIdx.x] = __ldcg(base + static_cast<long long>(i) * kSliceCap + threadIdx.x);
+  if (in_smem) {  // a slice publishes at most kSliceCap == NT keys; 8 slices' loads in flight at once
+    for (int i0 = 0; i0 < C; i0 += 8) {
+      unsigned long long v8[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (i0 + q < C && threadIdx.x < scnt[i0 + q])
+          v8[q] = __ldcg(base + static_cast<long long>(i0 + q) * kSliceCap + threadIdx.x);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (i0 + q < C && threadIdx.x < scnt[i0 + q]) U[soff[i0 + q] + threadIdx.x] = v8[q];
+    }
     __syncthreads();
   }
   uint64_t* cand = sel + kSliceCap;  // the k best, sorted (sel[kSliceCap, 2 kSliceCap))
@@ -1861,8 +1873,7 @@ __global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const
   if (threadIdx.x == 0) nbad = 0;
   if (threadIdx.x < static_cast<unsigned>(C)) isbad[threadIdx.x] = 0;
   __syncthreads();
-  if (threadIdx.x < static_cast<unsigned>(C) &&
-      __ldcg(&a.slice_thr[static_cast<long long>(row) * C + threadIdx.x]) > vk) {
+  if (threadIdx.x < static_cast<unsigned>(C) && my_thr > vk) {
     isbad[threadIdx.x] = 1;
     atomicAdd(&nbad, 1u);
   }
