@@ -81,7 +81,10 @@ struct TailShared {
 // parallel; every sum runs in one thread in the reference's order with
 // correctly rounded fp64 operations, so the result is the reference's
 // whenever the fp64 exp agrees.  pr, q: >= k doubles of shared scratch.
-__device__ void tail_pick(const uint64_t* c, int k, const DevOpts& o, unsigned long long* rng, int* out_id,
+// rng: the row's state, written back (advanced); rng0 / rng1: its words as
+// thread 0 loaded them early, off the critical path.
+__device__ void tail_pick(const uint64_t* c, int k, const DevOpts& o, unsigned long long* rng, unsigned long long rng0,
+                          unsigned long long rng1, int* out_id,
                           verbo_row_stats* st, double* pr, double* q, TailShared* ts) {
   const float mx = dval(c[0]);
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
@@ -135,7 +138,7 @@ __device__ void tail_pick(const uint64_t* c, int k, const DevOpts& o, unsigned l
   }
   double tot = 0.0;
   for (int i = 0; i < keep; ++i) tot = __dadd_rn(tot, pr[i]);
-  unsigned long long s1 = rng[0], s0 = rng[1];
+  unsigned long long s1 = rng0, s0 = rng1;
   const double u = rng_unit(s1, s0);
   rng[0] = s1;
   rng[1] = s0;
@@ -175,6 +178,11 @@ __device__ __forceinline__ uint64_t ckey(float v, uint32_t gid, int idxbits) {
 // ====================================================================== merge
 __global__ void __launch_bounds__(kThreads) merge_kernel(const MergeArgs a, const DevOpts o) {
   const int row = blockIdx.x;
+  unsigned long long rng0 = 0, rng1 = 0;  // read now, used by thread 0 at the draw
+  if (threadIdx.x == 0 && !o.greedy) {
+    rng0 = a.rng[2ll * row];
+    rng1 = a.rng[2ll * row + 1];
+  }
   extern __shared__ __align__(16) unsigned char smem[];
   const int total = a.nshards * a.k;
   const int P = next_pow2(max(total, 2));
@@ -216,7 +224,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const MergeArgs a, cons
     return;
   }
   const int kk = min(o.k, static_cast<int>(valid));
-  tail_pick(cand, kk, o, a.rng + 2ll * row, a.out_ids + row, a.stats ? a.stats + row : nullptr, pr, q, &ts);
+  tail_pick(cand, kk, o, a.rng + 2ll * row, rng0, rng1, a.out_ids + row, a.stats ? a.stats + row : nullptr, pr, q, &ts);
 }
 
 // ================================================================== general
@@ -1721,6 +1729,14 @@ __global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const
   uint32_t* H = reinterpret_cast<uint32_t*>(smem);        // kBinsS counts / fp64 tail scratch
   uint64_t* U = reinterpret_cast<uint64_t*>(H + kBinsS);  // kUnionCap keys
   __shared__ Shared sh;
+  // The row's RNG state is not written by the split grid (and the previous
+  // call's merge finished before this call's first kernel started): read it
+  // before waiting.
+  unsigned long long rng0 = 0, rng1 = 0;
+  if (kMode == kSplitSample && threadIdx.x == 0) {
+    rng0 = a.rng[2ll * row];
+    rng1 = a.rng[2ll * row + 1];
+  }
   grid_wait();  // the split grid's partials (programmatic launch)
   if (kMode == kSplitGreedy) {
     if (threadIdx.x < 32) {
@@ -1958,7 +1974,8 @@ __global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const
     }
   } else {
     double* pr = reinterpret_cast<double*>(H);  // H is free: fp64 scratch of the tail
-    tail_pick(cand, static_cast<int>(k), o, a.rng + 2ll * row, a.out_ids + row, a.stats ? a.stats + row : nullptr, pr,
+    tail_pick(cand, static_cast<int>(k), o, a.rng + 2ll * row, rng0, rng1, a.out_ids + row,
+              a.stats ? a.stats + row : nullptr, pr,
               pr + kSplitMaxK, &sh.tail);
     if (threadIdx.x == 0) ring_append(a, row, a.out_ids[row]);  // written by this thread in tail_pick
   }
