@@ -1722,7 +1722,7 @@ __global__ void __launch_bounds__(NT, 4) split_kernel(const RowArgs a, const Dev
 // Per-row merge of the slices' partial results, launched after split_kernel
 // on the same stream (so it sees every slice's stores; nothing waits).
 template <int kMode>
-__global__ void __launch_bounds__(NT) merge_slices_kernel(const RowArgs a, const DevOpts o) {
+__global__ void __launch_bounds__(NT, 6) merge_slices_kernel(const RowArgs a, const DevOpts o) {
   const int C = a.cluster;
   const int row = blockIdx.x;
   extern __shared__ __align__(16) unsigned char smem[];
