@@ -185,6 +185,33 @@ VERBO_CUDA_API int verbo_cuda_batch_accept(verbo_cuda_batch* b, int stream, cons
 VERBO_CUDA_API int verbo_cuda_batch_step(verbo_cuda_batch* b, const float* logits, int vocab, long long ld,
                                          int* out_ids, verbo_row_stats* stats, void* cuda_stream);
 
+/* ---- logits producer tail ------------------------------------------------
+   The end of Session::Impl::batch (src/session.cpp:163-169): the final
+   RMSNorm of each output row's hidden state (model.norm.weight, eps =
+   rms_norm_eps), the activation quantisation of Session::Impl::act
+   (src/session.cpp:88-103) for quantised heads, and matmul with the LM head
+   (lm_head.weight, or the tied embedding), writing fp32 logits rows straight
+   into a device buffer that verbo_cuda_sample / verbo_cuda_batch_step read.
+   The logits are bit-identical to those of the reference built with its
+   VERBO_SCALAR option; its default SIMD builds sum the same terms in another
+   order.  The reference computes this on the host with no device form. */
+typedef struct verbo_cuda_tail verbo_cuda_tail;
+/* Uploads a head to `device`.  dtype is verbo::DType (include/verbo/verbo.hpp:13):
+   0 F32, 1 Q8, 2 Q4.  q and s are HOST arrays in verbo::Tensor layout
+   (src/kernels.hpp:13-23): F32 vocab x dim floats (s unused, may be NULL);
+   Q8 vocab x dim int8; Q4 vocab x dim/2 bytes (byte i of a 32-block: element i
+   in the low nibble, element i+16 in the high one, each stored as value + 8);
+   s = vocab x dim/32 fp16 scales for Q8/Q4.  norm: dim host floats.  dim must
+   be a multiple of 32 in [32, 16384] (src/model.cpp:108); vocab in [1, 4194304]. */
+VERBO_CUDA_API verbo_cuda_tail* verbo_cuda_tail_new(int dtype, int vocab, int dim, const void* q,
+                                                    const unsigned short* s, const float* norm, float eps,
+                                                    int device);
+VERBO_CUDA_API void verbo_cuda_tail_free(verbo_cuda_tail* t);
+/* n device rows of hidden state (row i at x + i*ldx, dim floats) -> n device
+   rows of logits (row i at logits + i*ld, vocab floats), ordered on `stream`. */
+VERBO_CUDA_API int verbo_cuda_tail_logits(verbo_cuda_tail* t, const float* x, int n, long long ldx, float* logits,
+                                          long long ld, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -84,6 +84,41 @@ int ref_sample_rows(const float* logits, int rows, int vocab, long long ld, cons
                     const long long* hist_off, const oracle_sampling* opts,
                     const unsigned long long* seeds, int steps, int* out_ids, int threads);
 
+/* ---- Logits producer tail (src/session.cpp:163-169) ----------------------
+ *
+ * The final RMSNorm of the last hidden states followed by the LM head:
+ *   x      n rows of `dim` floats, row i at x + i*ldx;
+ *   norm   dim floats (model.norm.weight), eps = rms_norm_eps;
+ *   head   verbo::Tensor layout (src/kernels.hpp:13-23), `vocab` rows:
+ *            dtype 0 (F32)  q = vocab x dim floats, s unused;
+ *            dtype 1 (Q8)   q = vocab x dim int8, s = vocab x dim/32 fp16 bits;
+ *            dtype 2 (Q4)   q = vocab x dim/2 bytes (byte i of a 32-block holds
+ *                           element i in its low nibble and element i+16 in
+ *                           its high nibble, each stored as value + 8), s as Q8;
+ *   out    n rows of `vocab` floats, row i at out + i*ld;
+ *   xq, xs optional: the activations as quant_act leaves them (Q8/Q4 heads),
+ *          n x dim int8 and n x dim/32 float block scales.
+ * dim must be a positive multiple of 32 (src/model.cpp:108).  Returns 0, or -1
+ * on bad arguments. */
+int oracle_logits_tail(int dtype, int vocab, int dim, const void* q, const uint16_t* s, const float* norm,
+                       float eps, const float* x, int n, long long ldx, float* out, long long ld, int8_t* xq,
+                       float* xs);
+
+/* The same through the reference's own rmsnorm, quant_act and matmul
+   (oracle/_ref/libverbo_ref_tail*.so), matmul on a Pool of `threads`. */
+int ref_logits_tail(int dtype, int vocab, int dim, const void* q, const uint16_t* s, const float* norm, float eps,
+                    const float* x, int n, long long ldx, float* out, long long ld, int8_t* xq, float* xs,
+                    int threads);
+
+/* Runs a checkpoint through the reference's Session (oracle/_ref tail
+   harnesses): Model::load(dir, dtype), Session::eval_all(toks[0..n)), n <= 64.
+   Copies out the final hidden rows x (n x dim, before the last rmsnorm), the
+   reference's logits (n x vocab), its head q / s (verbo::Tensor layout, the
+   head's own dtype) and the norm weight.  meta = {dim, vocab, head dtype}; with
+   x_out NULL only meta and eps are filled. */
+int ref_model_tail(const char* dir, int dtype, const int* toks, int n, int threads, int* meta, float* eps_out,
+                   float* x_out, float* logits_out, void* q_out, uint16_t* s_out, float* norm_out);
+
 #ifdef __cplusplus
 }
 #endif

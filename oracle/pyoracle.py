@@ -23,6 +23,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "_build" / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libverbo_ref.so"
+REF_TAIL_LIBS = {"avx2": HERE / "_ref" / "libverbo_ref_tail.so", "scalar": HERE / "_ref" / "libverbo_ref_tail_scalar.so"}
 
 
 class OracleSampling(ctypes.Structure):
@@ -86,6 +87,8 @@ def oracle_lib():
         lib.oracle_sample_rows.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, _P, _P, _P, _P, _P, _P]
         lib.oracle_shard_topk.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, ctypes.c_int,
                                           ctypes.c_int, _P, _P, _P, ctypes.c_int, _P, _P]
+        lib.oracle_logits_tail.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_float, _P,
+                                           ctypes.c_int, ctypes.c_longlong, _P, ctypes.c_longlong, _P, _P]
         lib.oracle_merge_sample.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                             _P, _P, _P, _P]
         _oracle = lib
@@ -182,6 +185,117 @@ def ref_sample_rows(logits: np.ndarray, opts: OracleSampling, seeds: np.ndarray,
     ref_lib().ref_sample_rows(_ptr(logits), rows, vocab, ld, _ptr(h), _ptr(ho), ctypes.byref(opts),
                               _ptr(seeds), steps, _ptr(out), threads)
     return out
+
+
+_ref_tail = {}
+
+
+def ref_tail_available(build: str = "scalar") -> bool:
+    return REF_TAIL_LIBS[build].is_file()
+
+
+def _ref_tail_lib(build: str):
+    if build not in _ref_tail:
+        path = REF_TAIL_LIBS[build]
+        if not path.is_file():
+            raise RuntimeError(f"{path} missing: build it with `make -C oracle ref REF=<verbo checkout>`")
+        lib = ctypes.CDLL(str(path))
+        lib.ref_logits_tail.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_float, _P,
+                                        ctypes.c_int, ctypes.c_longlong, _P, ctypes.c_longlong, _P, _P, ctypes.c_int]
+        lib.ref_model_tail.argtypes = [ctypes.c_char_p, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P, _P,
+                                       _P, _P, _P]
+        _ref_tail[build] = lib
+    return _ref_tail[build]
+
+
+DTYPES = {"f32": 0, "q8": 1, "q4": 2}
+
+
+def _tail_args(dtype, q, s, norm, x):
+    dt = DTYPES[dtype] if isinstance(dtype, str) else int(dtype)
+    q = np.ascontiguousarray(q)
+    norm = np.ascontiguousarray(norm, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    s = None if dt == 0 else np.ascontiguousarray(s, dtype=np.uint16)
+    n, dim = x.shape
+    vocab = q.shape[0]
+    return dt, q, s, norm, x, n, dim, vocab
+
+
+def logits_tail(dtype, q, s, norm, eps, x):
+    """Oracle logits tail: (n, dim) hidden rows -> ((n, vocab) logits, xq, xs).
+
+    `q`/`s` hold the head in verbo::Tensor layout (src/kernels.hpp:13-23):
+    f32 (vocab, dim) floats; q8 (vocab, dim) int8; q4 (vocab, dim/2) uint8;
+    s (vocab, dim/32) fp16 bits as uint16.  xq/xs are None for f32 heads."""
+    dt, q, s, norm, x, n, dim, vocab = _tail_args(dtype, q, s, norm, x)
+    out = np.zeros((n, vocab), dtype=np.float32)
+    xq = np.zeros((n, dim), dtype=np.int8) if dt else None
+    xs = np.zeros((n, dim // 32), dtype=np.float32) if dt else None
+    rc = oracle_lib().oracle_logits_tail(dt, vocab, dim, _ptr(q), _ptr(s), _ptr(norm), eps, _ptr(x), n, dim,
+                                         _ptr(out), vocab, _ptr(xq), _ptr(xs))
+    if rc != 0:
+        raise ValueError("oracle_logits_tail rejected its arguments")
+    return out, xq, xs
+
+
+def ref_logits_tail(dtype, q, s, norm, eps, x, build: str = "scalar", threads: int = 1):
+    """The reference's own tail (rmsnorm, quant_act, matmul) from the `build`
+    ("scalar" = the VERBO_SCALAR option, "avx2" = the default x86 build)."""
+    dt, q, s, norm, x, n, dim, vocab = _tail_args(dtype, q, s, norm, x)
+    out = np.zeros((n, vocab), dtype=np.float32)
+    xq = np.zeros((n, dim), dtype=np.int8) if dt else None
+    xs = np.zeros((n, dim // 32), dtype=np.float32) if dt else None
+    rc = _ref_tail_lib(build).ref_logits_tail(dt, vocab, dim, _ptr(q), _ptr(s), _ptr(norm), eps, _ptr(x), n, dim,
+                                              _ptr(out), vocab, _ptr(xq), _ptr(xs), threads)
+    if rc != 0:
+        raise ValueError("ref_logits_tail rejected its arguments")
+    return out, xq, xs
+
+
+def ref_model_tail(model_dir, dtype, toks, build: str = "scalar", threads: int = 1) -> dict:
+    """Session::eval_all of the reference on a checkpoint directory, with the
+    final hidden rows read from the session: returns x (n, dim), logits
+    (n, vocab), the head (dtype name, q, s), norm and eps."""
+    lib = _ref_tail_lib(build)
+    dt = DTYPES[dtype] if isinstance(dtype, str) else int(dtype)
+    toks = np.ascontiguousarray(toks, dtype=np.int32)
+    meta = np.zeros(3, dtype=np.int32)
+    eps = np.zeros(1, dtype=np.float32)
+    path = str(model_dir).encode()
+    if lib.ref_model_tail(path, dt, None, 0, threads, _ptr(meta), _ptr(eps), None, None, None, None, None) != 0:
+        raise RuntimeError(f"the reference could not load {model_dir}")
+    dim, vocab, hdt = (int(v) for v in meta)
+    n = toks.size
+    x = np.zeros((n, dim), dtype=np.float32)
+    logits = np.zeros((n, vocab), dtype=np.float32)
+    if hdt == 0:
+        q = np.zeros((vocab, dim), dtype=np.float32)
+    elif hdt == 1:
+        q = np.zeros((vocab, dim), dtype=np.int8)
+    else:
+        q = np.zeros((vocab, dim // 2), dtype=np.uint8)
+    sc = np.zeros((vocab, dim // 32), dtype=np.uint16)
+    norm = np.zeros(dim, dtype=np.float32)
+    if lib.ref_model_tail(path, dt, _ptr(toks), n, threads, _ptr(meta), _ptr(eps), _ptr(x), _ptr(logits), _ptr(q),
+                          _ptr(sc), _ptr(norm)) != 0:
+        raise RuntimeError(f"the reference's session failed on {model_dir}")
+    name = {0: "f32", 1: "q8", 2: "q4"}[hdt]
+    return {"x": x, "logits": logits, "dtype": name, "q": q, "s": None if hdt == 0 else sc, "norm": norm,
+            "eps": float(eps[0])}
+
+
+def random_head(dtype: str, vocab: int, dim: int, seed: int = 0):
+    """A seeded head in verbo::Tensor layout with the value ranges the
+    reference's quant_rows produces (src/kernels.cpp:133-175): Q8 codes in
+    [-127, 127], Q4 nibbles in [0, 15], positive fp16 scales."""
+    g = np.random.default_rng(seed)
+    if dtype == "f32":
+        return (g.standard_normal((vocab, dim)) * 0.05).astype(np.float32), None
+    s = (np.abs(g.standard_normal((vocab, dim // 32))) * 0.004 + 1e-4).astype(np.float16).view(np.uint16)
+    if dtype == "q8":
+        return g.integers(-127, 128, size=(vocab, dim), dtype=np.int8), s
+    return g.integers(0, 256, size=(vocab, dim // 2), dtype=np.uint8), s
 
 
 def host_threads() -> int:

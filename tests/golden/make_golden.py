@@ -21,7 +21,14 @@ Writes, next to this script:
                      logits dump layout (cli/main.cpp:174-190: raw fp32 rows),
                      read back through verbo_b200.logits_dump;
 * ``dump_ids.json``  - the ids the reference's Sampler picks from those rows
-                     (2 picks per row) under three option sets.
+                     (2 picks per row) under three option sets;
+* ``tail_models.npz`` - the logits producer tail (src/session.cpp:163-169) on
+                     the reference's two tiny checkpoints: the final hidden
+                     rows read out of a reference Session after eval_all on
+                     the first TAIL_ROWS ids of ref.json, the head and norm
+                     that Model::load built, and the session's logits from the
+                     VERBO_SCALAR build (bit-exact target) and the default
+                     AVX2 build.
 
 The reference's Sampler has no golden vectors of its own for seeded draws
 (its tests check determinism and ranges only, tests/test_core.cpp:454-496),
@@ -53,6 +60,8 @@ DUMP_OPTS = {
 STEPS_SMALL = 3
 STEPS_CFG = 2
 CFG_ROWS = {"c1": 1, "c2": 6, "c3": 6, "c4": 4, "c5": 6}
+TAIL_ROWS = 12
+TAIL_CASES = (("tiny-qwen2", "q8"), ("tiny-llama", "q8"), ("tiny-llama", "f32"))
 
 
 def opts_array(o: dict) -> np.ndarray:
@@ -164,7 +173,27 @@ def main(ref_dir: str) -> None:
         ids = po.ref_sample_rows(back, po.sampling(**opts), seeds, None, None, steps=STEPS_CFG)
         dump["cases"][name] = {"opts": opts, "ids": ids.tolist()}
     (HERE / "dump_ids.json").write_text(json.dumps(dump, indent=1) + "\n")
-    print("wrote", HERE / "small.npz", HERE / "configs.json", HERE / "tiny_qwen2.f32", HERE / "dump_ids.json")
+
+    toks = json.loads((ref_dir / "tests/data/tiny-qwen2/ref.json").read_text())["ids"][:TAIL_ROWS]
+    tail = {"ncases": np.array(len(TAIL_CASES)), "toks": np.array(toks, dtype=np.int32)}
+    for i, (model, dtype) in enumerate(TAIL_CASES):
+        r = po.ref_model_tail(ref_dir / "tests/data" / model, dtype, toks, build="scalar")
+        tail[f"t{i}_name"] = np.array(f"{model}/{dtype}")
+        tail[f"t{i}_dtype"] = np.array(r["dtype"])
+        tail[f"t{i}_eps"] = np.array(r["eps"], dtype=np.float32)
+        tail[f"t{i}_x"] = r["x"]
+        tail[f"t{i}_q"] = r["q"]
+        if r["s"] is not None:
+            tail[f"t{i}_s"] = r["s"]
+        tail[f"t{i}_norm"] = r["norm"]
+        tail[f"t{i}_logits"] = r["logits"]
+        # the AVX2 build's tail on the scalar build's hidden rows (its own
+        # layers round differently, so its session logits are not comparable)
+        tail[f"t{i}_logits_avx2"] = po.ref_logits_tail(r["dtype"], r["q"], r["s"], r["norm"], r["eps"], r["x"],
+                                                       build="avx2")[0]
+    np.savez_compressed(HERE / "tail_models.npz", **tail)
+    print("wrote", HERE / "small.npz", HERE / "configs.json", HERE / "tiny_qwen2.f32", HERE / "dump_ids.json",
+          HERE / "tail_models.npz")
 
 
 if __name__ == "__main__":

@@ -17,6 +17,8 @@ Entry points
 ``shard_topk``      vocab-sharded step 1: a shard's k best (value, global id)
 ``merge_sample``    vocab-sharded step 2: merge shard candidates and draw
 ``seed_states``     per-row xoroshiro128+ states, seeded like Sampler::reset
+``Batch``           B generation streams with device-side RNG states and windows
+``Tail``            the logits producer tail: final RMSNorm + LM head on the device
 """
 from __future__ import annotations
 
@@ -27,7 +29,7 @@ from pathlib import Path
 from typing import Optional, Sequence
 
 __all__ = ["Sampling", "Sampler", "VerboCudaError", "load_library", "sample", "sample_noalloc", "shard_topk", "merge_sample",
-           "seed_states", "check", "version", "ROW_STATS_FIELDS"]
+           "seed_states", "check", "version", "ROW_STATS_FIELDS", "Batch", "Tail"]
 __version__ = "0.1.0"
 
 _HERE = Path(__file__).resolve().parent
@@ -128,6 +130,10 @@ def load_library():
         "verbo_cuda_batch_reset": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_ulonglong, _P]),
         "verbo_cuda_batch_accept": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_int, _P]),
         "verbo_cuda_batch_step": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_longlong, _P, _P, _P]),
+        "verbo_cuda_tail_new": (_P, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_float,
+                                     ctypes.c_int]),
+        "verbo_cuda_tail_free": (None, [_P]),
+        "verbo_cuda_tail_logits": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_longlong, _P, ctypes.c_longlong, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -368,3 +374,65 @@ class Batch:
                                             logits.stride(0), _dptr(out), _dptr(stats), _stream(cuda_stream)))
         return out
 
+
+
+TAIL_DTYPES = {"f32": 0, "q8": 1, "q4": 2}  # verbo::DType (include/verbo/verbo.hpp:13)
+
+
+class Tail:
+    """The logits producer tail of Session::Impl::batch (src/session.cpp:163-169)
+    on the device: final RMSNorm (``norm``, ``eps``) then the LM head.
+
+    ``q``/``s`` are host numpy arrays in verbo::Tensor layout
+    (src/kernels.hpp:13-23): f32 (vocab, dim) float32; q8 (vocab, dim) int8;
+    q4 (vocab, dim/2) uint8; s (vocab, dim/32) fp16 scales (float16 or their
+    uint16 bits).  ``logits`` maps CUDA float32 hidden rows [n, >= dim] to
+    logits rows [n, vocab] (or into ``out``, rows of stride(0) >= vocab)."""
+
+    def __init__(self, dtype, q, s, norm, eps: float, device: int = 0):
+        import numpy as np
+
+        self._lib = load_library()
+        dt = TAIL_DTYPES[dtype] if isinstance(dtype, str) else int(dtype)
+        q = np.ascontiguousarray(q)
+        norm = np.ascontiguousarray(norm, dtype=np.float32)
+        vocab, dim = q.shape[0], norm.shape[0]
+        sp = None
+        if dt != 0:
+            s = np.ascontiguousarray(s)
+            if s.dtype == np.float16:
+                s = s.view(np.uint16)
+            s = np.ascontiguousarray(s, dtype=np.uint16)
+            sp = s.ctypes.data
+        h = self._lib.verbo_cuda_tail_new(dt, int(vocab), int(dim), q.ctypes.data, sp, norm.ctypes.data,
+                                          float(eps), int(device))
+        if not h:
+            raise _err()
+        self._h = h
+        self.dtype, self.vocab, self.dim, self.device = dt, int(vocab), int(dim), int(device)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.verbo_cuda_tail_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def logits(self, x, out=None, stream=None):
+        import torch
+
+        n, cols = x.shape
+        if x.dtype != torch.float32:
+            raise VerboCudaError("hidden rows must be float32")
+        if out is None:
+            out = torch.empty(n, self.vocab, dtype=torch.float32, device=x.device)
+        if out.dtype != torch.float32 or out.shape[0] != n:
+            raise VerboCudaError("out must be float32 with one row per hidden row")
+        _ok(self._lib.verbo_cuda_tail_logits(self._h, _dptr(x, True), n, x.stride(0) if n else cols,
+                                             _dptr(out, True), out.stride(0) if n else self.vocab,
+                                             _stream(stream)))
+        return out

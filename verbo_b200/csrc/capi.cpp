@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "kernels.cuh"
+#include "tail.cuh"
 #include "verbo_cuda.h"
 
 namespace {
@@ -706,6 +707,129 @@ VERBO_CUDA_API int verbo_cuda_batch_step(verbo_cuda_batch* b, const float* logit
           a.ring_len = b->ring_len;
         }
         dispatch_rows(a, o, vocab, s, b->pen ? b->d_win : nullptr, b->win_w);
+        return 0;
+      },
+      -1);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Logits producer tail: the head (weights, zero-padded scales, norm weight)
+// resident on one device, and one scratch buffer per CUDA stream for the
+// quantised activations of a call.
+struct verbo_cuda_tail {
+  vb::TailHead h{};
+  int device = 0;
+  void* d_q = nullptr;
+  uint16_t* d_s = nullptr;
+  float* d_norm = nullptr;
+  std::mutex mu;
+  std::map<cudaStream_t, Scratch> scratch;
+};
+
+namespace {
+
+void tail_release(verbo_cuda_tail* t) {
+  if (!t) return;
+  cudaSetDevice(t->device);
+  for (auto& kv : t->scratch) cudaFree(kv.second.data);
+  cudaFree(t->d_q);
+  cudaFree(t->d_s);
+  cudaFree(t->d_norm);
+  delete t;
+}
+
+}  // namespace
+
+extern "C" {
+
+VERBO_CUDA_API verbo_cuda_tail* verbo_cuda_tail_new(int dtype, int vocab, int dim, const void* q,
+                                                    const unsigned short* s, const float* norm, float eps,
+                                                    int device) {
+  return guard(
+      [&]() -> verbo_cuda_tail* {
+        if (dtype < vb::kTailF32 || dtype > vb::kTailQ4) fail("dtype must be 0 (F32), 1 (Q8) or 2 (Q4)");
+        if (vocab < 1 || vocab > vb::kTailMaxVocab)
+          fail("vocab must be in [1, " + std::to_string(vb::kTailMaxVocab) + "]");
+        if (dim < vb::kTailBlk || dim > vb::kTailMaxDim || dim % vb::kTailBlk)
+          fail("dim must be a multiple of 32 in [32, " + std::to_string(vb::kTailMaxDim) + "]");
+        if (!q || !norm) fail("q and norm must not be NULL");
+        if (dtype != vb::kTailF32 && !s) fail("quantised heads need their scales s");
+        int ndev = 0;
+        cuda_ok(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+        if (device < 0 || device >= ndev) fail("no CUDA device " + std::to_string(device));
+        cuda_ok(cudaSetDevice(device), "cudaSetDevice");
+        auto* t = new verbo_cuda_tail();
+        t->device = device;
+        vb::TailHead& h = t->h;
+        h.dtype = dtype;
+        h.vocab = vocab;
+        h.dim = dim;
+        h.dimp = (dim + vb::kTailChunk - 1) / vb::kTailChunk * vb::kTailChunk;
+        h.nbp = h.dimp / vb::kTailBlk;
+        h.eps = eps;
+        try {
+          const size_t rows = static_cast<size_t>(vocab);
+          const size_t qbytes = dtype == vb::kTailF32 ? rows * dim * 4 : dtype == vb::kTailQ8 ? rows * dim : rows * dim / 2;
+          cuda_ok(cudaMalloc(&t->d_q, qbytes), "cudaMalloc head");
+          cuda_ok(cudaMemcpy(t->d_q, q, qbytes, cudaMemcpyHostToDevice), "upload head");
+          if (dtype != vb::kTailF32) {
+            // one row of scales per vocab id, zero-padded to nbp blocks
+            const int nb = dim / vb::kTailBlk;
+            std::vector<uint16_t> pad(rows * h.nbp, 0);
+            for (size_t r = 0; r < rows; ++r) std::memcpy(&pad[r * h.nbp], s + r * nb, sizeof(uint16_t) * nb);
+            cuda_ok(cudaMalloc(&t->d_s, pad.size() * 2), "cudaMalloc scales");
+            cuda_ok(cudaMemcpy(t->d_s, pad.data(), pad.size() * 2, cudaMemcpyHostToDevice), "upload scales");
+          }
+          cuda_ok(cudaMalloc(&t->d_norm, sizeof(float) * dim), "cudaMalloc norm");
+          cuda_ok(cudaMemcpy(t->d_norm, norm, sizeof(float) * dim, cudaMemcpyHostToDevice), "upload norm");
+        } catch (...) {
+          tail_release(t);
+          throw;
+        }
+        h.q = t->d_q;
+        h.s = t->d_s;
+        h.norm = t->d_norm;
+        return t;
+      },
+      static_cast<verbo_cuda_tail*>(nullptr));
+}
+
+VERBO_CUDA_API void verbo_cuda_tail_free(verbo_cuda_tail* t) { tail_release(t); }
+
+VERBO_CUDA_API int verbo_cuda_tail_logits(verbo_cuda_tail* t, const float* x, int n, long long ldx, float* logits,
+                                          long long ld, void* stream) {
+  return guard(
+      [&]() {
+        if (!t) fail("tail is NULL");
+        if (n < 0) fail("n must be >= 0");
+        if (n == 0) return 0;
+        if (!x || !logits) fail("x and logits must not be NULL");
+        if (ldx < t->h.dim) fail("ldx must be >= dim");
+        if (ld < t->h.vocab) fail("ld must be >= vocab");
+        cuda_ok(cudaSetDevice(t->device), "cudaSetDevice");
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        vb::TailArgs a{};
+        a.x = x;
+        a.ldx = ldx;
+        a.n = n;
+        a.logits = logits;
+        a.ld = ld;
+        const size_t bytes = vb::tail_scratch_bytes(t->h, n);
+        std::lock_guard<std::mutex> lk(t->mu);
+        Scratch& sc = t->scratch[s];
+        if (sc.bytes < bytes) {
+          cuda_ok(cudaStreamSynchronize(s), "stream");  // the old buffer may still be in use
+          const size_t nb = std::max(bytes, 2 * sc.bytes);
+          cudaFree(sc.data);
+          sc.data = nullptr;
+          sc.bytes = 0;
+          cuda_ok(cudaMalloc(&sc.data, nb), "cudaMalloc tail scratch");
+          sc.bytes = nb;
+        }
+        vb::tail_scratch_attach(t->h, n, sc.data, a);
+        cuda_ok(vb::launch_tail(t->h, a, s), "kernel launch");
         return 0;
       },
       -1);
