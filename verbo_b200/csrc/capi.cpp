@@ -405,6 +405,10 @@ VERBO_CUDA_API int verbo_cuda_check(void* stream) {
         cuda_ok(vb::read_status(&st, true, static_cast<cudaStream_t>(stream)), "stream");
         if (st & vb::kErrLoadTimeout) fail("a row load did not complete within the wait limit");
         if (st & vb::kErrSelect) fail("a selection found no element (inconsistent input)");
+        unsigned tst = 0;
+        cuda_ok(vb::tail_read_status(&tst, true), "tail status");
+        if (tst & vb::kErrTailWait) fail("a logits-tail pipeline wait did not complete within the wait limit");
+        if (tst) fail("tail device status " + std::to_string(tst));
         if (st) fail("device status " + std::to_string(st));
         return 0;
       },
@@ -721,8 +725,7 @@ VERBO_CUDA_API int verbo_cuda_batch_step(verbo_cuda_batch* b, const float* logit
 struct verbo_cuda_tail {
   vb::TailHead h{};
   int device = 0;
-  void* d_q = nullptr;
-  uint16_t* d_s = nullptr;
+  void* d_q = nullptr;  // F32: the reference layout; Q8/Q4: the tile-major head
   float* d_norm = nullptr;
   std::mutex mu;
   std::map<cudaStream_t, Scratch> scratch;
@@ -735,7 +738,6 @@ void tail_release(verbo_cuda_tail* t) {
   cudaSetDevice(t->device);
   for (auto& kv : t->scratch) cudaFree(kv.second.data);
   cudaFree(t->d_q);
-  cudaFree(t->d_s);
   cudaFree(t->d_norm);
   delete t;
 }
@@ -767,20 +769,23 @@ VERBO_CUDA_API verbo_cuda_tail* verbo_cuda_tail_new(int dtype, int vocab, int di
         h.vocab = vocab;
         h.dim = dim;
         h.dimp = (dim + vb::kTailChunk - 1) / vb::kTailChunk * vb::kTailChunk;
-        h.nbp = h.dimp / vb::kTailBlk;
+        h.nkc = h.dimp / vb::kTailChunk;
+        h.ntile = (vocab + vb::kTailRows - 1) / vb::kTailRows;
         h.eps = eps;
         try {
-          const size_t rows = static_cast<size_t>(vocab);
-          const size_t qbytes = dtype == vb::kTailF32 ? rows * dim * 4 : dtype == vb::kTailQ8 ? rows * dim : rows * dim / 2;
-          cuda_ok(cudaMalloc(&t->d_q, qbytes), "cudaMalloc head");
-          cuda_ok(cudaMemcpy(t->d_q, q, qbytes, cudaMemcpyHostToDevice), "upload head");
-          if (dtype != vb::kTailF32) {
-            // one row of scales per vocab id, zero-padded to nbp blocks
-            const int nb = dim / vb::kTailBlk;
-            std::vector<uint16_t> pad(rows * h.nbp, 0);
-            for (size_t r = 0; r < rows; ++r) std::memcpy(&pad[r * h.nbp], s + r * nb, sizeof(uint16_t) * nb);
-            cuda_ok(cudaMalloc(&t->d_s, pad.size() * 2), "cudaMalloc scales");
-            cuda_ok(cudaMemcpy(t->d_s, pad.data(), pad.size() * 2, cudaMemcpyHostToDevice), "upload scales");
+          if (dtype == vb::kTailF32) {
+            const size_t qbytes = static_cast<size_t>(vocab) * dim * 4;
+            cuda_ok(cudaMalloc(&t->d_q, qbytes), "cudaMalloc head");
+            cuda_ok(cudaMemcpy(t->d_q, q, qbytes, cudaMemcpyHostToDevice), "upload head");
+            h.q = static_cast<const float*>(t->d_q);
+          } else {
+            // once per head: the tile-major, pre-swizzled form the kernel streams
+            const size_t bytes = vb::tail_tiles_bytes(dtype, vocab, dim);
+            std::vector<unsigned char> packed(bytes);
+            vb::tail_pack_tiles(dtype, vocab, dim, q, s, packed.data());
+            cuda_ok(cudaMalloc(&t->d_q, bytes), "cudaMalloc head");
+            cuda_ok(cudaMemcpy(t->d_q, packed.data(), bytes, cudaMemcpyHostToDevice), "upload head");
+            h.tiles = static_cast<const unsigned char*>(t->d_q);
           }
           cuda_ok(cudaMalloc(&t->d_norm, sizeof(float) * dim), "cudaMalloc norm");
           cuda_ok(cudaMemcpy(t->d_norm, norm, sizeof(float) * dim, cudaMemcpyHostToDevice), "upload norm");
@@ -788,8 +793,6 @@ VERBO_CUDA_API verbo_cuda_tail* verbo_cuda_tail_new(int dtype, int vocab, int di
           tail_release(t);
           throw;
         }
-        h.q = t->d_q;
-        h.s = t->d_s;
         h.norm = t->d_norm;
         return t;
       },

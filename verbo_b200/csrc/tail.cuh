@@ -6,6 +6,21 @@
 // head matmul, writing fp32 logits rows straight into the sampler's input
 // buffer.  Results are bit-identical to the reference's scalar build
 // (VERBO_SCALAR) and follow its rounding step by step.
+//
+// Device layouts (HBM):
+//   quantised head   tile-major: for each tile of kTailRows vocab rows and
+//                    each K chunk of kTailChunk elements, one contiguous block
+//                    of the tile's weight bytes for the chunk (row stride
+//                    kTailChunk for Q8, kTailChunk/2 for Q4, 16-byte units
+//                    XOR-swizzled per row) followed by its fp16 scales (4 per
+//                    row).  Rows past the vocab and K past dim are zeros.  A
+//                    pipeline stage is one bulk copy of such a block.
+//   activations xq   chunk-major: [chunk][token][kTailChunk] int8, 16-byte
+//                    units XOR-swizzled by (token & 7); tokens padded to the
+//                    token tile with zeros.
+//   block scales xs  [chunk][4 blocks][token] fp32, same padding.
+//   F32 head         the reference layout, vocab x dim floats; its
+//                    normalised rows xb are [token][dimp] floats.
 #pragma once
 
 #include <cstddef>
@@ -16,11 +31,11 @@ namespace vb {
 
 constexpr int kTailBlk = 32;        // quantisation block (src/kernels.hpp:11)
 constexpr int kTailChunk = 128;     // K elements of one pipeline stage: 4 blocks
-constexpr int kTailRows = 128;      // vocab rows of one CTA tile (quantised heads)
+constexpr int kTailRows = 128;      // vocab rows of one head tile
 constexpr int kTailThreads = 256;
-constexpr int kTailStages = 4;
 constexpr int kTailMaxDim = 16384;
 constexpr int kTailMaxVocab = 1 << 22;
+constexpr unsigned kErrTailWait = 4u;  // a head-kernel pipeline wait hit its time limit
 
 enum TailDtype { kTailF32 = 0, kTailQ8 = 1, kTailQ4 = 2 };  // verbo::DType values
 
@@ -29,11 +44,12 @@ struct TailHead {
   int dtype;
   int vocab;
   int dim;
-  int dimp;            // dim rounded up to kTailChunk
-  int nbp;             // dimp / kTailBlk: scale blocks per row, zero-padded
-  const void* q;       // reference layout: F32 vocab x dim floats, Q8 vocab x dim int8, Q4 vocab x dim/2 bytes
-  const uint16_t* s;   // Q8/Q4: vocab x nbp fp16 bits (the reference's scales, zero-padded per row)
-  const float* norm;   // dim floats
+  int dimp;                    // dim rounded up to kTailChunk
+  int nkc;                     // dimp / kTailChunk
+  int ntile;                   // vocab tiles of kTailRows
+  const unsigned char* tiles;  // Q8 / Q4: the tile-major head
+  const float* q;              // F32: vocab x dim floats
+  const float* norm;           // dim floats
   float eps;
 };
 
@@ -42,16 +58,26 @@ struct TailArgs {
   const float* x;      // n rows, row i at x + i*ldx
   long long ldx;
   int n;
+  int n_pad;           // n rounded up to the token tile of the head kernel
+  int nt;              // token tile (8, 16, 32 or 64)
   float* logits;       // n rows, row i at logits + i*ld
   long long ld;
-  int8_t* xq;          // scratch: n x dimp quantised activations (Q8/Q4)
-  float* xs;           // scratch: n x nbp block scales (Q8/Q4)
-  float* xb;           // scratch: n x dimp normalised rows (F32)
+  int8_t* xq;          // scratch (Q8/Q4)
+  float* xs;           // scratch (Q8/Q4)
+  float* xb;           // scratch (F32)
 };
 
+// Bytes of the tile-major form of a quantised head, and the packing itself
+// (host memory to host memory) from the reference's Tensor layout.
+size_t tail_tiles_bytes(int dtype, int vocab, int dim);
+void tail_pack_tiles(int dtype, int vocab, int dim, const void* q, const uint16_t* s, unsigned char* out);
+
+int tail_token_tile(const TailHead& h, int n);
 size_t tail_scratch_bytes(const TailHead& h, int n);
 void tail_scratch_attach(const TailHead& h, int n, void* base, TailArgs& a);
 cudaError_t launch_tail(const TailHead& h, const TailArgs& a, cudaStream_t s);
-int tail_kernels_per_call(const TailHead& h);
+// Reads (and optionally clears) the tail kernels' error bits; the caller has
+// synchronised the stream.
+cudaError_t tail_read_status(unsigned* st, bool clear);
 
 }  // namespace vb
