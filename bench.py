@@ -27,6 +27,14 @@ synthetic logits rows.
 --impl reference times only that CPU reference (rank 0; other ranks exit).
 The c5 configuration measures the vocab-sharded form instead: per-rank
 column shard -> shard_topk -> NCCL all-gather of candidates -> merge_sample.
+
+--config tail measures the logits producer tail instead (final RMSNorm + LM
+head, src/session.cpp:163-169) on a Qwen2-0.5B-shaped Q8 head (151936 x 896,
+--head q8|q4|f32), --rows hidden rows per step (default 1: one decode step);
+its roofline is HBM bytes (the head, read once per call, plus the rows in and
+the logits out) over the step's CUDA-event time, and its CPU baseline and
+--impl reference arm are the reference's own rmsnorm + quant_act + matmul
+(AVX2 build, all host threads).
 """
 from __future__ import annotations
 
@@ -56,7 +64,8 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--config", default="c2", choices=sorted(wl.WORKLOADS))
+    p.add_argument("--config", default="c2", choices=sorted(wl.WORKLOADS) + ["tail"])
+    p.add_argument("--head", default="q8", choices=["q8", "q4", "f32"], help="head dtype of --config tail")
     p.add_argument("--rows", type=int, default=0, help="rows per GPU (default: the configuration's)")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--e2e-steps", type=int, default=0, help="steps of the host-buffer measurement (default min(K, 10))")
@@ -470,9 +479,242 @@ def workload_config(w: wl.Workload, rows_per_gpu: int, world: int, ranks=None, *
     return d
 
 
+TAIL_METRIC = "logits rows/s of the final RMSNorm + LM head (V=151936, dim=896); HBM GB/s vs measured peak"
+
+
+def tail_config(tw, rows_per_gpu: int, world: int) -> dict:
+    return {"workload": (f"tail: {rows_per_gpu} hidden rows x {tw.dim} (N(0, {tw.scale}^2)) -> rmsnorm (eps {tw.eps}) "
+                         f"-> {tw.dtype} LM head {tw.vocab} x {tw.dim} -> fp32 logits"),
+            "vocab": tw.vocab, "dim": tw.dim, "head": tw.dtype, "rows_per_gpu": rows_per_gpu,
+            "global_rows": rows_per_gpu * world, "parallelism": f"rows x{world}",
+            "l2": f"the head ({tw.head_bytes() >> 20} MiB) is larger than L2 and is read once per step"}
+
+
+def tail_alg_bytes(tw, R: int) -> int:
+    """Algorithmic bytes of one tail call: the head once, the hidden rows in,
+    the norm weight, the logits out."""
+    return tw.head_bytes() + R * tw.dim * 4 + tw.dim * 4 + R * tw.vocab * 4
+
+
+def tail_traffic(tw, R: int):
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    d = json.loads(path.read_text()).get(f"tail_{tw.dtype}", {})
+    return d.get(f"bytes_per_call_r{R}")
+
+
+def cpu_tail_rate(tw, q, s, norm, x, seconds: float, threads: int):
+    """The reference's AVX2 tail on `x`, repeated within the time budget."""
+    from oracle import pyoracle as po
+
+    kind = "reference" if po.ref_tail_available("avx2") else "port"
+
+    def run():
+        if kind == "reference":
+            po.ref_logits_tail(tw.dtype, q, s, norm, tw.eps, x, build="avx2", threads=threads)
+        else:
+            po.logits_tail(tw.dtype, q, s, norm, tw.eps, x)
+
+    run()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        reps += 1
+        if time.perf_counter() - t0 > seconds or reps >= 1000:
+            break
+    dt = time.perf_counter() - t0
+    return x.shape[0] * reps / dt, kind, threads if kind == "reference" else 1, reps
+
+
+def bench_tail(a, tw, rank: int, world: int, dev):
+    import torch
+    import torch.distributed as dist
+
+    import verbo_b200 as vb
+
+    R = tw.rows
+    q, s, norm = tw.make_head()
+    t = vb.Tail(tw.dtype, q, s, norm, tw.eps, device=dev.index)
+    xh = tw.make_hidden_np(R, seed_offset=rank)
+    x = torch.from_numpy(xh).to(dev)
+    out = torch.empty(R, tw.vocab, dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(i=0):
+        t.logits(x, out=out, stream=stream)
+
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(a.warmup):
+            step()
+        vb.check(stream)
+        graph = None
+        if not a.no_graph:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step()
+        run = (lambda i: graph.replay()) if graph is not None else step
+        clocks = Clocks(torch.cuda.current_device()) if rank == 0 else None
+        if clocks:
+            clocks.start()
+        if clocks and not a.no_soak:
+            t_soak = time.perf_counter()
+            i = 0
+            while time.perf_counter() - t_soak < 1.0:
+                run(i)
+                i += 1
+                if i % 64 == 0:
+                    torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for i in range(a.steps):
+            ev[i][0].record(stream)
+            run(i)
+            ev[i][1].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        if clocks:
+            clocks.stop()
+        vb.check(stream)
+        del graph
+        res = dict(R=R, elapsed_ms=t0.elapsed_time(t1),
+                   launch_ms=sum(s_.elapsed_time(e_) for s_, e_ in ev) / a.steps,
+                   clocks=clocks.summary() if clocks else None, graph=not a.no_graph)
+        if not a.no_e2e:
+            # through the public call with host buffers: hidden rows in, logits out
+            xp = torch.from_numpy(xh).pin_memory()
+            op = torch.empty(R, tw.vocab, dtype=torch.float32).pin_memory()
+            n_e2e = a.e2e_steps or min(a.steps, 10)
+            for _ in range(2):
+                x.copy_(xp, non_blocking=True)
+                step()
+                op.copy_(out, non_blocking=True)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(n_e2e):
+                x.copy_(xp, non_blocking=True)
+                step()
+                op.copy_(out, non_blocking=True)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            vb.check(stream)
+            res.update(e2e_ms=e0.elapsed_time(e1), e2e_steps=n_e2e, h2d=xp.numel() * 4, d2h=op.numel() * 4)
+    red = torch.tensor([res["elapsed_ms"], res["launch_ms"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(red, op=dist.ReduceOp.MAX)
+    res["elapsed_ms"], res["launch_ms"] = red.tolist()
+    host = (q, s, norm, xh) if rank == 0 and world == 1 and not a.no_cpu_baseline else None
+    t.close()
+    return res, host
+
+
+def bench_reference_tail(a, tw, world: int):
+    from oracle import pyoracle as po
+
+    threads = po.host_threads()
+    q, s, norm = tw.make_head()
+    x = tw.make_hidden_np(tw.rows)
+    kind = "reference" if po.ref_tail_available("avx2") else "port"
+
+    def step():
+        if kind == "reference":
+            po.ref_logits_tail(tw.dtype, q, s, norm, tw.eps, x, build="avx2", threads=threads)
+        else:
+            po.logits_tail(tw.dtype, q, s, norm, tw.eps, x)
+
+    for _ in range(a.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        step()
+    dt = time.perf_counter() - t0
+    value = a.steps * tw.rows / dt
+    line = {
+        "metric": TAIL_METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": dt * 1000.0 / a.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "i8/f32", "data": "synthetic", "impl": "reference",
+        "config": tail_config(tw, tw.rows, 1),
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads if kind == "reference" else 1,
+                         "kind": kind, "sample": f"all {tw.rows} rows of the step, the same rows every step"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main_tail(a, rank: int, local_rank: int, world: int):
+    tw = wl.TAIL.with_dtype(a.head)
+    if a.rows:
+        tw = tw.with_rows(a.rows)
+    if a.impl == "reference":
+        if rank == 0:
+            bench_reference_tail(a, tw, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import verbo_b200 as vb
+
+    vb.load_library()  # fails loudly if the CUDA library is missing
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    try:
+        res, host = bench_tail(a, tw, rank, world, dev)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peak()
+    R = res["R"]
+    value = R * world * a.steps / (res["elapsed_ms"] / 1000.0)
+    alg = tail_alg_bytes(tw, R)
+    achieved = alg / (res["launch_ms"] / 1000.0) / 1e9
+    head_kernel = "tail_head_f32_kernel" if tw.dtype == "f32" else "tail_head_q_kernel"
+    line = {
+        "metric": TAIL_METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": res["elapsed_ms"] / a.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32" if tw.dtype == "f32" else "i8/f32",
+        "data": "synthetic", "config": tail_config(tw, R, world),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "traffic": tail_traffic(tw, R),
+                     "kernel": "tail_norm_kernel + " + head_kernel, "alg_bytes_per_launch": alg,
+                     "launch_ms": res["launch_ms"]},
+        "clocks": res["clocks"],
+        "timing": "CUDA graph replay per step" if res.get("graph") else "host launch per step",
+        "gpu_launches": 2 * a.steps * world,
+    }
+    if "e2e_ms" in res:
+        line["e2e"] = {"value": R * world * res["e2e_steps"] / (res["e2e_ms"] / 1000.0), "unit": "rows/s",
+                       "h2d_bytes_per_step": res["h2d"] * world, "d2h_bytes_per_step": res["d2h"] * world}
+    else:
+        line["e2e"] = None
+    if host is not None:
+        from oracle import pyoracle as po
+
+        q, s, norm, xh = host
+        rate, kind, cores, reps = cpu_tail_rate(tw, q, s, norm, xh, a.cpu_seconds, po.host_threads())
+        line["cpu_baseline"] = {"value": rate, "unit": "rows/s", "cores": cores, "kind": kind,
+                                "sample": f"the {xh.shape[0]} rows of the timed step x {reps} passes"}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse_args()
     rank, local_rank, world = dist_env()
+    if a.config == "tail":
+        main_tail(a, rank, local_rank, world)
+        return
     w = wl.WORKLOADS[a.config]
     if a.rows:
         w = w.with_rows(a.rows)

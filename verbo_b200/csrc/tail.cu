@@ -2,9 +2,9 @@
 //
 // tail_norm_kernel      one CTA per hidden row: rmsnorm (src/session.cpp:14-19)
 //                       and, for quantised heads, quant_act (src/kernels.cpp:106),
-//                       written in the head kernel's chunk-major layouts;
+//                       written as the head kernel's activation blocks;
 // tail_head_q_kernel    Q8 / Q4 heads: a producer warp streams tile-major
-//                       head blocks and activation chunks into a ring of
+//                       head blocks (and activation blocks) into a ring of
 //                       shared-memory stages with bulk copies; eight consumer
 //                       warps run one int8 m16n8k32 tensor-core MMA per
 //                       32-element block and apply the block's fp32 scale in
@@ -42,27 +42,39 @@ constexpr int kHeadThreads = (kConsumers + 1) * 32;
 // serial; the CTA then normalises, and each warp quantises one 32-block at a
 // time.  CTAs past the last row write the zero padding of the token tile.
 __global__ void __launch_bounds__(kTailThreads) tail_norm_kernel(TailHead h, TailArgs a) {
-  extern __shared__ __align__(16) float xr[];  // the row, dim floats
+  grid_release();  // the head kernel may start streaming weights; it waits for this grid before the activations
+  extern __shared__ __align__(16) float xr[];  // the row, then the norm weights: 2 x dim floats
+  float* nw = xr + h.dim;
   __shared__ float s_r;
   const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nbp = h.dimp / kTailBlk;
+  const int ncol = a.n_pad / a.nt, ct = row / a.nt, c = row % a.nt;
+  const size_t actb = static_cast<size_t>(a.nt) * (kTailChunk + 16);
   if (row >= a.n) {  // padding token of a quantised head
     for (int b = warp; b < nbp; b += kTailThreads / 32) {
-      const int kc = b >> 2, bi = b & 3;
-      a.xq[(static_cast<size_t>(kc) * a.n_pad + row) * kTailChunk + bi * 32 + lane] = 0;
-      if (lane == 0) a.xs[(static_cast<size_t>(kc) * 4 + bi) * a.n_pad + row] = 0.0f;
+      unsigned char* blk = a.act + (static_cast<size_t>(b >> 2) * ncol + ct) * actb;
+      blk[c * kTailChunk + (b & 3) * 32 + lane] = 0;
+      if (lane == 0) reinterpret_cast<float*>(blk + a.nt * kTailChunk)[(b & 3) * a.nt + c] = 0.0f;
     }
     return;
   }
   const float* x = a.x + static_cast<long long>(row) * a.ldx;
-  for (int i = threadIdx.x; i < h.dim; i += kTailThreads) xr[i] = x[i];
+  for (int i = threadIdx.x; i < h.dim; i += kTailThreads) {
+    xr[i] = x[i];
+    nw[i] = h.norm[i];
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     float ss = 0.0f;
-    for (int i = 0; i < h.dim; i += 32) {  // dim is a multiple of 32
-      float4 v[8];
+    float4 v[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const float4*>(xr + i + 4 * j);
+    for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const float4*>(xr + 4 * j);
+    for (int i = 0; i < h.dim; i += 32) {  // dim is a multiple of 32
+      // the next 32 values load while these 32 are added
+      const int nx = i + 32 < h.dim ? i + 32 : i;
+      float4 w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = *reinterpret_cast<const float4*>(xr + nx + 4 * j);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         ss = __fadd_rn(ss, __fmul_rn(v[j].x, v[j].x));
@@ -70,6 +82,8 @@ __global__ void __launch_bounds__(kTailThreads) tail_norm_kernel(TailHead h, Tai
         ss = __fadd_rn(ss, __fmul_rn(v[j].z, v[j].z));
         ss = __fadd_rn(ss, __fmul_rn(v[j].w, v[j].w));
       }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = w[j];
     }
     s_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(h.dim)), h.eps)));
   }
@@ -77,22 +91,31 @@ __global__ void __launch_bounds__(kTailThreads) tail_norm_kernel(TailHead h, Tai
   const float r = s_r;
   if (h.dtype == kTailF32) {
     for (int i = threadIdx.x; i < h.dimp; i += kTailThreads)
-      a.xb[static_cast<long long>(row) * h.dimp + i] = i < h.dim ? __fmul_rn(h.norm[i], __fmul_rn(xr[i], r)) : 0.0f;
+      a.xb[static_cast<long long>(row) * h.dimp + i] = i < h.dim ? __fmul_rn(nw[i], __fmul_rn(xr[i], r)) : 0.0f;
     return;
   }
-  for (int b = warp; b < nbp; b += kTailThreads / 32) {
-    const int i = b * kTailBlk + lane;
-    const float v = i < h.dim ? __fmul_rn(h.norm[i], __fmul_rn(xr[i], r)) : 0.0f;
-    // std::max(amax, |v|) from 0: a NaN never becomes the maximum
-    const float m = fabsf(v);
-    const float amax = warp_max(m == m ? m : 0.0f);
-    const float d = __fdiv_rn(amax, 127.0f);
-    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    const int kc = b >> 2, bi = b & 3;
-    const int u = (bi * 32 + lane) >> 4;  // 16-byte unit of the chunk row
-    a.xq[(static_cast<size_t>(kc) * a.n_pad + row) * kTailChunk + ((u ^ (row & 7)) << 4) + (lane & 15)] =
-        static_cast<int8_t>(__float2int_rn(__fmul_rn(v, id)));  // NaN -> 0
-    if (lane == 0) a.xs[(static_cast<size_t>(kc) * 4 + bi) * a.n_pad + row] = d;
+  // four blocks per warp at a time, so that their shuffle and division chains overlap
+  constexpr int W = kTailThreads / 32;
+  for (int b0 = warp; b0 < nbp; b0 += 4 * W) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int b = b0 + j * W;
+      if (b < nbp) {
+        const int i = b * kTailBlk + lane;
+        const float v = i < h.dim ? __fmul_rn(nw[i], __fmul_rn(xr[i], r)) : 0.0f;
+        // std::max(amax, |v|) from 0: a NaN never becomes the maximum
+        const float m = fabsf(v);
+        const float amax = warp_max(m == m ? m : 0.0f);
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        const int bi = b & 3;
+        const int u = (bi * 32 + lane) >> 4;  // 16-byte unit of the chunk row
+        unsigned char* blk = a.act + (static_cast<size_t>(b >> 2) * ncol + ct) * actb;
+        blk[c * kTailChunk + ((u ^ (c & 7)) << 4) + (lane & 15)] =
+            static_cast<unsigned char>(static_cast<int8_t>(__float2int_rn(__fmul_rn(v, id))));  // NaN -> 0
+        if (lane == 0) reinterpret_cast<float*>(blk + a.nt * kTailChunk)[bi * a.nt + c] = d;
+      }
+    }
   }
 }
 
@@ -146,22 +169,24 @@ struct HeadCfg {
   static constexpr int WM = kTailRows / WARPS_M;  // vocab rows of one warp
   static constexpr int MI = WM / 16, NI = WN / 8;
   static constexpr int TB = TileBytes<kQ4>::TB;
-  static constexpr int B_OFF = TB;                     // NT x 128 activation bytes
-  static constexpr int XS_OFF = TB + NT * kTailChunk;  // [4 blocks][NT] fp32 scales
-  static constexpr int STAGE = XS_OFF + NT * 16;
+  static constexpr int ACTB = NT * (kTailChunk + 16);  // one activation block: codes + [4][NT] scales
+  static constexpr int STAGE = TB + ACTB;
   static constexpr int STAGES = (110 * 1024) / STAGE > 6 ? 6 : (110 * 1024) / STAGE;
-  static constexpr int OUT_LD = kTailRows + 4;
-  static constexpr int DATA = STAGES * STAGE > NT * OUT_LD * 4 ? STAGES * STAGE : NT * OUT_LD * 4;
+  static constexpr int DATA = STAGES * STAGE;
   static constexpr int SMEM = DATA + 2 * STAGES * 8 + 16;
 };
 
-// One CTA: the kTailRows vocab rows of tile blockIdx.y x NT tokens.  Warp 8
-// (lane 0) fills stage kc % STAGES with one bulk copy of the tile's chunk kc
-// and five of the activations, counted on full[s]; the consumer warps release
-// a stage on empty[s].  Every wait is bounded: on a timeout the kernel records
-// kErrTailWait, stops, waits (bounded) for the copies it issued and returns.
-// blockIdx.x (token tiles) runs fastest, so the CTAs of one weight tile run
-// together and all but the first read it from L2.
+// Persistent: CTA b takes the work items b, b + G, b + 2G, ... of the
+// (head tile, token tile) grid, token tiles fastest, so the CTAs that share a
+// weight tile run together and all but the first read it from L2.  Warp 8
+// (lane 0) keeps one ring of STAGES shared-memory stages full across all of
+// the CTA's items: chunk g goes to stage g % STAGES as one bulk copy of the
+// head block and one of the activation block, counted on full[s]; the
+// consumer warps release a stage on empty[s].  The kernel runs after the norm
+// kernel with programmatic dependent launch: the weights of the first stages
+// are requested before griddepcontrol.wait, the activations after it.  Every
+// wait is bounded: on a timeout the kernel records kErrTailWait, stops, waits
+// (bounded) for the copies it issued and returns.
 template <int NT, bool kQ4>
 __global__ void __launch_bounds__(kHeadThreads, 2) tail_head_q_kernel(TailHead h, TailArgs a) {
   using C = HeadCfg<NT, kQ4>;
@@ -170,8 +195,10 @@ __global__ void __launch_bounds__(kHeadThreads, 2) tail_head_q_kernel(TailHead h
   uint64_t* empty = full + C::STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + C::STAGES);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int col0 = blockIdx.x * NT;
+  const int ncol = a.n_pad / NT;
+  const int items = h.ntile * ncol;
   const int nkc = h.nkc;
+  const int G = gridDim.x;
   if (tid == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -181,52 +208,67 @@ __global__ void __launch_bounds__(kHeadThreads, 2) tail_head_q_kernel(TailHead h
   }
   __syncthreads();
 
-  float2 acc[C::MI][C::NI][2];  // [..][..][0]: row g, tokens 2t, 2t+1; [1]: row g + 8
-#pragma unroll
-  for (int mi = 0; mi < C::MI; ++mi)
-#pragma unroll
-    for (int ni = 0; ni < C::NI; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = make_float2(0.0f, 0.0f);
-
   if (warp == kConsumers) {
     if (lane == 0) {
-      const unsigned char* tile = h.tiles + static_cast<size_t>(blockIdx.y) * nkc * C::TB;
-      int issued = 0;
-      for (int kc = 0; kc < nkc; ++kc) {
-        const int s = kc % C::STAGES;
-        if (kc >= C::STAGES && !mbar_wait_bounded(&empty[s], ((kc / C::STAGES) - 1) & 1)) {
+      const int mine = blockIdx.x < items ? (items - blockIdx.x + G - 1) / G : 0;
+      const int total = mine * nkc;
+      auto stage_of = [&](int g) { return sm + (g % C::STAGES) * C::STAGE; };
+      auto issue_head = [&](int g) {
+        const int j = g / nkc, kc = g - j * nkc;
+        const int tile = (blockIdx.x + j * G) / ncol;
+        mbar_expect_tx(&full[g % C::STAGES], C::STAGE);
+        bulk_g2s_plain(stage_of(g), h.tiles + (static_cast<size_t>(tile) * nkc + kc) * C::TB, C::TB,
+                       &full[g % C::STAGES]);
+      };
+      auto issue_acts = [&](int g) {
+        const int j = g / nkc, kc = g - j * nkc;
+        const int ct = (blockIdx.x + j * G) % ncol;
+        bulk_g2s_plain(stage_of(g) + C::TB, a.act + (static_cast<size_t>(kc) * ncol + ct) * C::ACTB, C::ACTB,
+                       &full[g % C::STAGES]);
+      };
+      const int pre = total < C::STAGES ? total : C::STAGES;
+      for (int g = 0; g < pre; ++g) issue_head(g);
+      grid_wait();  // the norm kernel's activations are complete and visible
+      for (int g = 0; g < pre; ++g) issue_acts(g);
+      int issued = pre;
+      for (int g = pre; g < total; ++g) {
+        if (!mbar_wait_bounded(&empty[g % C::STAGES], ((g / C::STAGES) - 1) & 1)) {
           *abort_flag = 1;
           raise_tail(kErrTailWait);
           break;
         }
         if (*abort_flag) break;
-        unsigned char* st = sm + s * C::STAGE;
-        mbar_expect_tx(&full[s], C::STAGE);
-        bulk_g2s_plain(st, tile + static_cast<size_t>(kc) * C::TB, C::TB, &full[s]);
-        bulk_g2s_plain(st + C::B_OFF, a.xq + (static_cast<size_t>(kc) * a.n_pad + col0) * kTailChunk,
-                       NT * kTailChunk, &full[s]);
-#pragma unroll
-        for (int bi = 0; bi < 4; ++bi)
-          bulk_g2s_plain(st + C::XS_OFF + bi * NT * 4, a.xs + (static_cast<size_t>(kc) * 4 + bi) * a.n_pad + col0,
-                         NT * 4, &full[s]);
+        issue_head(g);
+        issue_acts(g);
         ++issued;
       }
       // no copy may still be in flight when the CTA's shared memory goes away
-      for (int kc = issued > C::STAGES ? issued - C::STAGES : 0; kc < issued; ++kc)
-        (void)mbar_wait_bounded(&full[kc % C::STAGES], (kc / C::STAGES) & 1);
+      for (int g = issued > C::STAGES ? issued - C::STAGES : 0; g < issued; ++g)
+        (void)mbar_wait_bounded(&full[g % C::STAGES], (g / C::STAGES) & 1);
     }
-  } else {
-    const int wm = warp % C::WARPS_M, wn = warp / C::WARPS_M;
-    for (int kc = 0; kc < nkc; ++kc) {
-      const int s = kc % C::STAGES;
-      if (!mbar_wait_bounded(&full[s], (kc / C::STAGES) & 1)) {
+    return;
+  }
+
+  const int wm = warp % C::WARPS_M, wn = warp / C::WARPS_M;
+  int g = 0;
+  for (int it = blockIdx.x; it < items; it += G) {
+    const int tile = it / ncol, col0 = (it % ncol) * NT;
+    float2 acc[C::MI][C::NI][2];  // [..][..][0]: row g, tokens 2t, 2t+1; [1]: row g + 8
+#pragma unroll
+    for (int mi = 0; mi < C::MI; ++mi)
+#pragma unroll
+      for (int ni = 0; ni < C::NI; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = make_float2(0.0f, 0.0f);
+    for (int kc = 0; kc < nkc; ++kc, ++g) {
+      const int s = g % C::STAGES;
+      if (!mbar_wait_bounded(&full[s], (g / C::STAGES) & 1)) {
         *abort_flag = 1;
         raise_tail(kErrTailWait);
-        break;
+        return;
       }
       const unsigned char* A = sm + s * C::STAGE;
       const unsigned char* WS = A + TileBytes<kQ4>::A;
-      const unsigned char* B = A + C::B_OFF;
-      const float* XS = reinterpret_cast<const float*>(A + C::XS_OFF);
+      const unsigned char* B = A + C::TB;
+      const float* XS = reinterpret_cast<const float*>(B + NT * kTailChunk);
       uint2 wraw[C::MI][2];  // 4 fp16 scales of each of my rows
 #pragma unroll
       for (int mi = 0; mi < C::MI; ++mi)
@@ -298,32 +340,23 @@ __global__ void __launch_bounds__(kHeadThreads, 2) tail_head_q_kernel(TailHead h
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
-  }
-  __syncthreads();
-  if (*abort_flag) return;
-
-  // transpose through shared memory: each token's 128 logits leave as one run
-  float* ot = reinterpret_cast<float*>(sm);
-  if (warp < kConsumers) {
-    const int wm = warp % C::WARPS_M, wn = warp / C::WARPS_M;
+    // straight from registers: for each token a warp writes 8 consecutive
+    // logits (one 32-byte sector) per row group
+    const int row0 = tile * kTailRows + wm * C::WM + (lane >> 2);
+    const int c0 = col0 + wn * C::WN + 2 * (lane & 3);
 #pragma unroll
     for (int mi = 0; mi < C::MI; ++mi)
 #pragma unroll
-      for (int ni = 0; ni < C::NI; ++ni) {
-        const int r = wm * C::WM + mi * 16 + (lane >> 2);
-        const int c = wn * C::WN + ni * 8 + 2 * (lane & 3);
-        ot[c * C::OUT_LD + r] = acc[mi][ni][0].x;
-        ot[(c + 1) * C::OUT_LD + r] = acc[mi][ni][0].y;
-        ot[c * C::OUT_LD + r + 8] = acc[mi][ni][1].x;
-        ot[(c + 1) * C::OUT_LD + r + 8] = acc[mi][ni][1].y;
-      }
-  }
-  __syncthreads();
-  const int row0 = blockIdx.y * kTailRows;
-  for (int id = tid; id < NT * kTailRows; id += kHeadThreads) {
-    const int c = id / kTailRows, r = id % kTailRows;
-    if (col0 + c < a.n && row0 + r < h.vocab)
-      a.logits[static_cast<long long>(col0 + c) * a.ld + row0 + r] = ot[c * C::OUT_LD + r];
+      for (int ni = 0; ni < C::NI; ++ni)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int r = row0 + mi * 16 + hh * 8;
+          const int c = c0 + ni * 8;
+          if (r < h.vocab) {
+            if (c < a.n) a.logits[static_cast<long long>(c) * a.ld + r] = acc[mi][ni][hh].x;
+            if (c + 1 < a.n) a.logits[static_cast<long long>(c + 1) * a.ld + r] = acc[mi][ni][hh].y;
+          }
+        }
   }
 }
 
@@ -375,15 +408,30 @@ __global__ void __launch_bounds__(kTailThreads) tail_head_f32_kernel(TailHead h,
 template <int NT, bool kQ4>
 cudaError_t launch_head_q(const TailHead& h, const TailArgs& a, cudaStream_t s) {
   using C = HeadCfg<NT, kQ4>;
-  cudaError_t e =
-      cudaFuncSetAttribute(tail_head_q_kernel<NT, kQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  auto kern = tail_head_q_kernel<NT, kQ4>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(tail_head_q_kernel<NT, kQ4>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                           cudaSharedmemCarveoutMaxShared);
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
-  const dim3 grid(a.n_pad / NT, h.ntile);
-  tail_head_q_kernel<NT, kQ4><<<grid, kHeadThreads, C::SMEM, s>>>(h, a);
-  return cudaGetLastError();
+  int dev = 0, sms = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  // the fewest items per CTA that two CTAs per SM allow, then the fewest CTAs
+  // that carry them: every CTA ends up with the same count, give or take one
+  const int items = h.ntile * (a.n_pad / NT);
+  const int per = (items + 2 * sms - 1) / (2 * sms);
+  const int grid = (items + per - 1) / per;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kHeadThreads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, h, a);
 }
 
 template <bool kQ4>
@@ -448,30 +496,26 @@ int tail_token_tile(const TailHead& h, int n) {
 }
 
 size_t tail_scratch_bytes(const TailHead& h, int n) {
+  if (h.dtype == kTailF32) return align256(static_cast<size_t>(n) * h.dimp * 4);
   const int nt = tail_token_tile(h, n);
   const size_t n_pad = static_cast<size_t>((n + nt - 1) / nt) * nt;
-  if (h.dtype == kTailF32) return align256(static_cast<size_t>(n) * h.dimp * 4);
-  return align256(n_pad * h.dimp) + align256(n_pad * (h.dimp / kTailBlk) * 4);
+  return align256(static_cast<size_t>(h.nkc) * n_pad * (kTailChunk + 16));
 }
 
 void tail_scratch_attach(const TailHead& h, int n, void* base, TailArgs& a) {
-  unsigned char* p = static_cast<unsigned char*>(base);
   a.nt = tail_token_tile(h, n);
   a.n_pad = (n + a.nt - 1) / a.nt * a.nt;
-  a.xq = nullptr;
-  a.xs = nullptr;
+  a.act = nullptr;
   a.xb = nullptr;
-  if (h.dtype == kTailF32) {
-    a.xb = reinterpret_cast<float*>(p);
-    return;
-  }
-  a.xq = reinterpret_cast<int8_t*>(p);
-  a.xs = reinterpret_cast<float*>(p + align256(static_cast<size_t>(a.n_pad) * h.dimp));
+  if (h.dtype == kTailF32)
+    a.xb = static_cast<float*>(base);
+  else
+    a.act = static_cast<unsigned char*>(base);
 }
 
 cudaError_t launch_tail(const TailHead& h, const TailArgs& a, cudaStream_t s) {
   if (a.n <= 0) return cudaSuccess;
-  const int norm_smem = h.dim * 4;
+  const int norm_smem = h.dim * 8;
   cudaError_t e = cudaFuncSetAttribute(tail_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, norm_smem);
   if (e != cudaSuccess) return e;
   tail_norm_kernel<<<h.dtype == kTailF32 ? a.n : a.n_pad, kTailThreads, norm_smem, s>>>(h, a);

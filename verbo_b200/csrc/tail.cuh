@@ -15,10 +15,11 @@
 //                    XOR-swizzled per row) followed by its fp16 scales (4 per
 //                    row).  Rows past the vocab and K past dim are zeros.  A
 //                    pipeline stage is one bulk copy of such a block.
-//   activations xq   chunk-major: [chunk][token][kTailChunk] int8, 16-byte
-//                    units XOR-swizzled by (token & 7); tokens padded to the
-//                    token tile with zeros.
-//   block scales xs  [chunk][4 blocks][token] fp32, same padding.
+//   activations      one block per (K chunk, token tile of nt tokens), chunk
+//                    major: the nt x kTailChunk int8 codes (16-byte units
+//                    XOR-swizzled by (token & 7)) then their block scales as
+//                    [4 blocks][nt] fp32; tokens past n are zeros.  A stage
+//                    takes one such block with one bulk copy.
 //   F32 head         the reference layout, vocab x dim floats; its
 //                    normalised rows xb are [token][dimp] floats.
 #pragma once
@@ -62,8 +63,7 @@ struct TailArgs {
   int nt;              // token tile (8, 16, 32 or 64)
   float* logits;       // n rows, row i at logits + i*ld
   long long ld;
-  int8_t* xq;          // scratch (Q8/Q4)
-  float* xs;           // scratch (Q8/Q4)
+  unsigned char* act;  // scratch (Q8/Q4): the activation blocks
   float* xb;           // scratch (F32)
 };
 

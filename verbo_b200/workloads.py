@@ -130,3 +130,56 @@ def make_hist_torch(w: Workload, rows: int, device, seed_offset: int = 0):
     hist = torch.randint(0, w.vocab, (rows * w.hist_len,), device=device, generator=g, dtype=torch.int32)
     off = torch.arange(rows + 1, device=device, dtype=torch.int64) * w.hist_len
     return hist, off
+
+
+# ------------------------------------------------------------ logits tail --
+@dataclass(frozen=True)
+class TailWorkload:
+    """The logits producer tail (src/session.cpp:163-169) on a Qwen2-0.5B-shaped
+    head: vocab x dim weights in verbo::Tensor layout (src/kernels.hpp:13-23),
+    seeded synthetic values with the ranges the reference's quant_rows gives
+    (Q8 codes in [-127, 127], Q4 nibbles in [0, 15], positive fp16 scales),
+    a norm weight near 1 and hidden rows N(0, scale^2).  The default batch is
+    one row: one decode step of the reference's generate loop."""
+    name: str = "tail"
+    rows: int = 1
+    vocab: int = 151936
+    dim: int = 896
+    dtype: str = "q8"
+    eps: float = 1e-6
+    scale: float = 3.0
+    data_seed: int = 5
+
+    def with_rows(self, rows: int) -> "TailWorkload":
+        return replace(self, rows=rows)
+
+    def with_dtype(self, dtype: str) -> "TailWorkload":
+        return replace(self, dtype=dtype)
+
+    def head_bytes(self) -> int:
+        """Bytes of the head the kernel must read once per call."""
+        if self.dtype == "f32":
+            return self.vocab * self.dim * 4
+        q = self.vocab * self.dim if self.dtype == "q8" else self.vocab * self.dim // 2
+        return q + self.vocab * (self.dim // 32) * 2
+
+    def make_head(self):
+        """(q, s, norm) host arrays of the head."""
+        g = np.random.default_rng(self.data_seed)
+        norm = (1.0 + 0.1 * g.standard_normal(self.dim)).astype(np.float32)
+        if self.dtype == "f32":
+            return (g.standard_normal((self.vocab, self.dim)) * 0.05).astype(np.float32), None, norm
+        s = (np.abs(g.standard_normal((self.vocab, self.dim // 32))) * 0.004 + 1e-4).astype(np.float16)
+        if self.dtype == "q8":
+            q = g.integers(-127, 128, size=(self.vocab, self.dim), dtype=np.int8)
+        else:
+            q = g.integers(0, 256, size=(self.vocab, self.dim // 2), dtype=np.uint8)
+        return q, s.view(np.uint16), norm
+
+    def make_hidden_np(self, rows: Optional[int] = None, seed_offset: int = 0) -> np.ndarray:
+        rows = self.rows if rows is None else rows
+        g = np.random.default_rng(self.data_seed * 1000 + 7 + seed_offset)
+        return (g.standard_normal((rows, self.dim)) * self.scale).astype(np.float32)
+
+
+TAIL = TailWorkload()
