@@ -1729,9 +1729,11 @@ __global__ void __launch_bounds__(NT, 6) merge_slices_kernel(const RowArgs a, co
   uint32_t* H = reinterpret_cast<uint32_t*>(smem);        // kBinsS counts / fp64 tail scratch
   uint64_t* U = reinterpret_cast<uint64_t*>(H + kBinsS);  // kUnionCap keys
   __shared__ Shared sh;
+  // The next call's first kernel may be scheduled now; it waits for this grid.
+  grid_release();
   // The row's RNG state is not written by the split grid (and the previous
-  // call's merge finished before this call's first kernel started): read it
-  // before waiting.
+  // call's merge finished before this call's first kernel went past its
+  // wait): read it before waiting.
   unsigned long long rng0 = 0, rng1 = 0;
   if (kMode == kSplitSample && threadIdx.x == 0) {
     rng0 = a.rng[2ll * row];
@@ -2026,7 +2028,12 @@ namespace split {
 // Copies each row's penalty window (its last repeat_last history ids,
 // src/sampler.cpp:58-64) into win[row][0, win_w), padded with -1.
 __global__ void __launch_bounds__(256) window_kernel(const RowArgs a, const DevOpts o) {
-  grid_release();  // the split grid may start its logits loads meanwhile
+  // Launched with programmatic serialization after whatever precedes it: wait
+  // for that grid (e.g. the previous call's merge, which still reads the
+  // scratch this call rewrites) before anything else, then let the split grid
+  // start its logits loads.
+  grid_wait();
+  grid_release();
   const int row = blockIdx.x;
   const long long h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
   const long long len = h1 - h0;
@@ -2088,9 +2095,9 @@ static cudaError_t launch_split_lz(const RowArgs& a0, const DevOpts& o, cudaStre
   if (e != cudaSuccess) return e;
   const int grid = a.rows * a.cluster;
   if (windows && !a.ring_pos) {  // batched streams keep their windows in place
-    // launched normally: it starts after everything before it on the stream
-    split::window_kernel<<<a.rows, 256, 0, s>>>(a, o);
-    e = cudaGetLastError();
+    // programmatic launch: scheduled while the previous kernel drains, it
+    // waits for it before touching memory
+    e = launch_after(split::window_kernel, a.rows, 256, 0, s, a, o);
     if (e != cudaSuccess) return e;
     e = launch_after(split::split_kernel<kMode, kPen, kLZ>, grid, split::NT, sm, s, a, o);
   } else {

@@ -42,7 +42,11 @@ constexpr int kHeadThreads = (kConsumers + 1) * 32;
 // serial; the CTA then normalises, and each warp quantises one 32-block at a
 // time.  CTAs past the last row write the zero padding of the token tile.
 __global__ void __launch_bounds__(kTailThreads) tail_norm_kernel(TailHead h, TailArgs a) {
-  grid_release();  // the head kernel may start streaming weights; it waits for this grid before the activations
+  // Launched with programmatic serialization: wait for the preceding grid (it
+  // may write x), then let the head kernel start streaming weights; it waits
+  // for this grid before it requests the activations.
+  grid_wait();
+  grid_release();
   extern __shared__ __align__(16) float xr[];  // the row, then the norm weights: 2 x dim floats
   float* nw = xr + h.dim;
   __shared__ float s_r;
@@ -199,6 +203,7 @@ __global__ void __launch_bounds__(kHeadThreads, 2) tail_head_q_kernel(TailHead h
   const int items = h.ntile * ncol;
   const int nkc = h.nkc;
   const int G = gridDim.x;
+  grid_release();  // the next kernel may be scheduled; a programmatic one waits for this grid
   if (tid == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -518,8 +523,17 @@ cudaError_t launch_tail(const TailHead& h, const TailArgs& a, cudaStream_t s) {
   const int norm_smem = h.dim * 8;
   cudaError_t e = cudaFuncSetAttribute(tail_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, norm_smem);
   if (e != cudaSuccess) return e;
-  tail_norm_kernel<<<h.dtype == kTailF32 ? a.n : a.n_pad, kTailThreads, norm_smem, s>>>(h, a);
-  e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(h.dtype == kTailF32 ? a.n : a.n_pad);
+  cfg.blockDim = dim3(kTailThreads);
+  cfg.dynamicSmemBytes = norm_smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, tail_norm_kernel, h, a);
   if (e != cudaSuccess) return e;
   switch (h.dtype) {
     case kTailQ8:
