@@ -66,6 +66,9 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--config", default="c2", choices=sorted(wl.WORKLOADS) + ["tail"])
     p.add_argument("--head", default="q8", choices=["q8", "q4", "f32"], help="head dtype of --config tail")
+    p.add_argument("--shard-head", action="store_true",
+                   help="--config tail: tensor-parallel head (vocab rows split over the ranks), each step "
+                        "tail shard -> shard top-k -> NCCL all-gather -> merge (greedy pick)")
     p.add_argument("--rows", type=int, default=0, help="rows per GPU (default: the configuration's)")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--e2e-steps", type=int, default=0, help="steps of the host-buffer measurement (default min(K, 10))")
@@ -527,12 +530,83 @@ def cpu_tail_rate(tw, q, s, norm, x, seconds: float, threads: int):
     return x.shape[0] * reps / dt, kind, threads if kind == "reference" else 1, reps
 
 
+def bench_tail_sharded(a, tw, rank: int, world: int, dev):
+    """Tensor-parallel head: rank r holds vocab rows shard_bounds(V, N, r) of
+    the head and the same hidden rows; a step is the shard's tail, its top-8
+    candidates, the NCCL all-gather and the merge (greedy), identical ids on
+    every rank.  Host launches per step (the collective stays outside graphs);
+    the CUDA-event window of each step covers the tail shard."""
+    import torch
+    import torch.distributed as dist
+
+    import verbo_b200 as vb
+    from verbo_b200 import sharded
+
+    R = tw.rows
+    q, s, norm = tw.make_head()
+    lo, hi = sharded.shard_bounds(tw.vocab, world, rank)
+    t = vb.Tail(tw.dtype, q[lo:hi], None if s is None else s[lo:hi], norm, tw.eps, device=dev.index)
+    x = torch.from_numpy(tw.make_hidden_np(R)).to(dev)   # the same rows on every rank
+    shard = torch.empty(R, hi - lo, dtype=torch.float32, device=dev)
+    k = 8
+    opts = vb.Sampling(temp=0.0)
+    lv = torch.empty(R, k, dtype=torch.float32, device=dev)
+    li = torch.empty(R, k, dtype=torch.int32, device=dev)
+    cv = torch.empty(world, R, k, dtype=torch.float32, device=dev)
+    ci = torch.empty(world, R, k, dtype=torch.int32, device=dev)
+    out = torch.empty(R, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    ev = []
+
+    def step(timed=False):
+        if timed:
+            e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            e[0].record(stream)
+        t.logits(x, out=shard, stream=stream)
+        if timed:
+            e[1].record(stream)
+            ev.append(e)
+        vb.shard_topk(shard, lo, tw.vocab, opts, k, cand_val=lv, cand_id=li, stream=stream)
+        if world > 1:
+            dist.all_gather_into_tensor(cv, lv)
+            dist.all_gather_into_tensor(ci, li)
+        else:
+            cv[0].copy_(lv)
+            ci[0].copy_(li)
+        vb.merge_sample(cv, ci, tw.vocab, opts, out=out, stream=stream)
+
+    for _ in range(a.warmup):
+        step()
+    vb.check(stream)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(a.steps):
+        step(timed=True)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    vb.check(stream)
+    red = torch.tensor([t0.elapsed_time(t1), sum(s_.elapsed_time(e_) for s_, e_ in ev) / a.steps],
+                       dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(red, op=dist.ReduceOp.MAX)
+    t.close()
+    return dict(R=R, elapsed_ms=red[0].item(), launch_ms=red[1].item(), shard_rows=hi - lo, clocks=None,
+                graph=False), None
+
+
 def bench_tail(a, tw, rank: int, world: int, dev):
     import torch
     import torch.distributed as dist
 
     import verbo_b200 as vb
 
+    if a.shard_head:
+        return bench_tail_sharded(a, tw, rank, world, dev)
     R = tw.rows
     q, s, norm = tw.make_head()
     t = vb.Tail(tw.dtype, q, s, norm, tw.eps, device=dev.index)
@@ -677,22 +751,30 @@ def main_tail(a, rank: int, local_rank: int, world: int):
         return
     peak, peak_kind = measured_peak()
     R = res["R"]
-    value = R * world * a.steps / (res["elapsed_ms"] / 1000.0)
-    alg = tail_alg_bytes(tw, R)
+    sharded_head = "shard_rows" in res
+    value = R * (1 if sharded_head else world) * a.steps / (res["elapsed_ms"] / 1000.0)
+    if sharded_head:  # one rank's share: its head rows, the rows in, its logits out
+        alg = (tw.head_bytes() * res["shard_rows"]) // tw.vocab + R * tw.dim * 4 + tw.dim * 4 + R * res["shard_rows"] * 4
+    else:
+        alg = tail_alg_bytes(tw, R)
     achieved = alg / (res["launch_ms"] / 1000.0) / 1e9
     head_kernel = "tail_head_f32_kernel" if tw.dtype == "f32" else "tail_head_q_kernel"
+    cfg = tail_config(tw, R, 1 if sharded_head else world)
+    if sharded_head:
+        cfg.update(parallelism=f"head vocab shards x{world}", head_rows_per_gpu=res["shard_rows"],
+                   step="tail shard -> shard_topk (k 8) -> NCCL all-gather -> merge_sample (greedy)")
     line = {
         "metric": TAIL_METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": res["elapsed_ms"] / a.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32" if tw.dtype == "f32" else "i8/f32",
-        "data": "synthetic", "config": tail_config(tw, R, world),
+        "scaling": "strong" if sharded_head else "weak", "vs_baseline": None,
+        "dtype": "f32" if tw.dtype == "f32" else "i8/f32", "data": "synthetic", "config": cfg,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "traffic": tail_traffic(tw, R),
                      "kernel": "tail_norm_kernel + " + head_kernel, "alg_bytes_per_launch": alg,
                      "launch_ms": res["launch_ms"]},
         "clocks": res["clocks"],
         "timing": "CUDA graph replay per step" if res.get("graph") else "host launch per step",
-        "gpu_launches": 2 * a.steps * world,
+        "gpu_launches": (5 if sharded_head else 2) * a.steps * world,
     }
     if "e2e_ms" in res:
         line["e2e"] = {"value": R * world * res["e2e_steps"] / (res["e2e_ms"] / 1000.0), "unit": "rows/s",

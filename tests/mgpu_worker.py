@@ -2,8 +2,11 @@
 process per GPU, NCCL).  Every rank builds the same seeded rows, samples its
 column shard through verbo_b200.sharded (shard top-k -> NCCL all-gather ->
 merge), and rank 0 checks the ids against the unsharded CUDA path on the full
-rows; every rank checks that all ranks drew the same ids.  Exit status 0 on
-success."""
+rows; every rank checks that all ranks drew the same ids.  Then the
+tensor-parallel logits tail: each rank holds a vocab shard of a seeded Q8 head,
+turns the same hidden rows into its shard's logits and picks through the same
+sharded merge; rank 0 checks the ids against the full head's tail on one GPU
+followed by the unsharded pick.  Exit status 0 on success."""
 from __future__ import annotations
 
 import os
@@ -51,6 +54,31 @@ def main() -> int:
             ok = ok and torch.equal(want, got)
             print(f"rank0: sharded over {world} GPUs == unsharded: {torch.equal(want, got)}; ranks agree: "
                   f"{all(torch.equal(e, got) for e in every)}", flush=True)
+        # tensor-parallel logits tail: head rows sharded, logits never gathered
+        tv, td = 32000, 896
+        tg = np.random.default_rng(7)
+        tq = tg.integers(-127, 128, size=(tv, td), dtype=np.int8)
+        ts = (np.abs(tg.standard_normal((tv, td // 32))) * 0.004 + 1e-4).astype(np.float16).view(np.uint16)
+        tn = (1 + 0.1 * tg.standard_normal(td)).astype(np.float32)
+        hx = torch.from_numpy((tg.standard_normal((rows, td)) * 3).astype(np.float32)).to(dev)
+        tlo, thi = sharded.shard_bounds(tv, world, rank)
+        tail = vb.Tail("q8", tq[tlo:thi], ts[tlo:thi], tn, 1e-6, device=dev.index)
+        topts = vb.Sampling(temp=0.8, top_k=40, top_p=0.9)
+        trng = torch.from_numpy(st.view(np.int64).copy()).to(dev)
+        tids = torch.stack([sharded.sample_tail_sharded(tail, hx, tlo, tv, topts, 64, trng).clone()
+                            for _ in range(2)])
+        vb.check()
+        tevery = [torch.empty_like(tids) for _ in range(world)]
+        dist.all_gather(tevery, tids)
+        ok = ok and all(torch.equal(e, tids) for e in tevery)
+        if rank == 0:
+            full_tail = vb.Tail("q8", tq, ts, tn, 1e-6, device=dev.index)
+            trng2 = torch.from_numpy(st.view(np.int64).copy()).to(dev)
+            twant = torch.stack([vb.sample(full_tail.logits(hx), topts, rng=trng2).clone() for _ in range(2)])
+            vb.check()
+            tok = torch.equal(twant, tids)
+            ok = ok and tok
+            print(f"rank0: tensor-parallel tail over {world} GPUs == one-GPU tail + pick: {tok}", flush=True)
         flag = torch.tensor([1 if ok else 0], device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         return 0 if flag.item() == 1 else 1

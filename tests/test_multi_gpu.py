@@ -2,7 +2,8 @@
 
 Runs tests/mgpu_worker.py under torch.distributed.run on 2 GPUs (skipped
 with fewer): the sharded ids must equal the unsharded CUDA path's and agree
-on every rank.  The CPU tests of the same host logic (gloo) are in
+on every rank, for column shards of logits rows and for the tensor-parallel
+logits tail (vocab shards of the LM head).  The CPU tests of the same host logic (gloo) are in
 tests/test_distributed.py.
 """
 from __future__ import annotations
@@ -38,3 +39,4 @@ def test_vocab_sharded_over_two_gpus_matches_unsharded(cuda_lib):
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert "== unsharded: True" in r.stdout
+    assert "one-GPU tail + pick: True" in r.stdout

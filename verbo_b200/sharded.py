@@ -11,6 +11,13 @@ shard ``shard_bounds(vocab, world, rank)``, the per-rank candidate buffers
 the same ids.  The global top_k set lies in the union of the shards' top-k
 sets when top_k <= k, so the result equals the unsharded pick.
 
+Tensor-parallel logits tail: with the LM head split by vocab rows (rank r
+holds rows ``shard_bounds(vocab, world, r)``, e.g. ``verbo_b200.Tail`` built
+from that slice of the head), every rank turns the same hidden rows into the
+logits of its own shard only and feeds them to the same sharded pick
+(``sample_tail_sharded``): no rank ever holds a full logits row, and each reads
+1/world of the head.
+
 The collective is the only cross-rank step; ``gather_candidates`` uses the
 process group's timeout, so a rank that died turns into an error on the
 others instead of a hang.
@@ -59,3 +66,15 @@ def sample_vocab_sharded(shard, col_offset: int, vocab: int, opts, k: int, rng, 
     cv, ci = vb.shard_topk(shard, col_offset, vocab, opts, k, hist, hist_off, stream=stream)
     gv, gi = gather_candidates(cv, ci, group)
     return vb.merge_sample(gv, gi, vocab, opts, rng=rng, out=out, stream=stream)
+
+
+def sample_tail_sharded(tail, x, col_offset: int, vocab: int, opts, k: int, rng, hist=None, hist_off=None,
+                        out=None, logits=None, group=None, stream=None):
+    """Tensor-parallel logits tail + pick: `tail` holds the head rows
+    [col_offset, col_offset + tail.vocab) of a vocab sharding of the LM head,
+    `x` the hidden rows (the same on every rank).  This rank's shard of the
+    logits (into `logits` if given) feeds the vocab-sharded pick; returns the
+    ids, identical on every rank."""
+    shard = tail.logits(x, out=logits, stream=stream)
+    return sample_vocab_sharded(shard, col_offset, vocab, opts, k, rng, hist, hist_off, out=out, group=group,
+                                stream=stream)
