@@ -695,6 +695,15 @@ __global__ void __launch_bounds__(kThreads, 2) general_kernel(const RowArgs a, c
       return static_cast<int>(fminf(__fmul_rn(d, inv_w), static_cast<float>(kVBins - 1)));
     };
     // ---- mass pass: S over the k-set; (mass, count) of the min-p set per value bin
+    // The bin masses accumulate as three 16-bit limbs in 32-bit shared counters
+    // (Gv's bytes, zero here) and are folded into Lv->m after the pass: 32-bit
+    // shared atomics are much cheaper than 64-bit ones.  No limb sum overflows:
+    // the two low limbs add < 2^16 per column over a slice of <= 40960
+    // columns, and a mass is < 2^(64 - bitlen(vocab)), so the high limb adds
+    // < 2^(32 - bitlen(vocab)) per column over fewer than 2^bitlen(vocab).
+    uint32_t* lm0 = reinterpret_cast<uint32_t*>(Gv);
+    uint32_t* lm1 = lm0 + kVBins;
+    uint32_t* lm2 = lm1 + kVBins;
     unsigned long long s_local = 0, z_local = 0;
     if (klim == kAll && !(thr > 0.0)) {
       // every column is in the k-set and the min-p set: no keys needed
@@ -709,7 +718,9 @@ __global__ void __launch_bounds__(kThreads, 2) general_kernel(const RowArgs a, c
         s_local += qm;
         const int bi = vbin(vv);
         atomicAdd(&Lv->c[bi], 1u);
-        atomicAdd(&Lv->m[bi], qm);
+        atomicAdd(&lm0[bi], static_cast<uint32_t>(qm & 0xffffu));
+        atomicAdd(&lm1[bi], static_cast<uint32_t>((qm >> 16) & 0xffffu));
+        atomicAdd(&lm2[bi], static_cast<uint32_t>(qm >> 32));
       }
     } else {
       for (int j = threadIdx.x; j < n; j += kThreads) {
@@ -726,8 +737,18 @@ __global__ void __launch_bounds__(kThreads, 2) general_kernel(const RowArgs a, c
         }
         const int bi = vbin(vv);
         atomicAdd(&Lv->c[bi], 1u);
-        atomicAdd(&Lv->m[bi], qm);
+        atomicAdd(&lm0[bi], static_cast<uint32_t>(qm & 0xffffu));
+        atomicAdd(&lm1[bi], static_cast<uint32_t>((qm >> 16) & 0xffffu));
+        atomicAdd(&lm2[bi], static_cast<uint32_t>(qm >> 32));
       }
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < kVBins; b += kThreads) {
+      Lv->m[b] = static_cast<unsigned long long>(lm0[b]) + (static_cast<unsigned long long>(lm1[b]) << 16) +
+                 (static_cast<unsigned long long>(lm2[b]) << 32);
+      lm0[b] = 0u;
+      lm1[b] = 0u;
+      lm2[b] = 0u;
     }
     s_local = block_sum(s_local, sh.ws64);
     z_local = block_sum(z_local, sh.ws64);
