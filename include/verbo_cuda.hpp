@@ -100,5 +100,30 @@ class Batch {
   verbo_cuda_batch* h_ = nullptr;
 };
 
+// The logits producer tail (verbo_cuda_tail_*): the final RMSNorm and LM head
+// of Session::Impl::batch (src/session.cpp:163-169) on the device.  dtype is
+// verbo::DType as an int (0 F32, 1 Q8, 2 Q4); q / s / norm are the host
+// arrays of the loaded model's head Tensor and norm weight.
+class Tail {
+ public:
+  Tail(int dtype, int vocab, int dim, const void* q, const unsigned short* s, const float* norm, float eps,
+       int device = 0) {
+    h_ = verbo_cuda_tail_new(dtype, vocab, dim, q, s, norm, eps, device);
+    if (!h_) throw std::runtime_error(verbo_cuda_last_error());
+  }
+  ~Tail() { verbo_cuda_tail_free(h_); }
+  Tail(const Tail&) = delete;
+  Tail& operator=(const Tail&) = delete;
+
+  // n device rows of hidden state (stride ldx) -> n device rows of logits (stride ld)
+  void logits(const float* d_x, int n, long long ldx, float* d_logits, long long ld, void* cuda_stream = nullptr) {
+    if (verbo_cuda_tail_logits(h_, d_x, n, ldx, d_logits, ld, cuda_stream) < 0)
+      throw std::runtime_error(verbo_cuda_last_error());
+  }
+
+ private:
+  verbo_cuda_tail* h_ = nullptr;
+};
+
 }  // namespace cuda
 }  // namespace verbo
