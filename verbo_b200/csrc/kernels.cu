@@ -600,21 +600,40 @@ __global__ void __launch_bounds__(kThreads, 2) general_kernel(const RowArgs a, c
     }
     __syncthreads();
   }
+  // Every column of the slice once: f(value, column).  The 16-byte aligned
+  // body (from v + h) is read with 16-byte shared loads, 4 consecutive columns
+  // per thread and step; each thread sees its columns in increasing order.
+  // Every pass below is free of visiting order (integer sums, keyed minima,
+  // gathered members sorted later).
+  auto each = [&](auto&& f) {
+    if (static_cast<int>(threadIdx.x) < h) f(v[threadIdx.x], static_cast<int>(threadIdx.x));
+    const float4* v4 = reinterpret_cast<const float4*>(v + h);
+    const int n4 = (n - h) >> 2;
+    for (int q = threadIdx.x; q < n4; q += kThreads) {
+      const float4 t = v4[q];
+      const int j = h + 4 * q;
+      f(t.x, j);
+      f(t.y, j + 1);
+      f(t.z, j + 2);
+      f(t.w, j + 3);
+    }
+    for (int j = h + 4 * n4 + threadIdx.x; j < n; j += kThreads) f(v[j], j);
+  };
   // ---- row maximum (smallest key) across the cluster
   // (float compares: `vj > bv` keeps the lowest column on ties and never
   // takes a NaN; a thread whose columns are all -inf/NaN keeps its first)
   float bv = -__int_as_float(0x7f800000);
-  int bj = -1;
+  int bj = -1, first = -1;
   float lo_f = __int_as_float(0x7f800000);  // smallest finite value
-  for (int j = threadIdx.x; j < n; j += kThreads) {
-    const float vj = v[j];
+  each([&](float vj, int j) {
+    if (first < 0) first = j;
     if (vj > bv) {
       bv = vj;
       bj = j;
     }
     if (vj > -__int_as_float(0x7f800000)) lo_f = fminf(lo_f, vj);  // NaN and -inf fail; +inf kept
-  }
-  if (bj < 0 && static_cast<int>(threadIdx.x) < n) bj = threadIdx.x;
+  });
+  if (bj < 0) bj = first;
   uint64_t best = bj >= 0 ? dkey(bv, static_cast<uint32_t>(g_lo + bj)) : kNoKey;
   best = block_min<unsigned long long>(best, sh.ws64);
   lo_f = block_min<float>(lo_f, reinterpret_cast<float*>(sh.ws64));
@@ -707,13 +726,12 @@ __global__ void __launch_bounds__(kThreads, 2) general_kernel(const RowArgs a, c
     unsigned long long s_local = 0, z_local = 0;
     if (klim == kAll && !(thr > 0.0)) {
       // every column is in the k-set and the min-p set: no keys needed
-      for (int j = threadIdx.x; j < n; j += kThreads) {
-        const float vv = v[j];
+      each([&](float vv, int) {
         double m;
         const unsigned long long qm = fixed_mass(x, vv, &m);
         if (qm == 0) {  // below the fixed-point resolution: counted, never drawn
           ++z_local;
-          continue;
+          return;
         }
         s_local += qm;
         const int bi = vbin(vv);
@@ -721,26 +739,25 @@ __global__ void __launch_bounds__(kThreads, 2) general_kernel(const RowArgs a, c
         atomicAdd(&lm0[bi], static_cast<uint32_t>(qm & 0xffffu));
         atomicAdd(&lm1[bi], static_cast<uint32_t>((qm >> 16) & 0xffffu));
         atomicAdd(&lm2[bi], static_cast<uint32_t>(qm >> 32));
-      }
+      });
     } else {
-      for (int j = threadIdx.x; j < n; j += kThreads) {
-        const float vv = v[j];
+      each([&](float vv, int j) {
         const unsigned long long kc = ckey(vv, static_cast<uint32_t>(g_lo + j), a.idxbits);
-        if (kc > klim) continue;
+        if (kc > klim) return;
         double m;
         const unsigned long long qm = fixed_mass(x, vv, &m);
         s_local += qm;
-        if (!in_pset(x, m, thr, kc)) continue;
+        if (!in_pset(x, m, thr, kc)) return;
         if (qm == 0) {  // below the fixed-point resolution: counted, never drawn
           ++z_local;
-          continue;
+          return;
         }
         const int bi = vbin(vv);
         atomicAdd(&Lv->c[bi], 1u);
         atomicAdd(&lm0[bi], static_cast<uint32_t>(qm & 0xffffu));
         atomicAdd(&lm1[bi], static_cast<uint32_t>((qm >> 16) & 0xffffu));
         atomicAdd(&lm2[bi], static_cast<uint32_t>(qm >> 32));
-      }
+      });
     }
     __syncthreads();
     for (int b = threadIdx.x; b < kVBins; b += kThreads) {
@@ -840,21 +857,20 @@ __global__ void __launch_bounds__(kThreads, 2) general_kernel(const RowArgs a, c
     // copy and walks it.  Returns the member count (or cap + 1 on overflow).
     auto gather = [&](auto pick, unsigned long long* gkey, unsigned long long* gmass, int cap) -> int {
       uint32_t* cnt0 = cl.map_shared_rank(&sh.gcount[gseq++], 0);
-      for (int j = threadIdx.x; j < n; j += kThreads) {
-        const float vv = v[j];
-        if (!pick(vv)) continue;  // (cheap test first; the key only for members)
+      each([&](float vv, int j) {
+        if (!pick(vv)) return;  // (cheap test first; the key only for members)
         const unsigned long long kc = ckey(vv, static_cast<uint32_t>(g_lo + j), a.idxbits);
-        if (kc > klim) continue;
+        if (kc > klim) return;
         double m;
         const unsigned long long qm = fixed_mass(x, vv, &m);
-        if (!in_pset(x, m, thr, kc) || qm == 0) continue;
+        if (!in_pset(x, m, thr, kc) || qm == 0) return;
         const uint32_t p = atomicAdd(cnt0, 1u);
         if (p < static_cast<uint32_t>(cap))
           for (int r = 0; r < C; ++r) {
             *cl.map_shared_rank(&gkey[p], r) = kc;
             *cl.map_shared_rank(&gmass[p], r) = qm;
           }
-      }
+      });
       cluster_sync_all();
       if (threadIdx.x == 0) sh.ng = *cnt0;
       __syncthreads();
@@ -1056,19 +1072,18 @@ __global__ void __launch_bounds__(kThreads, 2) general_kernel(const RowArgs a, c
           Ls->m[b] = 0;
         }
         __syncthreads();
-        for (int j = threadIdx.x; j < n; j += kThreads) {
-          const float vv = v[j];
-          if (vbin(vv) != bd) continue;
+        each([&](float vv, int j) {
+          if (vbin(vv) != bd) return;
           const unsigned long long kc = ckey(vv, static_cast<uint32_t>(g_lo + j), a.idxbits);
-          if (kc > klim) continue;
+          if (kc > klim) return;
           double m;
           const unsigned long long qm = fixed_mass(x, vv, &m);
-          if (!in_pset(x, m, thr, kc) || qm == 0) continue;
+          if (!in_pset(x, m, thr, kc) || qm == 0) return;
           const float tt = __fmul_rn(__fsub_rn(x.M, canon(vv)), inv_w);
           const int sb = min(kVBins - 1, static_cast<int>(__fmul_rn(__fsub_rn(tt, static_cast<float>(bd)), 1024.0f)));
           atomicAdd(&Ls->c[sb], 1u);
           atomicAdd(&Ls->m[sb], qm);
-        }
+        });
         cluster_sync_all();
         unsigned long long s0m = 0, s1m = 0;
         uint32_t s0c = 0, s1c = 0;
