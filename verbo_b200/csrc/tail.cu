@@ -35,6 +35,7 @@ constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
 constexpr int kF32Chunk = 512;          // K floats of the F32 kernel's activation stage
 constexpr int kConsumers = 8;           // consumer warps of the head kernel
 constexpr int kHeadThreads = (kConsumers + 1) * 32;
+constexpr int kL2Ahead = 10;            // head blocks a CTA prefetches into L2 before waiting for the norm
 
 // ---------------------------------------------------------------- norm ----
 // Thread 0 sums the squares in index order (the reference's loop), reading
@@ -146,6 +147,11 @@ __device__ __forceinline__ void bulk_g2s_plain(void* dst_smem, const void* src_g
       "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Bulk prefetch of global memory into L2 (16-byte aligned, bytes a multiple
+// of 16); nothing lands in shared memory and nothing waits for it.
+__device__ __forceinline__ void prefetch_l2(const void* src_gmem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src_gmem), "r"(bytes) : "memory");
+}
 // D = A * B + C over one 32-element block; C = the bits of 1.5 * 2^23, so that
 // D, read as a float, is 1.5 * 2^23 + (block sum): |sum| <= 32 * 127 * 128 < 2^22.
 __device__ __forceinline__ void mma_block(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -233,6 +239,14 @@ __global__ void __launch_bounds__(kHeadThreads, 2) tail_head_q_kernel(TailHead h
       };
       const int pre = total < C::STAGES ? total : C::STAGES;
       for (int g = 0; g < pre; ++g) issue_head(g);
+      // While the norm kernel still runs, pull the next head blocks into L2
+      // too (no shared memory, no completion to wait for): the stages that
+      // follow the wait then read them from L2 and HBM stays busy meanwhile.
+      for (int g = pre; g < total && g < pre + kL2Ahead; ++g) {
+        const int j = g / nkc, kc = g - j * nkc;
+        const int tile = (blockIdx.x + j * G) / ncol;
+        prefetch_l2(h.tiles + (static_cast<size_t>(tile) * nkc + kc) * C::TB, C::TB);
+      }
       grid_wait();  // the norm kernel's activations are complete and visible
       for (int g = 0; g < pre; ++g) issue_acts(g);
       int issued = pre;
