@@ -510,7 +510,7 @@ void tail_pack_tiles(int dtype, int vocab, int dim, const void* q, const uint16_
 }
 
 int tail_token_tile(const TailHead& h, int n) {
-  if (h.dtype == kTailF32) return n <= 8 ? 8 : 16;
+  if (h.dtype == kTailF32) return n <= 2 ? 2 : n <= 4 ? 4 : n <= 8 ? 8 : 16;
   return n <= 8 ? 8 : n <= 16 ? 16 : n <= 32 ? 32 : 64;
 }
 
@@ -555,7 +555,16 @@ cudaError_t launch_tail(const TailHead& h, const TailArgs& a, cudaStream_t s) {
     case kTailQ4:
       return launch_head_q_nt<true>(h, a, s);
     default:
-      return a.nt == 8 ? launch_head_f32<8>(h, a, s) : launch_head_f32<16>(h, a, s);
+      switch (a.nt) {
+        case 2:
+          return launch_head_f32<2>(h, a, s);
+        case 4:
+          return launch_head_f32<4>(h, a, s);
+        case 8:
+          return launch_head_f32<8>(h, a, s);
+        default:
+          return launch_head_f32<16>(h, a, s);
+      }
   }
 }
 

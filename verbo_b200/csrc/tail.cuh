@@ -60,7 +60,7 @@ struct TailArgs {
   long long ldx;
   int n;
   int n_pad;           // n rounded up to the token tile of the head kernel
-  int nt;              // token tile (8, 16, 32 or 64)
+  int nt;              // token tile (quantised heads 8, 16, 32 or 64; F32 heads 2, 4, 8 or 16)
   float* logits;       // n rows, row i at logits + i*ld
   long long ld;
   unsigned char* act;  // scratch (Q8/Q4): the activation blocks
