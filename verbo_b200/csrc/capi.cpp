@@ -725,7 +725,7 @@ VERBO_CUDA_API int verbo_cuda_batch_step(verbo_cuda_batch* b, const float* logit
 struct verbo_cuda_tail {
   vb::TailHead h{};
   int device = 0;
-  void* d_q = nullptr;  // F32: the reference layout; Q8/Q4: the tile-major head
+  void* d_q = nullptr;  // the tile-major head
   float* d_norm = nullptr;
   std::mutex mu;
   std::map<cudaStream_t, Scratch> scratch;
@@ -773,13 +773,8 @@ VERBO_CUDA_API verbo_cuda_tail* verbo_cuda_tail_new(int dtype, int vocab, int di
         h.ntile = (vocab + vb::kTailRows - 1) / vb::kTailRows;
         h.eps = eps;
         try {
-          if (dtype == vb::kTailF32) {
-            const size_t qbytes = static_cast<size_t>(vocab) * dim * 4;
-            cuda_ok(cudaMalloc(&t->d_q, qbytes), "cudaMalloc head");
-            cuda_ok(cudaMemcpy(t->d_q, q, qbytes, cudaMemcpyHostToDevice), "upload head");
-            h.q = static_cast<const float*>(t->d_q);
-          } else {
-            // once per head: the tile-major, pre-swizzled form the kernel streams
+          {
+            // once per head: the tile-major, pre-swizzled form the kernels stream
             const size_t bytes = vb::tail_tiles_bytes(dtype, vocab, dim);
             std::vector<unsigned char> packed(bytes);
             vb::tail_pack_tiles(dtype, vocab, dim, q, s, packed.data());

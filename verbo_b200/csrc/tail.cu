@@ -10,7 +10,8 @@
 //                       32-element block and apply the block's fp32 scale in
 //                       that MMA's epilogue (dot_q8 / dot_q4,
 //                       src/kernels.cpp:576-600);
-// tail_head_f32_kernel  F32 heads: one vocab row per thread (dot_f32,
+// tail_head_f32_kernel  F32 heads: the same ring over a tile-major fp32 head,
+//                       one vocab row per consumer thread (dot_f32,
 //                       src/kernels.cpp:570-574).
 //
 // Every rounding step is the reference scalar build's, in its order: the sum
@@ -32,7 +33,6 @@ __device__ unsigned int g_tail_status;
 
 constexpr int kMagicBits = 0x4B400000;  // bits of 1.5 * 2^23
 constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
-constexpr int kF32Chunk = 512;          // K floats of the F32 kernel's activation stage
 constexpr int kConsumers = 8;           // consumer warps of the head kernel
 constexpr int kHeadThreads = (kConsumers + 1) * 32;
 constexpr int kL2Ahead = 10;            // head blocks a CTA prefetches into L2 before waiting for the norm
@@ -55,6 +55,11 @@ __global__ void __launch_bounds__(kTailThreads) tail_norm_kernel(TailHead h, Tai
   const int nbp = h.dimp / kTailBlk;
   const int ncol = a.n_pad / a.nt, ct = row / a.nt, c = row % a.nt;
   const size_t actb = static_cast<size_t>(a.nt) * (kTailChunk + 16);
+  if (row >= a.n && h.dtype == kTailF32) {  // padding token of an fp32 head
+    for (int i = threadIdx.x; i < h.dim; i += kTailThreads)
+      a.xb[((static_cast<size_t>(i >> 5) * ncol + ct) * 32 + (i & 31)) * a.nt + c] = 0.0f;
+    return;
+  }
   if (row >= a.n) {  // padding token of a quantised head
     for (int b = warp; b < nbp; b += kTailThreads / 32) {
       unsigned char* blk = a.act + (static_cast<size_t>(b >> 2) * ncol + ct) * actb;
@@ -94,9 +99,10 @@ __global__ void __launch_bounds__(kTailThreads) tail_norm_kernel(TailHead h, Tai
   }
   __syncthreads();
   const float r = s_r;
-  if (h.dtype == kTailF32) {
-    for (int i = threadIdx.x; i < h.dimp; i += kTailThreads)
-      a.xb[static_cast<long long>(row) * h.dimp + i] = i < h.dim ? __fmul_rn(nw[i], __fmul_rn(xr[i], r)) : 0.0f;
+  if (h.dtype == kTailF32) {  // activation blocks [dim / 32][token tiles][32][nt]
+    for (int i = threadIdx.x; i < h.dim; i += kTailThreads)
+      a.xb[((static_cast<size_t>(i >> 5) * ncol + ct) * 32 + (i & 31)) * a.nt + c] =
+          __fmul_rn(nw[i], __fmul_rn(xr[i], r));
     return;
   }
   // four blocks per warp at a time, so that their shuffle and division chains overlap
@@ -380,47 +386,137 @@ __global__ void __launch_bounds__(kHeadThreads, 2) tail_head_q_kernel(TailHead h
 }
 
 // ------------------------------------------------------------ F32 head ----
-// One vocab row per thread, NT tokens per CTA, the activations staged k-major
-// so that a token pair is one float2; per (row, token) the products are added
-// in index order, each rounded, as the reference's dot_f32.  Scalar
-// __fmul_rn / __fadd_rn: the packed float2 forms are fused into one FFMA2 by
-// the compiler, which the reference's separate roundings forbid.
+// The same persistent ring as the quantised heads, for an fp32 head packed
+// tile-major (kTailRows rows x kF32K floats per 16 KB block, 16-byte units
+// XOR-swizzled by (row & 7)): a producer warp streams each block and the
+// matching activation block ([kF32K][NT] floats from the norm kernel) with
+// bulk copies; four consumer warps hold one vocab row per thread and NT
+// tokens, and add the products in index order, each rounded, as the
+// reference's dot_f32.  Scalar __fmul_rn / __fadd_rn: the packed float2 forms
+// are fused into one FFMA2 by the compiler, which the reference's separate
+// roundings forbid.
+constexpr int kF32K = 32;                                  // K floats per block
+constexpr int kF32Block = kTailRows * kF32K * 4;           // 16 KB
+constexpr int kF32Consumers = kTailRows / 32;              // one row per consumer thread
+constexpr int kF32Threads = (kF32Consumers + 1) * 32;
+
 template <int NT>
-__global__ void __launch_bounds__(kTailThreads) tail_head_f32_kernel(TailHead h, TailArgs a) {
-  __shared__ __align__(16) float xt[kF32Chunk][NT];
-  const int row = blockIdx.y * kTailThreads + threadIdx.x;
-  const int col0 = blockIdx.x * NT;
-  const float* w = h.q + static_cast<size_t>(min(row, h.vocab - 1)) * h.dim;
-  float2 acc[NT / 2];
-#pragma unroll
-  for (int j = 0; j < NT / 2; ++j) acc[j] = make_float2(0.0f, 0.0f);
-  for (int k0 = 0; k0 < h.dim; k0 += kF32Chunk) {
-    const int len = min(kF32Chunk, h.dim - k0);  // a multiple of 32
-    __syncthreads();
-    for (int id = threadIdx.x; id < NT * len; id += kTailThreads) {
-      const int c = id / len, k = id % len;
-      xt[k][c] = col0 + c < a.n ? a.xb[static_cast<long long>(col0 + c) * h.dimp + k0 + k] : 0.0f;
+struct F32Cfg {
+  static constexpr int XB = kF32K * NT * 4;  // one activation block
+  static constexpr int STAGE = kF32Block + XB;
+  static constexpr int STAGES = (110 * 1024) / STAGE > 6 ? 6 : (110 * 1024) / STAGE;
+  static constexpr int DATA = STAGES * STAGE;
+  static constexpr int SMEM = DATA + 2 * STAGES * 8 + 16;
+};
+
+template <int NT>
+__global__ void __launch_bounds__(kF32Threads, 2) tail_head_f32_kernel(TailHead h, TailArgs a) {
+  using C = F32Cfg<NT>;
+  extern __shared__ __align__(128) unsigned char sm[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::DATA);
+  uint64_t* empty = full + C::STAGES;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + C::STAGES);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ncol = a.n_pad / NT;
+  const int items = h.ntile * ncol;
+  const int nk = h.dim / kF32K;
+  const int G = gridDim.x;
+  grid_release();  // the next kernel may be scheduled; a programmatic one waits for this grid
+  if (tid == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kF32Consumers);
     }
-    __syncthreads();
-    for (int k = 0; k < len; k += 4) {
-      const float4 wv = *reinterpret_cast<const float4*>(w + k0 + k);
-      const float we[4] = {wv.x, wv.y, wv.z, wv.w};
+    *abort_flag = 0;
+  }
+  __syncthreads();
+
+  if (warp == kF32Consumers) {
+    if (lane == 0) {
+      const int mine = blockIdx.x < items ? (items - blockIdx.x + G - 1) / G : 0;
+      const int total = mine * nk;
+      auto stage_of = [&](int g) { return sm + (g % C::STAGES) * C::STAGE; };
+      auto block_of = [&](int g) {
+        const int j = g / nk, kc = g - j * nk;
+        const int tile = (blockIdx.x + j * G) / ncol;
+        return h.tiles + (static_cast<size_t>(tile) * nk + kc) * kF32Block;
+      };
+      auto issue_head = [&](int g) {
+        mbar_expect_tx(&full[g % C::STAGES], C::STAGE);
+        bulk_g2s_plain(stage_of(g), block_of(g), kF32Block, &full[g % C::STAGES]);
+      };
+      auto issue_acts = [&](int g) {
+        const int j = g / nk, kc = g - j * nk;
+        const int ct = (blockIdx.x + j * G) % ncol;
+        bulk_g2s_plain(stage_of(g) + kF32Block,
+                       reinterpret_cast<const unsigned char*>(a.xb) + (static_cast<size_t>(kc) * ncol + ct) * C::XB,
+                       C::XB, &full[g % C::STAGES]);
+      };
+      const int pre = total < C::STAGES ? total : C::STAGES;
+      for (int g = 0; g < pre; ++g) issue_head(g);
+      for (int g = pre; g < total && g < pre + kL2Ahead; ++g) prefetch_l2(block_of(g), kF32Block);
+      grid_wait();  // the norm kernel's activations are complete and visible
+      for (int g = 0; g < pre; ++g) issue_acts(g);
+      int issued = pre;
+      for (int g = pre; g < total; ++g) {
+        if (!mbar_wait_bounded(&empty[g % C::STAGES], ((g / C::STAGES) - 1) & 1)) {
+          *abort_flag = 1;
+          raise_tail(kErrTailWait);
+          break;
+        }
+        if (*abort_flag) break;
+        issue_head(g);
+        issue_acts(g);
+        ++issued;
+      }
+      // no copy may still be in flight when the CTA's shared memory goes away
+      for (int g = issued > C::STAGES ? issued - C::STAGES : 0; g < issued; ++g)
+        (void)mbar_wait_bounded(&full[g % C::STAGES], (g / C::STAGES) & 1);
+    }
+    return;
+  }
+
+  const int r = tid;  // this thread's row of the tile
+  int g = 0;
+  for (int it = blockIdx.x; it < items; it += G) {
+    const int tile = it / ncol, col0 = (it % ncol) * NT;
+    float2 acc[NT / 2];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+    for (int j = 0; j < NT / 2; ++j) acc[j] = make_float2(0.0f, 0.0f);
+    for (int kc = 0; kc < nk; ++kc, ++g) {
+      const int s = g % C::STAGES;
+      if (!mbar_wait_bounded(&full[s], (g / C::STAGES) & 1)) {
+        *abort_flag = 1;
+        raise_tail(kErrTailWait);
+        return;
+      }
+      const unsigned char* W = sm + s * C::STAGE;
+      const float* X = reinterpret_cast<const float*>(W + kF32Block);  // [kF32K][NT]
 #pragma unroll
-        for (int j = 0; j < NT / 2; ++j) {
-          const float2 xv = *reinterpret_cast<const float2*>(&xt[k + e][2 * j]);
-          acc[j].x = __fadd_rn(acc[j].x, __fmul_rn(we[e], xv.x));
-          acc[j].y = __fadd_rn(acc[j].y, __fmul_rn(we[e], xv.y));
+      for (int u = 0; u < kF32K / 4; ++u) {
+        const float4 wv = *reinterpret_cast<const float4*>(W + r * (kF32K * 4) + ((u ^ (r & 7)) << 4));
+        const float we[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+#pragma unroll
+          for (int j = 0; j < NT / 2; ++j) {
+            const float2 xv = *reinterpret_cast<const float2*>(X + (4 * u + e) * NT + 2 * j);
+            acc[j].x = __fadd_rn(acc[j].x, __fmul_rn(we[e], xv.x));
+            acc[j].y = __fadd_rn(acc[j].y, __fmul_rn(we[e], xv.y));
+          }
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
-  }
-  if (row >= h.vocab) return;
+    const int row = tile * kTailRows + r;
+    if (row < h.vocab) {
 #pragma unroll
-  for (int j = 0; j < NT / 2; ++j) {
-    if (col0 + 2 * j < a.n) a.logits[static_cast<long long>(col0 + 2 * j) * a.ld + row] = acc[j].x;
-    if (col0 + 2 * j + 1 < a.n) a.logits[static_cast<long long>(col0 + 2 * j + 1) * a.ld + row] = acc[j].y;
+      for (int j = 0; j < NT / 2; ++j) {
+        if (col0 + 2 * j < a.n) a.logits[static_cast<long long>(col0 + 2 * j) * a.ld + row] = acc[j].x;
+        if (col0 + 2 * j + 1 < a.n) a.logits[static_cast<long long>(col0 + 2 * j + 1) * a.ld + row] = acc[j].y;
+      }
+    }
   }
 }
 
@@ -469,9 +565,29 @@ cudaError_t launch_head_q_nt(const TailHead& h, const TailArgs& a, cudaStream_t 
 
 template <int NT>
 cudaError_t launch_head_f32(const TailHead& h, const TailArgs& a, cudaStream_t s) {
-  const dim3 grid((a.n + NT - 1) / NT, (h.vocab + kTailThreads - 1) / kTailThreads);
-  tail_head_f32_kernel<NT><<<grid, kTailThreads, 0, s>>>(h, a);
-  return cudaGetLastError();
+  using C = F32Cfg<NT>;
+  auto kern = tail_head_f32_kernel<NT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  const int items = h.ntile * (a.n_pad / NT);
+  const int per = (items + 2 * sms - 1) / (2 * sms);
+  const int grid = (items + per - 1) / per;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kF32Threads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, h, a);
 }
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -480,11 +596,26 @@ size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 size_t tail_tiles_bytes(int dtype, int vocab, int dim) {
   const size_t ntile = (vocab + kTailRows - 1) / kTailRows;
+  if (dtype == kTailF32) return ntile * (dim / kF32K) * kF32Block;
   const size_t nkc = (dim + kTailChunk - 1) / kTailChunk;
   return ntile * nkc * (dtype == kTailQ4 ? TileBytes<true>::TB : TileBytes<false>::TB);
 }
 
 void tail_pack_tiles(int dtype, int vocab, int dim, const void* q, const uint16_t* s, unsigned char* out) {
+  if (dtype == kTailF32) {  // blocks of kTailRows rows x kF32K floats, 16-byte units swizzled by (row & 7)
+    const int ntile = (vocab + kTailRows - 1) / kTailRows, nk = dim / kF32K;
+    std::memset(out, 0, tail_tiles_bytes(dtype, vocab, dim));
+    const unsigned char* src = static_cast<const unsigned char*>(q);
+    for (int t = 0; t < ntile; ++t)
+      for (int kc = 0; kc < nk; ++kc) {
+        unsigned char* blk = out + (static_cast<size_t>(t) * nk + kc) * kF32Block;
+        for (int r = 0; r < kTailRows && t * kTailRows + r < vocab; ++r) {
+          const unsigned char* row = src + (static_cast<size_t>(t) * kTailRows + r) * dim * 4 + kc * kF32K * 4;
+          for (int u = 0; u < kF32K / 4; ++u) std::memcpy(blk + r * kF32K * 4 + ((u ^ (r & 7)) << 4), row + u * 16, 16);
+        }
+      }
+    return;
+  }
   const bool q4 = dtype == kTailQ4;
   const int ab = q4 ? TileBytes<true>::AB : TileBytes<false>::AB;
   const size_t tb = q4 ? TileBytes<true>::TB : TileBytes<false>::TB;
@@ -515,9 +646,9 @@ int tail_token_tile(const TailHead& h, int n) {
 }
 
 size_t tail_scratch_bytes(const TailHead& h, int n) {
-  if (h.dtype == kTailF32) return align256(static_cast<size_t>(n) * h.dimp * 4);
   const int nt = tail_token_tile(h, n);
   const size_t n_pad = static_cast<size_t>((n + nt - 1) / nt) * nt;
+  if (h.dtype == kTailF32) return align256(static_cast<size_t>(h.dim) * n_pad * 4);
   return align256(static_cast<size_t>(h.nkc) * n_pad * (kTailChunk + 16));
 }
 
@@ -538,7 +669,7 @@ cudaError_t launch_tail(const TailHead& h, const TailArgs& a, cudaStream_t s) {
   cudaError_t e = cudaFuncSetAttribute(tail_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, norm_smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(h.dtype == kTailF32 ? a.n : a.n_pad);
+  cfg.gridDim = dim3(a.n_pad);
   cfg.blockDim = dim3(kTailThreads);
   cfg.dynamicSmemBytes = norm_smem;
   cfg.stream = s;

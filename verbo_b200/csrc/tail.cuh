@@ -20,8 +20,10 @@
 //                    XOR-swizzled by (token & 7)) then their block scales as
 //                    [4 blocks][nt] fp32; tokens past n are zeros.  A stage
 //                    takes one such block with one bulk copy.
-//   F32 head         the reference layout, vocab x dim floats; its
-//                    normalised rows xb are [token][dimp] floats.
+//   F32 head         tile-major too: for each tile of kTailRows rows and each
+//                    32 floats of K, a 16 KB block (16-byte units swizzled by
+//                    row & 7); its normalised rows xb are blocks of
+//                    [32 floats of K][nt tokens] per (K block, token tile).
 #pragma once
 
 #include <cstddef>
@@ -48,8 +50,7 @@ struct TailHead {
   int dimp;                    // dim rounded up to kTailChunk
   int nkc;                     // dimp / kTailChunk
   int ntile;                   // vocab tiles of kTailRows
-  const unsigned char* tiles;  // Q8 / Q4: the tile-major head
-  const float* q;              // F32: vocab x dim floats
+  const unsigned char* tiles;  // the tile-major head
   const float* norm;           // dim floats
   float eps;
 };
@@ -64,7 +65,7 @@ struct TailArgs {
   float* logits;       // n rows, row i at logits + i*ld
   long long ld;
   unsigned char* act;  // scratch (Q8/Q4): the activation blocks
-  float* xb;           // scratch (F32)
+  float* xb;           // scratch (F32): the activation blocks
 };
 
 // Bytes of the tile-major form of a quantised head, and the packing itself
