@@ -249,6 +249,47 @@ def test_shard_topk_small_shards_pad():
     assert (ci.cpu().numpy()[:, 50:] == -1).all()
 
 
+@pytest.mark.parametrize("form", ["sorted", "shuffled", "holes", "duplicates"])
+@pytest.mark.parametrize("nshards,k", [(1, 64), (3, 50), (16, 256)])
+def test_merge_candidate_lists(form, nshards, k):
+    # merge_sample on lists made directly: in step 1's order (the merge of
+    # sorted lists), shuffled, with missing slots between real ones, and with
+    # the same candidate in two shards; 16 x 256 is the largest merge
+    import verbo_b200 as vb
+    from tests.gpu_util import to_dev_rng
+
+    g = np.random.default_rng(nshards * 1000 + k)
+    rows, vocab = 6, 200000
+    ids = np.stack([g.choice(vocab, size=(nshards, k), replace=False) for _ in range(rows)], axis=1)
+    val = g.standard_normal((nshards, rows, k)).astype(np.float32) * 2
+    val[:, 0, : k // 2] = 1.25                     # ties broken by id
+    ids = ids.astype(np.int32)
+    if form == "duplicates" and nshards > 1:
+        ids[1, :, :5], val[1, :, :5] = ids[0, :, :5], val[0, :, :5]
+    for s in range(nshards):
+        for r in range(rows):
+            o = np.lexsort((ids[s, r], -val[s, r]))
+            ids[s, r], val[s, r] = ids[s, r][o], val[s, r][o]
+    if form == "holes":
+        ids[:, :, 1::3] = -1
+        val[:, :, 1::3] = -np.inf
+    elif form == "shuffled":
+        for s in range(nshards):
+            for r in range(rows):
+                p = g.permutation(k)
+                ids[s, r], val[s, r] = ids[s, r][p], val[s, r][p]
+    seeds = np.arange(rows, dtype=np.uint64) + np.uint64(17)
+    dv, di = torch.from_numpy(val).cuda(), torch.from_numpy(ids).cuda()
+    for opts in (dict(temp=0.8, top_k=k, top_p=0.9, min_p=0.02), dict(temp=1.1, top_k=min(k, 40), top_p=1.0),
+                 dict(temp=0.0)):
+        st = po.seed_states(seeds)
+        rng = to_dev_rng(st)
+        got = vb.merge_sample(dv, di, vocab, vb.Sampling(**opts), rng=rng).cpu().numpy()
+        vb.check()
+        ora, ost = po.merge_sample(val, ids, vocab, po.sampling(**opts), st)
+        compare(got[:, None], ora[:, None], ost[:, None], f"{form} {nshards}x{k} {opts}")
+
+
 def test_min_p_extremes_keep_first():
     # keep starts at 1 (src/sampler.cpp:89): min_p >= 1 keeps the maximum (and its ties)
     g = np.random.default_rng(21)

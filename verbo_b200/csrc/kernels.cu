@@ -25,6 +25,7 @@
 //                   mass-weighted radix selection over the keys handles rows
 //                   whose bins are too crowded.  No full sort.
 //   merge_kernel    merges per-shard candidates and runs the same tail.
+#include <algorithm>
 #include <mutex>
 #include <utility>
 
@@ -80,12 +81,19 @@ struct TailShared {
 // sorted in the reference order (src/sampler.cpp:79-108).  The exps run in
 // parallel; every sum runs in one thread in the reference's order with
 // correctly rounded fp64 operations, so the result is the reference's
-// whenever the fp64 exp agrees.  pr, q: >= k doubles of shared scratch.
+// whenever the fp64 exp agrees.  The softmax sum leaves its running value in
+// pre (pre[i] = pr[0] + ... + pr[i], summed from 0.0 in that order), which is
+// exactly the reference's later sum of the kept candidates (pre[keep - 1])
+// and the mass below the pick (pre[pick - 1]).  While thread 0 sums, warp 1
+// finds the min-p cut (the first i >= 1 with pr[i] below the threshold) by
+// ballots.  The sequential top-p and draw chains read their inputs eight
+// ahead.  pr, q, pre: >= k doubles of shared scratch each; blockDim.x >= 64.
 // rng: the row's state, written back (advanced); rng0 / rng1: its words as
 // thread 0 loaded them early, off the critical path.
 __device__ void tail_pick(const uint64_t* c, int k, const DevOpts& o, unsigned long long* rng, unsigned long long rng0,
                           unsigned long long rng1, int* out_id,
-                          verbo_row_stats* st, double* pr, double* q, TailShared* ts) {
+                          verbo_row_stats* st, double* pr, double* q, double* pre, TailShared* ts) {
+  constexpr int kAhead = 8;
   const float mx = dval(c[0]);
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
     const float v = dval(c[i]);
@@ -93,16 +101,34 @@ __device__ void tail_pick(const uint64_t* c, int k, const DevOpts& o, unsigned l
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    double sum = 0.0;
-    for (int i = 0; i < k; ++i) sum = __dadd_rn(sum, pr[i]);
+    double run = 0.0;
+    for (int i0 = 0; i0 < k; i0 += kAhead) {
+      double v[kAhead];
+#pragma unroll
+      for (int u = 0; u < kAhead; ++u) v[u] = i0 + u < k ? pr[i0 + u] : 0.0;
+#pragma unroll
+      for (int u = 0; u < kAhead; ++u)
+        if (i0 + u < k) {
+          run = __dadd_rn(run, v[u]);
+          pre[i0 + u] = run;
+        }
+    }
+    ts->sum = run;
+  } else if (threadIdx.x >> 5 == 1) {
     int keep = k;
     if (o.min_p > 0.0f) {
+      const int lane = threadIdx.x & 31;
       const double thr = __dmul_rn(pr[0], static_cast<double>(o.min_p));
-      keep = 1;
-      while (keep < k && pr[keep] >= thr) ++keep;
+      for (int b = 1; b < k; b += 32) {
+        const int i = b + lane;
+        const unsigned low = __ballot_sync(0xffffffffu, i < k && !(pr[i] >= thr));
+        if (low) {
+          keep = b + __ffs(low) - 1;
+          break;
+        }
+      }
     }
-    ts->sum = sum;
-    ts->keep = keep;
+    if ((threadIdx.x & 31) == 0) ts->keep = keep;
   }
   __syncthreads();
   const bool use_p = o.top_p > 0.0f && o.top_p < 1.0f;
@@ -122,11 +148,23 @@ __device__ void tail_pick(const uint64_t* c, int k, const DevOpts& o, unsigned l
   if (use_p) {
     const double tp = static_cast<double>(o.top_p);
     double acc = 0.0, prev = 0.0;
-    int i = 0;
-    for (; i < keep; ++i) {
-      prev = acc;
-      acc = __dadd_rn(acc, q[i]);
-      if (acc >= tp) break;
+    int i = keep;  // the first index whose running mass reaches tp, else keep
+    for (int i0 = 0; i0 < keep; i0 += kAhead) {
+      double v[kAhead];
+#pragma unroll
+      for (int u = 0; u < kAhead; ++u) v[u] = i0 + u < keep ? q[i0 + u] : 0.0;
+      int hit = -1;
+#pragma unroll
+      for (int u = 0; u < kAhead; ++u)
+        if (hit < 0 && i0 + u < keep) {
+          prev = acc;
+          acc = __dadd_rn(acc, v[u]);
+          if (acc >= tp) hit = u;
+        }
+      if (hit >= 0) {
+        i = i0 + hit;
+        break;
+      }
     }
     if (i < keep) {
       cut = fmin(cut, acc - tp);
@@ -136,8 +174,7 @@ __device__ void tail_pick(const uint64_t* c, int k, const DevOpts& o, unsigned l
     }
     keep = keep < i + 1 ? keep : i + 1;
   }
-  double tot = 0.0;
-  for (int i = 0; i < keep; ++i) tot = __dadd_rn(tot, pr[i]);
+  const double tot = pre[keep - 1];  // keep >= 1
   unsigned long long s1 = rng0, s0 = rng1;
   const double u = rng_unit(s1, s0);
   rng[0] = s1;
@@ -145,18 +182,26 @@ __device__ void tail_pick(const uint64_t* c, int k, const DevOpts& o, unsigned l
   double r = __dmul_rn(u, tot);
   const double r0 = r;
   int pick = keep - 1;
-  for (int i = 0; i < keep; ++i) {
-    r = __dsub_rn(r, pr[i]);
-    if (r <= 0.0) {
-      pick = i;
+  for (int i0 = 0; i0 < keep; i0 += kAhead) {
+    double v[kAhead];
+#pragma unroll
+    for (int w = 0; w < kAhead; ++w) v[w] = i0 + w < keep ? pr[i0 + w] : 0.0;
+    int hit = -1;
+#pragma unroll
+    for (int w = 0; w < kAhead; ++w)
+      if (hit < 0 && i0 + w < keep) {
+        r = __dsub_rn(r, v[w]);
+        if (r <= 0.0) hit = w;
+      }
+    if (hit >= 0) {
+      pick = i0 + hit;
       break;
     }
   }
   const int id = static_cast<int>(did(c[pick]));
   *out_id = id;
   if (st) {
-    double below = 0.0;
-    for (int i = 0; i < pick; ++i) below += pr[i];
+    const double below = pick > 0 ? pre[pick - 1] : 0.0;
     double m = inf;
     if (pick > 0) m = fmin(m, r0 - below);
     if (pick < keep - 1) m = fmin(m, below + pr[pick] - r0);
@@ -176,7 +221,15 @@ __device__ __forceinline__ uint64_t ckey(float v, uint32_t gid, int idxbits) {
 }
 
 // ====================================================================== merge
-__global__ void __launch_bounds__(kThreads) merge_kernel(const MergeArgs a, const DevOpts o) {
+// A row's merge is latency-bound (a few thousand keys at most, then the
+// serial sums of the pick).  kRank: place the keys by ranking them across
+// the shards' sorted lists (one pass, short search chains when the lists
+// are few and short) and sort only lists that are not sorted; otherwise
+// sort every row.  T threads per CTA.
+constexpr int kMergeRankThreads = 256;
+
+template <int T, bool kRank>
+__global__ void __launch_bounds__(T, T == 512 ? 4 : 1) merge_kernel(const MergeArgs a, const DevOpts o) {
   const int row = blockIdx.x;
   unsigned long long rng0 = 0, rng1 = 0;  // read now, used by thread 0 at the draw
   if (threadIdx.x == 0 && !o.greedy) {
@@ -186,13 +239,15 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const MergeArgs a, cons
   extern __shared__ __align__(16) unsigned char smem[];
   const int total = a.nshards * a.k;
   const int P = next_pow2(max(total, 2));
-  uint64_t* cand = reinterpret_cast<uint64_t*>(smem);
-  double* pr = reinterpret_cast<double*>(cand + P);
+  uint64_t* cand = reinterpret_cast<uint64_t*>(smem);  // P keys in input order
+  uint64_t* merged = cand + P;                          // kRank: P keys in merged order
+  double* pr = reinterpret_cast<double*>(kRank ? merged + P : merged);
   double* q = pr + kSplitMaxK;
-  __shared__ uint32_t ws[kWarps];
+  double* pre = q + kSplitMaxK;
+  __shared__ uint32_t ws[T / 32];
   __shared__ TailShared ts;
   uint32_t valid = 0;
-  for (int i = threadIdx.x; i < P; i += kThreads) {
+  for (int i = threadIdx.x; i < P; i += T) {
     uint64_t d = kNoKey;
     if (i < total) {
       const int s = i / a.k, j = i - s * a.k;
@@ -205,8 +260,55 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const MergeArgs a, cons
     }
     cand[i] = d;
   }
-  valid = block_sum(valid, ws);
-  bitonic_sort_u64(cand, P);
+  bool unsorted = true;
+  if constexpr (kRank) {
+    __syncthreads();
+    // Step 1 emits each shard's list in the reference order with missing slots
+    // last, i.e. ascending keys.  Then the merged order is a stable merge of
+    // sorted lists: a key's place is its index in its own list plus, for every
+    // other list, the number of keys before it (<= for earlier lists, < for
+    // later ones, so equal keys keep distinct places).  The pick reads only
+    // the first min(k, valid) places (the first one when greedy), so a key
+    // stops as soon as its place reaches that cap, and each search looks only
+    // at the entries that could keep it below.  Every list's first r =
+    // ceil(cap / nshards) keys are <= bound, the largest of the lists' r-th
+    // keys: that is >= cap keys, so a key above bound has no place either.
+    // The places written are the cap's first ones, each exactly once; lists
+    // that are not sorted discard them and take the full sort instead.
+    const int cap = o.greedy ? 1 : o.k;
+    const int m = min(a.k, cap);  // keys of each list that can be placed
+    const int r = (cap + a.nshards - 1) / a.nshards;
+    uint64_t bound = 0;
+    for (int t = 0; t < a.nshards; ++t) bound = max(bound, cand[t * a.k + r - 1]);
+    bool bad = false;
+    for (int i = threadIdx.x; i < total; i += T) {
+      const int s = i / a.k;
+      if (i > s * a.k && cand[i - 1] > cand[i]) bad = true;
+    }
+    for (int x = threadIdx.x; x < a.nshards * m; x += T) {
+      const int s = x / m, j = x - s * m;
+      const uint64_t d = cand[s * a.k + j];
+      if (d > bound) continue;  // kNoKey included
+      int at = j;
+      for (int t = 0; t < a.nshards && at < cap; ++t) {
+        if (t == s) continue;
+        const uint64_t* seg = cand + t * a.k;
+        int lo = 0, hi = min(a.k, cap - at);
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          const uint64_t e = seg[mid];
+          if (t < s ? e <= d : e < d) lo = mid + 1;
+          else hi = mid;
+        }
+        at += lo;
+      }
+      if (at < cap) merged[at] = d;
+    }
+    unsorted = __syncthreads_or(bad);
+  }
+  valid = block_sum<uint32_t, T>(valid, ws);  // its barriers publish cand
+  if (unsorted) bitonic_sort_u64(cand, P);
+  const uint64_t* c = unsorted ? cand : merged;
   if (valid == 0) {
     if (threadIdx.x == 0) {
       raise_status(kErrSelect);
@@ -216,7 +318,7 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const MergeArgs a, cons
   }
   if (o.greedy) {
     if (threadIdx.x == 0) {
-      const int id = static_cast<int>(did(cand[0]));
+      const int id = static_cast<int>(did(c[0]));
       a.out_ids[row] = id;
       if (a.stats) write_stats(a.stats + row, 0.0, 0.0, 0.0, __longlong_as_double(0x7ff0000000000000ll),
                                __longlong_as_double(0x7ff0000000000000ll), o.vocab, 1, id, 1);
@@ -224,7 +326,8 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const MergeArgs a, cons
     return;
   }
   const int kk = min(o.k, static_cast<int>(valid));
-  tail_pick(cand, kk, o, a.rng + 2ll * row, rng0, rng1, a.out_ids + row, a.stats ? a.stats + row : nullptr, pr, q, &ts);
+  tail_pick(c, kk, o, a.rng + 2ll * row, rng0, rng1, a.out_ids + row, a.stats ? a.stats + row : nullptr, pr, q, pre,
+            &ts);
 }
 
 // ================================================================== general
@@ -1197,7 +1300,21 @@ static int next_pow2_host(int x) {
   while (p < x) p <<= 1;
   return p;
 }
-size_t merge_smem(int n) { return static_cast<size_t>(next_pow2_host(n < 2 ? 2 : n)) * 8 + 2 * kSplitMaxK * 8; }
+// The rank merge of the shards' lists runs when each thread's search chain
+// stays short: at most (nshards - 1) binary searches over the first m
+// entries of a list for each key it places, m = min(k, places the pick
+// reads).  Longer chains cost more than sorting the row.
+static bool merge_by_rank(const MergeArgs& a, const DevOpts& o) {
+  const int m = std::min(a.k, o.greedy ? 1 : o.k);
+  int steps = 0;
+  while ((1 << steps) <= m) ++steps;
+  const int per = (a.nshards * m + kMergeRankThreads - 1) / kMergeRankThreads;
+  return (a.nshards - 1) * per * steps <= 128;
+}
+
+static size_t merge_smem(int n, bool rank) {
+  return static_cast<size_t>(next_pow2_host(n < 2 ? 2 : n)) * (rank ? 16 : 8) + 3 * kSplitMaxK * 8;
+}
 
 template <class K, class A>
 static cudaError_t launch_cluster(K kernel, const A& args, const DevOpts& o, int grid, int cluster, size_t smem,
@@ -1224,10 +1341,19 @@ cudaError_t launch_general(const RowArgs& a, const DevOpts& o, cudaStream_t s) {
 }
 
 cudaError_t launch_merge(const MergeArgs& a, const DevOpts& o, cudaStream_t s) {
-  const size_t sm = merge_smem(a.nshards * a.k);
-  cudaError_t e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
-  if (e != cudaSuccess) return e;
-  merge_kernel<<<a.rows, kThreads, sm, s>>>(a, o);
+  const bool rank = merge_by_rank(a, o);
+  const size_t sm = merge_smem(a.nshards * a.k, rank);
+  if (rank) {
+    auto* kernel = merge_kernel<kMergeRankThreads, true>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+    if (e != cudaSuccess) return e;
+    kernel<<<a.rows, kMergeRankThreads, sm, s>>>(a, o);
+  } else {
+    auto* kernel = merge_kernel<kThreads, false>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+    if (e != cudaSuccess) return e;
+    kernel<<<a.rows, kThreads, sm, s>>>(a, o);
+  }
   return cudaGetLastError();
 }
 
@@ -1812,7 +1938,7 @@ __global__ void __launch_bounds__(NT, 6) merge_slices_kernel(const RowArgs a, co
   if (threadIdx.x == 0) sh.ncand = 0;
   __syncthreads();
   const unsigned long long* base = a.slice_keys + static_cast<long long>(row) * C * kSliceCap;
-  uint64_t* sel = reinterpret_cast<uint64_t*>(H) + 512;  // H bytes [4 KB, 8 KB); the tail uses [0, 4 KB)
+  uint64_t* sel = reinterpret_cast<uint64_t*>(H) + 512;  // H bytes [4 KB, 8 KB); the tail uses [0, 6 KB)
   const bool in_smem = utot <= static_cast<uint32_t>(kUnionCap);
   if (in_smem) {  // a slice publishes at most kSliceCap == NT keys; 8 slices' loads in flight at once
     for (int i0 = 0; i0 < C; i0 += 8) {
@@ -2011,10 +2137,13 @@ __global__ void __launch_bounds__(NT, 6) merge_slices_kernel(const RowArgs a, co
       a.cand_id[at] = ok ? static_cast<int>(did(cand[i])) : -1;
     }
   } else {
-    double* pr = reinterpret_cast<double*>(H);  // H is free: fp64 scratch of the tail
+    // H's first 4 KB and sel (the k best are in cand now) are free: fp64
+    // scratch of the tail, ending where cand starts
+    double* pr = reinterpret_cast<double*>(H);
+    static_assert(3 * kSplitMaxK * sizeof(double) == 512 * sizeof(uint64_t) + kSliceCap * sizeof(uint64_t),
+                  "the tail's scratch is H bytes [0, 6 KB)");
     tail_pick(cand, static_cast<int>(k), o, a.rng + 2ll * row, rng0, rng1, a.out_ids + row,
-              a.stats ? a.stats + row : nullptr, pr,
-              pr + kSplitMaxK, &sh.tail);
+              a.stats ? a.stats + row : nullptr, pr, pr + kSplitMaxK, pr + 2 * kSplitMaxK, &sh.tail);
     if (threadIdx.x == 0) ring_append(a, row, a.out_ids[row]);  // written by this thread in tail_pick
   }
 }

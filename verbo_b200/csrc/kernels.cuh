@@ -116,7 +116,6 @@ struct MergeArgs {
 cudaError_t launch_general(const RowArgs& a, const DevOpts& o, cudaStream_t s);
 cudaError_t launch_merge(const MergeArgs& a, const DevOpts& o, cudaStream_t s);
 size_t general_smem(int slice);
-size_t merge_smem(int n);
 cudaError_t read_status(unsigned* st, bool clear, cudaStream_t s);
 
 }  // namespace vb
