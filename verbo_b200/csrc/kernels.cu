@@ -222,14 +222,13 @@ __device__ __forceinline__ uint64_t ckey(float v, uint32_t gid, int idxbits) {
 
 // ====================================================================== merge
 // A row's merge is latency-bound (a few thousand keys at most, then the
-// serial sums of the pick).  kRank: place the keys by ranking them across
-// the shards' sorted lists (one pass, short search chains when the lists
-// are few and short) and sort only lists that are not sorted; otherwise
-// sort every row.  T threads per CTA.
-constexpr int kMergeRankThreads = 256;
+// serial sums of the pick): it places the keys by ranking them across the
+// shards' sorted lists and sorts only lists that are not sorted.  Small CTAs,
+// so that 512 rows run in one wave.
+constexpr int kMergeThreads = 256;
 
-template <int T, bool kRank>
-__global__ void __launch_bounds__(T, T == 512 ? 4 : 1) merge_kernel(const MergeArgs a, const DevOpts o) {
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeArgs a, const DevOpts o) {
+  constexpr int T = kMergeThreads;
   const int row = blockIdx.x;
   unsigned long long rng0 = 0, rng1 = 0;  // read now, used by thread 0 at the draw
   if (threadIdx.x == 0 && !o.greedy) {
@@ -240,8 +239,8 @@ __global__ void __launch_bounds__(T, T == 512 ? 4 : 1) merge_kernel(const MergeA
   const int total = a.nshards * a.k;
   const int P = next_pow2(max(total, 2));
   uint64_t* cand = reinterpret_cast<uint64_t*>(smem);  // P keys in input order
-  uint64_t* merged = cand + P;                          // kRank: P keys in merged order
-  double* pr = reinterpret_cast<double*>(kRank ? merged + P : merged);
+  uint64_t* merged = cand + P;                          // P keys in merged order
+  double* pr = reinterpret_cast<double*>(merged + P);
   double* q = pr + kSplitMaxK;
   double* pre = q + kSplitMaxK;
   __shared__ uint32_t ws[T / 32];
@@ -260,53 +259,52 @@ __global__ void __launch_bounds__(T, T == 512 ? 4 : 1) merge_kernel(const MergeA
     }
     cand[i] = d;
   }
-  bool unsorted = true;
-  if constexpr (kRank) {
-    __syncthreads();
-    // Step 1 emits each shard's list in the reference order with missing slots
-    // last, i.e. ascending keys.  Then the merged order is a stable merge of
-    // sorted lists: a key's place is its index in its own list plus, for every
-    // other list, the number of keys before it (<= for earlier lists, < for
-    // later ones, so equal keys keep distinct places).  The pick reads only
-    // the first min(k, valid) places (the first one when greedy), so a key
-    // stops as soon as its place reaches that cap, and each search looks only
-    // at the entries that could keep it below.  Every list's first r =
-    // ceil(cap / nshards) keys are <= bound, the largest of the lists' r-th
-    // keys: that is >= cap keys, so a key above bound has no place either.
-    // The places written are the cap's first ones, each exactly once; lists
-    // that are not sorted discard them and take the full sort instead.
-    const int cap = o.greedy ? 1 : o.k;
-    const int m = min(a.k, cap);  // keys of each list that can be placed
-    const int r = (cap + a.nshards - 1) / a.nshards;
-    uint64_t bound = 0;
-    for (int t = 0; t < a.nshards; ++t) bound = max(bound, cand[t * a.k + r - 1]);
-    bool bad = false;
-    for (int i = threadIdx.x; i < total; i += T) {
-      const int s = i / a.k;
-      if (i > s * a.k && cand[i - 1] > cand[i]) bad = true;
-    }
-    for (int x = threadIdx.x; x < a.nshards * m; x += T) {
-      const int s = x / m, j = x - s * m;
-      const uint64_t d = cand[s * a.k + j];
-      if (d > bound) continue;  // kNoKey included
-      int at = j;
-      for (int t = 0; t < a.nshards && at < cap; ++t) {
-        if (t == s) continue;
-        const uint64_t* seg = cand + t * a.k;
-        int lo = 0, hi = min(a.k, cap - at);
-        while (lo < hi) {
-          const int mid = (lo + hi) >> 1;
-          const uint64_t e = seg[mid];
-          if (t < s ? e <= d : e < d) lo = mid + 1;
-          else hi = mid;
-        }
-        at += lo;
-      }
-      if (at < cap) merged[at] = d;
-    }
-    unsorted = __syncthreads_or(bad);
+  __syncthreads();
+  // Step 1 emits each shard's list in the reference order with missing slots
+  // last, i.e. ascending keys.  Then the merged order is a stable merge of
+  // sorted lists: a key's place is its index in its own list plus, for every
+  // other list, the number of keys before it (<= for earlier lists, < for
+  // later ones, so equal keys keep distinct places).  The pick reads only
+  // the first min(k, valid) places (the first one when greedy), so a key
+  // stops as soon as its place reaches that cap, and each search looks only
+  // at the entries that could keep it below.  Every list's first r =
+  // ceil(cap / nshards) keys are <= bound, the largest of the lists' r-th
+  // keys: that is >= cap keys, so a key above bound has no place either.
+  // The places written are the cap's first ones, each exactly once; lists
+  // that are not sorted discard them and take the full sort instead.
+  const int cap = o.greedy ? 1 : o.k;
+  const int m = min(a.k, cap);  // keys of each list that can be placed
+  const int r = (cap + a.nshards - 1) / a.nshards;
+  uint64_t bound = 0;
+  for (int t = 0; t < a.nshards; ++t) bound = max(bound, cand[t * a.k + r - 1]);
+  bool bad = false;
+  for (int i = threadIdx.x; i < total; i += T) {
+    const int s = i / a.k;
+    if (i > s * a.k && cand[i - 1] > cand[i]) bad = true;
   }
-  valid = block_sum<uint32_t, T>(valid, ws);  // its barriers publish cand
+  // keys taken index-major, so that the few below the bound (the lists'
+  // first ones) fall to different threads
+  for (int x = threadIdx.x; x < a.nshards * m; x += T) {
+    const int j = x / a.nshards, s = x - j * a.nshards;
+    const uint64_t d = cand[s * a.k + j];
+    if (d > bound) continue;  // kNoKey included
+    int at = j;
+    for (int t = 0; t < a.nshards && at < cap; ++t) {
+      if (t == s) continue;
+      const uint64_t* seg = cand + t * a.k;
+      int lo = 0, hi = min(a.k, cap - at);
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        const uint64_t e = seg[mid];
+        if (t < s ? e <= d : e < d) lo = mid + 1;
+        else hi = mid;
+      }
+      at += lo;
+    }
+    if (at < cap) merged[at] = d;
+  }
+  const bool unsorted = __syncthreads_or(bad);
+  valid = block_sum<uint32_t, T>(valid, ws);
   if (unsorted) bitonic_sort_u64(cand, P);
   const uint64_t* c = unsorted ? cand : merged;
   if (valid == 0) {
@@ -1300,20 +1298,8 @@ static int next_pow2_host(int x) {
   while (p < x) p <<= 1;
   return p;
 }
-// The rank merge of the shards' lists runs when each thread's search chain
-// stays short: at most (nshards - 1) binary searches over the first m
-// entries of a list for each key it places, m = min(k, places the pick
-// reads).  Longer chains cost more than sorting the row.
-static bool merge_by_rank(const MergeArgs& a, const DevOpts& o) {
-  const int m = std::min(a.k, o.greedy ? 1 : o.k);
-  int steps = 0;
-  while ((1 << steps) <= m) ++steps;
-  const int per = (a.nshards * m + kMergeRankThreads - 1) / kMergeRankThreads;
-  return (a.nshards - 1) * per * steps <= 128;
-}
-
-static size_t merge_smem(int n, bool rank) {
-  return static_cast<size_t>(next_pow2_host(n < 2 ? 2 : n)) * (rank ? 16 : 8) + 3 * kSplitMaxK * 8;
+static size_t merge_smem(int n) {
+  return static_cast<size_t>(next_pow2_host(n < 2 ? 2 : n)) * 16 + 3 * kSplitMaxK * 8;
 }
 
 template <class K, class A>
@@ -1341,19 +1327,10 @@ cudaError_t launch_general(const RowArgs& a, const DevOpts& o, cudaStream_t s) {
 }
 
 cudaError_t launch_merge(const MergeArgs& a, const DevOpts& o, cudaStream_t s) {
-  const bool rank = merge_by_rank(a, o);
-  const size_t sm = merge_smem(a.nshards * a.k, rank);
-  if (rank) {
-    auto* kernel = merge_kernel<kMergeRankThreads, true>;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
-    if (e != cudaSuccess) return e;
-    kernel<<<a.rows, kMergeRankThreads, sm, s>>>(a, o);
-  } else {
-    auto* kernel = merge_kernel<kThreads, false>;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
-    if (e != cudaSuccess) return e;
-    kernel<<<a.rows, kThreads, sm, s>>>(a, o);
-  }
+  const size_t sm = merge_smem(a.nshards * a.k);
+  cudaError_t e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  if (e != cudaSuccess) return e;
+  merge_kernel<<<a.rows, kMergeThreads, sm, s>>>(a, o);
   return cudaGetLastError();
 }
 
