@@ -250,7 +250,7 @@ def test_shard_topk_small_shards_pad():
 
 
 @pytest.mark.parametrize("form", ["sorted", "shuffled", "holes", "duplicates"])
-@pytest.mark.parametrize("nshards,k", [(1, 64), (3, 50), (16, 256)])
+@pytest.mark.parametrize("nshards,k", [(1, 64), (3, 50), (16, 256), (16, 1), (2, 256)])
 def test_merge_candidate_lists(form, nshards, k):
     # merge_sample on lists made directly: in step 1's order (the merge of
     # sorted lists), shuffled, with missing slots between real ones, and with
