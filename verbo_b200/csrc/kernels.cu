@@ -1917,16 +1917,25 @@ __global__ void __launch_bounds__(NT, 6) merge_slices_kernel(const RowArgs a, co
   const unsigned long long* base = a.slice_keys + static_cast<long long>(row) * C * kSliceCap;
   uint64_t* sel = reinterpret_cast<uint64_t*>(H) + 512;  // H bytes [4 KB, 8 KB); the tail uses [0, 6 KB)
   const bool in_smem = utot <= static_cast<uint32_t>(kUnionCap);
-  if (in_smem) {  // a slice publishes at most kSliceCap == NT keys; 8 slices' loads in flight at once
-    for (int i0 = 0; i0 < C; i0 += 8) {
-      unsigned long long v8[8];
+  if (in_smem) {
+    // The union's keys spread evenly over the threads (key e of the union is
+    // key e - soff[i] of slice i): at most kUnionCap / NT == 8 per thread,
+    // all of them in flight at once.
+    static_assert(kUnionCap == 8 * NT, "eight union keys per thread");
+    unsigned long long v8[8];
+    int sl = 0;  // the slice of the thread's current key; keys ascend, so do slices
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (i0 + q < C && threadIdx.x < scnt[i0 + q])
-          v8[q] = __ldcg(base + static_cast<long long>(i0 + q) * kSliceCap + threadIdx.x);
+    for (int q = 0; q < 8; ++q) {
+      const int e = threadIdx.x + q * NT;
+      if (e < static_cast<int>(utot)) {
+        while (sl + 1 < C && static_cast<int>(soff[sl + 1]) <= e) ++sl;
+        v8[q] = __ldcg(base + static_cast<long long>(sl) * kSliceCap + (e - static_cast<int>(soff[sl])));
+      }
+    }
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (i0 + q < C && threadIdx.x < scnt[i0 + q]) U[soff[i0 + q] + threadIdx.x] = v8[q];
+    for (int q = 0; q < 8; ++q) {
+      const int e = threadIdx.x + q * NT;
+      if (e < static_cast<int>(utot)) U[e] = v8[q];
     }
     __syncthreads();
   }
