@@ -3,9 +3,11 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
 
-The default configuration is C2 (the one the metric is
-quoted on: 256 greedy rows at V = 151936); C1 and C3-C5 are selectable with
---config and are parity cases of the test suite.
+The default configuration is C4: 4096 sampled rows at V = 151936 (flat
+N(0, 0.5^2) logits, temp 1.5, top_p 0.99, no top-k), the full-vocabulary
+nucleus that the metric's "sampled rows/s ... 1/2/4/8 B200" is quoted on,
+sharded by rows over the GPUs.  C1-C3 and C5 are selectable with --config and
+are parity cases of the test suite.
 
 Under torchrun (N > 1) every rank runs the same per-rank workload (weak
 scaling: rows are independent, no collective on the data path) and rank 0
@@ -64,7 +66,7 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--config", default="c2", choices=sorted(wl.WORKLOADS) + ["tail"])
+    p.add_argument("--config", default="c4", choices=sorted(wl.WORKLOADS) + ["tail"])
     p.add_argument("--head", default="q8", choices=["q8", "q4", "f32"], help="head dtype of --config tail")
     p.add_argument("--shard-head", action="store_true",
                    help="--config tail: tensor-parallel head (vocab rows split over the ranks), each step "
@@ -155,29 +157,43 @@ class Clocks:
                 "samples": len(sm)}
 
 
+def rotating_copies(batch_bytes: int) -> int:
+    """Input copies the timed steps rotate through, so that consecutive steps
+    never find their rows in L2: at least twice L2 in total."""
+    return max(1, -(-2 * L2_BYTES // batch_bytes))
+
+
 def algorithmic_bytes_per_row(w: wl.Workload, cols: int | None = None) -> int:
     cols = w.vocab if cols is None else cols
     return 4 * cols + 4 * w.hist_len + 4
 
 
 # ----------------------------------------------------------- CPU reference ----
-def cpu_reference_rate(w: wl.Workload, x: np.ndarray, h, off, seconds: float, threads: int):
-    """Rows/s of the reference's compiled Sampler (oracle/_ref, else the C
-    restatement) over the host rows `x`, repeated until `seconds` elapse."""
+# The bench line's cpu_baseline and the --impl reference arm time the CPU
+# reference the same way: the same sample of rows (host_rows_for_budget), one
+# untimed pass, then whole timed passes over that sample, on all host threads.
+def cpu_reference_pass(w: wl.Workload, x: np.ndarray, h, off, threads: int):
+    """One pass of the reference's compiled Sampler (oracle/_ref, else the C
+    restatement on one thread) over the host rows `x`.  Returns (kind, threads used)."""
     from oracle import pyoracle as po
 
     o = po.sampling(**w.sampling_kwargs())
     seeds = w.sampler_seeds(0, x.shape[0])
     if po.ref_available():
-        kind, used = "reference", threads
-        run = lambda: po.ref_sample_rows(x, o, seeds, h, off, steps=1, threads=threads)  # noqa: E731
-    else:
-        kind, used = "port", 1
-        run = lambda: po.sample_rows(x, o, po.seed_states(seeds), h, off)  # noqa: E731
+        po.ref_sample_rows(x, o, seeds, h, off, steps=1, threads=threads)
+        return "reference", threads
+    po.sample_rows(x, o, po.seed_states(seeds), h, off)
+    return "port", 1
+
+
+def cpu_reference_rate(w: wl.Workload, x: np.ndarray, h, off, seconds: float, threads: int):
+    """Rows/s of the CPU reference over the host rows `x`: one untimed pass,
+    then timed passes until `seconds` elapse."""
+    kind, used = cpu_reference_pass(w, x, h, off, threads)
     t0 = time.perf_counter()
     n = 0
     while True:
-        run()
+        cpu_reference_pass(w, x, h, off, threads)
         n += 1
         dt = time.perf_counter() - t0
         if dt >= seconds or n >= 1000:
@@ -213,7 +229,7 @@ def bench_rows(a, w: wl.Workload, rank: int, world: int, dev):
     V = w.vocab
     opts = vb.Sampling(**w.sampling_kwargs())
     batch_bytes = R * V * 4
-    copies = 1 if batch_bytes > L2_BYTES else -(-2 * L2_BYTES // batch_bytes)
+    copies = rotating_copies(batch_bytes)
     xs = [wl.make_rows_torch(w, R, dev, seed_offset=rank * 1000 + c) for c in range(copies)]
     h, off = wl.make_hist_torch(w, R, dev, seed_offset=rank)
     seeds = w.sampler_seeds(rank * R, R)
@@ -360,7 +376,7 @@ def bench_sharded(a, w: wl.Workload, rank: int, world: int, dev):
     shard_w = wl.Workload(w.name, R, cols, w.dist, w.scale, w.data_seed, w.temp, w.top_k, w.top_p, w.min_p,
                           w.repeat, w.hist_len)
     batch_bytes = R * cols * 4
-    copies = 1 if batch_bytes > L2_BYTES else -(-2 * L2_BYTES // batch_bytes)
+    copies = rotating_copies(batch_bytes)
     xs = [wl.make_rows_torch(shard_w, R, dev, seed_offset=rank * 1000 + c) for c in range(copies)]
     h, off = wl.make_hist_torch(w, R, dev, seed_offset=0)        # the same histories on every rank
     st = np.array(vb.seed_states(w.sampler_seeds(0, R).tolist()), dtype=np.uint64)
@@ -430,6 +446,9 @@ def bench_sharded(a, w: wl.Workload, rank: int, world: int, dev):
 
 # ------------------------------------------------------------ reference arm ----
 def bench_reference(a, w: wl.Workload, world: int):
+    """The CPU reference as the reference arm: --warmup untimed and --steps
+    timed passes over a sample of the configuration's rows, timed as the bench
+    line's cpu_baseline is (cpu_reference_pass)."""
     from oracle import pyoracle as po
 
     threads = po.host_threads()
@@ -437,21 +456,12 @@ def bench_reference(a, w: wl.Workload, world: int):
     n = min(w.rows, host_rows_for_budget(w, per_step, threads, w.rows))
     x = wl.make_rows_np(w, n)
     h, off = wl.make_hist_np(w, n)
-    o = po.sampling(**w.sampling_kwargs())
-    seeds = w.sampler_seeds(0, n)
-    kind = "reference" if po.ref_available() else "port"
-
-    def step():
-        if kind == "reference":
-            po.ref_sample_rows(x, o, seeds, h, off, steps=1, threads=threads)
-        else:
-            po.sample_rows(x, o, po.seed_states(seeds), h, off)
-
+    kind, used = "port", 1
     for _ in range(a.warmup):
-        step()
+        kind, used = cpu_reference_pass(w, x, h, off, threads)
     t0 = time.perf_counter()
     for _ in range(a.steps):
-        step()
+        cpu_reference_pass(w, x, h, off, threads)
     dt = time.perf_counter() - t0
     value = a.steps * n / dt
     sample = f"{n} of the {w.rows} rows of {w.name}, the same rows every step"
@@ -460,8 +470,7 @@ def bench_reference(a, w: wl.Workload, world: int):
         "ms_per_step": dt * 1000.0 / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic", "impl": "reference",
         "config": workload_config(w, n, 1),
-        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads if kind == "reference" else 1,
-                         "kind": kind, "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": used, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -104,8 +104,12 @@ VERBO_CUDA_API int verbo_cuda_sample(const float* logits, int rows, int vocab, l
    Its scratch is a fixed 8 MiB array inside the library, held by every device
    that loads the library until the process exits: up to about 272 top-k rows
    per call at vocab 151936 (127 at the largest vocab, 327680) and about
-   46,000 greedy rows; larger calls are rejected with an error.  The first call on each device looks up the
-   array's address (cudaGetSymbolAddress); make that first call before any
+   46,000 greedy rows; larger calls are rejected with an error.  Each call
+   looks up the array's address (cudaGetSymbolAddress).  CUDA loads a
+   library's device code lazily, so the first call on each device also loads
+   this library's module there, placing the array and the kernels' code in
+   device memory at that moment: make that first call (or run with
+   CUDA_MODULE_LOADING=EAGER) before reserving the memory pool and before any
    stream capture.  All calls share the array: calls that overlap on the GPU
    (concurrent streams or host threads) race and must be serialised by the
    caller. */

@@ -19,6 +19,7 @@ import numpy as np
 import pytest
 
 from oracle import pyoracle as po
+from tests.gpu_util import compare
 
 pytestmark = pytest.mark.gpu
 
@@ -66,8 +67,40 @@ def test_noalloc_matches_sample_on_two_calls(vb, vocab, rows, opts):
         vb.check()
         assert torch.equal(got, want), f"call {call}: ids differ"
         assert torch.equal(rng_a, rng_b), f"call {call}: rng states differ"
+        if call == 0:
+            # and the first call's ids against the oracle (the reference's
+            # Sampler restated), on the same rows, histories and seeds
+            xh, hh, oh = x.cpu().numpy(), hist.cpu().numpy(), off.cpu().numpy()
+            ora, ost = po.sample_rows(xh, po.sampling(**opts), po.seed_states(seeds), hh, oh)
+            compare(got.cpu().numpy()[:, None], ora[:, None], ost[:, None], "noalloc vs oracle")
     torch.cuda.synchronize()
     assert torch.cuda.mem_get_info()[0] == free_before
+
+
+def test_noalloc_first_call_in_a_fresh_process(vb):
+    """The allocation-free entry point as the first call of the library in a
+    process.  CUDA loads the library's module lazily, so this first call is
+    where the module's device memory (the fixed scratch array and the code)
+    is placed: the worker reports that cost, and checks that the calls after
+    it change the device's free memory by nothing."""
+    import json
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    env = dict(os.environ)
+    env.pop("CUDA_MODULE_LOADING", None)
+    r = subprocess.run([sys.executable, str(root / "tests" / "noalloc_first_call.py")], capture_output=True,
+                       text=True, timeout=300, env=env, cwd=str(root))
+    assert r.returncode == 0, r.stdout + r.stderr
+    rep = json.loads(r.stdout.strip().splitlines()[-1])
+    print("first allocation-free call:", rep)
+    assert rep["ids_equal"] and rep["later_calls_bytes"] == 0
+    # what the first call placed: the library's module (the 8 MiB array plus
+    # code and small globals), or nothing if the module was loaded eagerly
+    assert rep["first_call_bytes"] <= 64 << 20
 
 
 def test_noalloc_rejects_sizes_beyond_the_scratch(vb):

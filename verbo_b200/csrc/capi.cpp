@@ -326,11 +326,19 @@ VERBO_CUDA_API int verbo_cuda_sample_noalloc(const float* logits, int rows, int 
                                          static_cast<cudaStream_t>(stream), &too_big),
                 "kernel launch");
         if (too_big) {
-          const long long per_row = 4ll * a.cluster + 8ll * a.cluster * (o.greedy ? 1 : vb::kSliceCap) +
-                                    (o.greedy ? 0ll : 4ll * a.cluster) + 4ll * vb::split_window_width(o);
+          // the largest row count the same layout fits (binary search, so the
+          // quoted limit is exactly the one the check enforces)
+          const int win_w = vb::split_window_width(o);
+          long long lo = 0, hi = rows;  // lo fits, hi does not
+          while (hi - lo > 1) {
+            const long long mid = lo + (hi - lo) / 2;
+            if (vb::split_scratch_layout(mid, a.cluster, o.greedy != 0, win_w).bytes <= vb::kNoAllocScratchBytes)
+              lo = mid;
+            else
+              hi = mid;
+          }
           fail("rows x vocab exceed the fixed scratch of " + std::to_string(vb::kNoAllocScratchBytes >> 20) +
-               " MiB: at most about " + std::to_string((vb::kNoAllocScratchBytes - 512) / per_row) +
-               " rows at vocab " + std::to_string(vocab) + " per call");
+               " MiB: at most " + std::to_string(lo) + " rows at vocab " + std::to_string(vocab) + " per call");
         }
         return 0;
       },

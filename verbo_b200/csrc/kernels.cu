@@ -2290,24 +2290,18 @@ cudaError_t launch_split(const RowArgs& a, const DevOpts& o, int mode, cudaStrea
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 // The array's device address on the current device.  Host code cannot use the
-// symbol itself (that is a host-side stand-in, not a device address): the
-// address is looked up once per device with cudaGetSymbolAddress, with that
-// device current.
+// symbol itself (that is a host-side stand-in, not a device address), so the
+// address is looked up with cudaGetSymbolAddress, with the device current, on
+// every call: the lookup allocates nothing once the module is loaded, and a
+// fresh lookup stays right after cudaDeviceReset recreates the context.  The
+// first lookup on a device loads the library's module there (CUDA loads
+// modules lazily): the array and the kernels' code are placed in device memory
+// at that moment.
 static cudaError_t noalloc_scratch_address(void** out) {
-  static std::mutex mu;
-  static void* addr[64] = {};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lk(mu);
-  if (!addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return e;
-    addr[dev] = p;
-  }
-  *out = addr[dev];
+  *out = p;
   return cudaSuccess;
 }
 

@@ -11,7 +11,7 @@ c1     1 x 49152       N(0, 3^2)                                       temp .7 t
 c2     256 x 151936    N(0, 2^2)                                       greedy, repeat 1.2                        128 ids
 c3     1024 x 151936   log(rank^-1.1) + N(0, .1^2), permuted per row   temp .8 top_k 50 top_p .95 rep 1.1        256 ids
 c4     4096 x 151936   N(0, .5^2)                                      temp 1.5 top_k 0 top_p .99                none
-c5     512 x 151936    N(0, 3^2), 8 column shards of 18992             temp .9 top_k 64 min_p .1 rep 1.15        1024 ids
+c5     512 x 151936    N(0, 3^2), 8 column shards of 18992             temp .9 top_k 64 top_p .9 min_p .1 rep 1.15  1024 ids
 =====  ==============  ==============================================  ========================================  ==========
 
 History ids are uniform in [0, vocab).  The penalty window equals the history
@@ -69,7 +69,8 @@ WORKLOADS = {
     "c2": Workload("c2", 256, 151936, "normal", 2.0, 1, 0.0, 40, 0.9, 0.0, 1.2, 128),
     "c3": Workload("c3", 1024, 151936, "zipf", 0.1, 2, 0.8, 50, 0.95, 0.0, 1.1, 256),
     "c4": Workload("c4", 4096, 151936, "normal", 0.5, 3, 1.5, 0, 0.99, 0.0, 1.0, 0),
-    "c5": Workload("c5", 512, 151936, "normal", 3.0, 4, 0.9, 64, 1.0, 0.1, 1.15, 1024, shards=8),
+    # C5 names no top_p: the reference's default, 0.9 (include/verbo/verbo.hpp:58), applies
+    "c5": Workload("c5", 512, 151936, "normal", 3.0, 4, 0.9, 64, 0.9, 0.1, 1.15, 1024, shards=8),
 }
 
 
