@@ -143,6 +143,13 @@ VERBO_CUDA_API int verbo_cuda_merge_sample(const float* cand_val, const int* can
    last check (then clears them): 0 if none, -1 with a message otherwise. */
 VERBO_CUDA_API int verbo_cuda_check(void* stream);
 
+/* Diagnostics of the full-vocabulary path (top_k == 0 or >= vocab, no min-p,
+   no penalty; no counterpart in the reference): synchronises `stream` and
+   returns how many rows of the last such call on it were settled by the
+   staged cluster kernel instead of the streaming one (rows whose cutoff or
+   draw fell among crowded or underflow columns), or -1 on error. */
+VERBO_CUDA_API int verbo_cuda_full_vocab_fallbacks(void* stream);
+
 /* ---- Single-stream sampler object: the verbo::Sampler interface
         (include/verbo/verbo.hpp:116-132) as an opaque handle. ---- */
 typedef struct verbo_cuda_sampler verbo_cuda_sampler;

@@ -28,7 +28,7 @@ from dataclasses import dataclass
 from pathlib import Path
 from typing import Optional, Sequence
 
-__all__ = ["Sampling", "Sampler", "VerboCudaError", "load_library", "sample", "sample_noalloc", "shard_topk", "merge_sample",
+__all__ = ["Sampling", "Sampler", "VerboCudaError", "load_library", "sample", "sample_noalloc", "full_vocab_fallbacks", "shard_topk", "merge_sample",
            "seed_states", "check", "version", "ROW_STATS_FIELDS", "Batch", "Tail"]
 __version__ = "0.1.0"
 
@@ -119,6 +119,7 @@ def load_library():
         "verbo_cuda_merge_sample": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                    ctypes.POINTER(_Sampling), _P, _P, _P, _P]),
         "verbo_cuda_check": (ctypes.c_int, [_P]),
+        "verbo_cuda_full_vocab_fallbacks": (ctypes.c_int, [_P]),
         "verbo_cuda_sampler_new": (_P, [ctypes.POINTER(_Sampling), ctypes.c_int]),
         "verbo_cuda_sampler_free": (None, [_P]),
         "verbo_cuda_sampler_pick": (ctypes.c_int, [_P, _P, ctypes.c_int]),
@@ -273,6 +274,14 @@ def merge_sample(cand_val, cand_id, vocab: int, opts: Sampling, rng=None, out=No
 def check(stream=None) -> None:
     """Synchronises the stream and raises if a kernel recorded a failure."""
     _ok(load_library().verbo_cuda_check(_stream(stream)))
+
+
+def full_vocab_fallbacks(stream=None) -> int:
+    """Rows of the last full-vocabulary call on the stream that the staged
+    cluster kernel settled instead of the streaming one (synchronises)."""
+    n = load_library().verbo_cuda_full_vocab_fallbacks(_stream(stream))
+    _ok(0 if n >= 0 else -1)
+    return n
 
 
 class Sampler:

@@ -19,8 +19,9 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "_lib"
 LIB = LIB_DIR / "libverbo_cuda.so"
-SOURCES = [CSRC / "kernels.cu", CSRC / "tail.cu", CSRC / "capi.cpp"]
-HEADERS = [CSRC / "device.cuh", CSRC / "kernels.cuh", CSRC / "tail.cuh", ROOT / "include" / "verbo_cuda.h"]
+SOURCES = [CSRC / "kernels.cu", CSRC / "nucleus.cu", CSRC / "tail.cu", CSRC / "capi.cpp"]
+HEADERS = [CSRC / "device.cuh", CSRC / "kernels.cuh", CSRC / "rowdev.cuh", CSRC / "tail.cuh",
+           ROOT / "include" / "verbo_cuda.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

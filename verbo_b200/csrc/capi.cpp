@@ -149,6 +149,28 @@ void attach_split_scratch(vb::RowArgs& a, const vb::DevOpts& o, bool greedy, cud
   vb::split_scratch_attach(a, sc.data, l, win_w);
 }
 
+// Scratch of the streaming full-vocabulary path, one buffer per (device,
+// stream): per-row state, the claim counter, the list of rows left to the
+// staged kernel and the histogram slots (nucleus.cu).  Grown on demand.
+std::map<std::pair<int, cudaStream_t>, Scratch> g_nuc_scratch;
+
+void* nucleus_scratch(int rows, int ncols, cudaStream_t s) {
+  int dev = 0;
+  cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
+  const size_t bytes = vb::nucleus_scratch_bytes(rows, ncols);
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  Scratch& sc = g_nuc_scratch[{dev, s}];
+  if (sc.bytes < bytes) {
+    cuda_ok(cudaStreamSynchronize(s), "stream");  // the old buffer may still be in use
+    cudaFree(sc.data);
+    sc.data = nullptr;
+    sc.bytes = 0;
+    cuda_ok(cudaMalloc(&sc.data, bytes), "cudaMalloc scratch");
+    sc.bytes = bytes;
+  }
+  return sc.data;
+}
+
 // Slices of the split-row kernels: the fewest slices of <= kSplitSlice columns.
 void plan_split(vb::RowArgs& a) {
   a.cluster = (a.ncols + vb::kSplitSlice - 1) / vb::kSplitSlice;
@@ -174,7 +196,10 @@ void dispatch_rows(vb::RowArgs& a, const vb::DevOpts& o, int vocab, cudaStream_t
       a.win = ring;
       a.win_w = ring_w;
     }
-    e = vb::launch_general(a, o, s);
+    if (vb::nucleus_eligible(o, vocab) && a.col_off == 0 && a.ncols == vocab)
+      e = vb::launch_nucleus(a, o, nucleus_scratch(a.rows, a.ncols, s), s);
+    else
+      e = vb::launch_general(a, o, s);
   }
   cuda_ok(e, "kernel launch");
 }
@@ -419,6 +444,26 @@ VERBO_CUDA_API int verbo_cuda_check(void* stream) {
         if (tst) fail("tail device status " + std::to_string(tst));
         if (st) fail("device status " + std::to_string(st));
         return 0;
+      },
+      -1);
+}
+
+VERBO_CUDA_API int verbo_cuda_full_vocab_fallbacks(void* stream) {
+  return guard(
+      [&]() {
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        int dev = 0;
+        cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
+        void* data = nullptr;
+        {
+          std::lock_guard<std::mutex> lk(g_scratch_mu);
+          const auto it = g_nuc_scratch.find({dev, s});
+          if (it != g_nuc_scratch.end()) data = it->second.data;
+        }
+        if (!data) return 0;
+        unsigned n = 0;
+        cuda_ok(vb::nucleus_fallbacks(data, s, &n), "read fallback count");
+        return static_cast<int>(n);
       },
       -1);
 }

@@ -31,45 +31,13 @@
 
 #include "device.cuh"
 #include "kernels.cuh"
+#include "rowdev.cuh"
 
 namespace vb {
 
 __device__ unsigned int g_status;
 
 __device__ __forceinline__ void raise_status(unsigned bits) { atomicOr(&g_status, bits); }
-
-// Sampler::accept (src/sampler.cpp:43-48) of a batched stream on the device:
-// the ring keeps the last ring_len ids, which is all the penalty window reads.
-__device__ __forceinline__ void ring_append(const RowArgs& a, int row, int id) {
-  if (!a.ring_pos) return;
-  const long long p = a.ring_pos[row];
-  a.win[static_cast<long long>(row) * a.win_w + p % a.ring_len] = id;
-  a.ring_pos[row] = p + 1;
-}
-
-// xoroshiro128+ draw, Sampler::unit (src/sampler.cpp:33-41).
-__device__ __forceinline__ double rng_unit(unsigned long long& s1_io, unsigned long long& s0_io) {
-  unsigned long long s1 = s1_io;
-  const unsigned long long s0 = s0_io;
-  const unsigned long long r = s0 + s1;
-  s1_io = s0;
-  s1 ^= s1 << 23;
-  s0_io = s1 ^ s0 ^ (s1 >> 18) ^ (s0 >> 5);
-  return __dmul_rn(static_cast<double>(r >> 11), 1.0 / 9007199254740992.0);
-}
-
-__device__ __forceinline__ void write_stats(verbo_row_stats* st, double sum, double tot, double u, double dm,
-                                            double cm, int k, int keep, int id, int greedy) {
-  st->sum = sum;
-  st->tot = tot;
-  st->u = u;
-  st->draw_margin = dm;
-  st->cut_margin = cm;
-  st->k = k;
-  st->keep = keep;
-  st->id = id;
-  st->greedy = greedy;
-}
 
 // ======================================================== shared tail (top-k)
 struct TailShared {
@@ -617,11 +585,11 @@ __device__ void select_weighted(const GenCtx& x, bool by_mass, unsigned long lon
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 2) general_kernel(const RowArgs a, const DevOpts o) {
+// One row of the staged full-vocabulary path, run by every CTA of a cluster.
+__device__ __noinline__ void general_row(const RowArgs& a, const DevOpts& o, const int row) {
   cg::cluster_group cl = cg::this_cluster();
   const int C = a.cluster;
   const int crank = static_cast<int>(cl.block_rank());
-  const int row = blockIdx.x / C;
   const int lo = crank * a.slice;
   const int n = max(0, min(a.ncols - lo, a.slice));
   const float* src = a.logits + static_cast<long long>(row) * a.ld + lo;
@@ -1287,6 +1255,20 @@ __global__ void __launch_bounds__(kThreads, 2) general_kernel(const RowArgs a, c
   cluster_sync_all();
 }
 
+__global__ void __launch_bounds__(kThreads, 2) general_kernel(const RowArgs a, const DevOpts o) {
+  general_row(a, o, static_cast<int>(blockIdx.x) / a.cluster);
+}
+
+// The rows the streaming nucleus kernel listed as not settled (list[0, *count)),
+// one cluster per row at a time: a small grid whose clusters take every
+// (gridDim.x / cluster)-th listed row.
+__global__ void __launch_bounds__(kThreads, 2) general_list_kernel(const RowArgs a, const DevOpts o, const int* list,
+                                                                    const unsigned* count) {
+  const unsigned n = *count;
+  const unsigned step = gridDim.x / static_cast<unsigned>(a.cluster);
+  for (unsigned i = blockIdx.x / static_cast<unsigned>(a.cluster); i < n; i += step) general_row(a, o, list[i]);
+}
+
 // ================================================================ launchers
 size_t general_smem(int slice) {
   const size_t vwords = static_cast<size_t>(((slice + 4 + 3) / 4) * 4);
@@ -1326,6 +1308,27 @@ cudaError_t launch_general(const RowArgs& a, const DevOpts& o, cudaStream_t s) {
   return launch_cluster(general_kernel, a, o, a.rows * a.cluster, a.cluster, general_smem(a.slice), s);
 }
 
+cudaError_t launch_general_list(const RowArgs& a, const DevOpts& o, const int* list, const unsigned* count,
+                                int max_rows, cudaStream_t s) {
+  const size_t smem = general_smem(a.slice);
+  cudaError_t e =
+      cudaFuncSetAttribute(general_list_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(std::min(max_rows, 32) * a.cluster);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = a.cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, general_list_kernel, a, o, list, count);
+}
+
 cudaError_t launch_merge(const MergeArgs& a, const DevOpts& o, cudaStream_t s) {
   const size_t sm = merge_smem(a.nshards * a.k);
   cudaError_t e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
@@ -1342,7 +1345,11 @@ cudaError_t read_status(unsigned* st, bool clear, cudaStream_t s) {
   if (clear && *st) {
     const unsigned z = 0;
     e = cudaMemcpyToSymbol(g_status, &z, sizeof(unsigned));
+    if (e != cudaSuccess) return e;
   }
+  unsigned st2 = 0;
+  e = read_nucleus_status(&st2, clear);
+  *st |= st2;
   return e;
 }
 

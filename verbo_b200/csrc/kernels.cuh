@@ -114,6 +114,24 @@ struct MergeArgs {
 
 // Host launchers (kernels.cu).  Return a cudaError_t.
 cudaError_t launch_general(const RowArgs& a, const DevOpts& o, cudaStream_t s);
+// The staged full-vocabulary kernel over the rows list[0, *count) (device
+// memory, read when the kernel starts); max_rows bounds *count.
+cudaError_t launch_general_list(const RowArgs& a, const DevOpts& o, const int* list, const unsigned* count,
+                                int max_rows, cudaStream_t s);
+
+// Streaming full-vocabulary path (nucleus.cu): top_k == 0 or >= vocab,
+// min_p == 0, no penalty, vocab >= kNucleusMinVocab.  One persistent kernel
+// reads every row once from HBM and settles almost every row; the rest go to
+// the staged kernel above (launched by launch_nucleus on the same stream).
+constexpr int kNucleusMinVocab = 4096;
+bool nucleus_eligible(const DevOpts& o, int vocab);
+size_t nucleus_scratch_bytes(int rows, int ncols);
+cudaError_t launch_nucleus(const RowArgs& a, const DevOpts& o, void* scratch, cudaStream_t s);
+// Rows of the last launch_nucleus on `scratch` that went to the staged kernel
+// (synchronises the stream).
+cudaError_t nucleus_fallbacks(const void* scratch, cudaStream_t s, unsigned* out);
+// Device-side failures of the nucleus kernel (bounded waits that ran out).
+cudaError_t read_nucleus_status(unsigned* st, bool clear);
 cudaError_t launch_merge(const MergeArgs& a, const DevOpts& o, cudaStream_t s);
 size_t general_smem(int slice);
 cudaError_t read_status(unsigned* st, bool clear, cudaStream_t s);

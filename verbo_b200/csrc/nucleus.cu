@@ -1,0 +1,1026 @@
+// Streaming full-vocabulary path of Sampler::pick (src/sampler.cpp:71-108 with
+// top_k == 0 or top_k >= vocab): the full sort, the softmax over every
+// column, the top-p cutoff and the inverse-CDF draw, without sorting and with
+// every logits row read from HBM once.
+//
+// Three streaming kernels, each over every (row, slice of <= kSliceCols
+// columns) with one CTA per slice and no CTA ever waiting for another:
+//
+//   nuc_a_kernel  streams the slice from HBM and publishes its maximum and its
+//                 smallest finite value (row atomics);
+//   nuc_b_kernel  takes the row maximum M and builds an exact histogram of the
+//                 slice's masses exp((v - M) / temp) over fine cells of
+//                 x = (v - M) / temp.  The row's last slice to finish (a
+//                 per-row counter) merges the slices' histograms and places the
+//                 top-p cutoff (src/sampler.cpp:92-100) and the draw (:101-108)
+//                 in one or two cells each;
+//   nuc_c_kernel  gathers the slice's members of those cells; the row's last
+//                 slice resolves the pick among them with the reference's fp64
+//                 weights, in the reference's order.
+//
+// The B and C kernels run over chunks of kChunkRows rows so that the slices'
+// histograms and the gathered members need scratch for one chunk only.
+//
+// Exact masses without an exponential per column: cell j holds the columns
+// whose x rounds to -j 2^-K; with r = x + j 2^-K (|r| <= 2^-(K+1)),
+// exp(x) = exp(-j 2^-K) (1 + e(r)), e(r) = r + r^2/2 + r^3/6 evaluated in fp32
+// and summed per cell in fixed point (2^-(K+22) units) with 32-bit shared
+// atomics; the merge applies exp(-j 2^-K) once per cell in fp64.  Cumulative
+// masses are within a few 1e-9 of the reference's sequential fp64 sums
+// (kDelta bounds it), and the members of the cells where the decisions fall
+// are resolved with exp((double)(v - M) / temp) as the reference computes it.
+//
+// Rows this path cannot settle exactly (a non-finite maximum, a cell holding
+// more columns than its fixed-point sum allows, a decision outside the cells,
+// too many members) are listed for the staged cluster kernel of kernels.cu,
+// which launch_nucleus runs next on the same stream.
+//
+#include <algorithm>
+#include <cstdint>
+
+#include "device.cuh"
+#include "kernels.cuh"
+#include "rowdev.cuh"
+
+namespace vb {
+namespace nuc {
+
+constexpr int NT = 256;
+constexpr int kW = NT / 32;
+constexpr int kSliceCols = 32768;    // columns of one slice (at most)
+constexpr int kChunkRows = 512;      // rows per B / C launch (their scratch)
+constexpr int kCells = 2048;         // histogram capacity
+constexpr int kCellTarget = 1024;    // the row's x-range is spread over about this many cells
+constexpr int kKMin = 6;             // cells at most 2^-6 wide: |r| <= 2^-7
+constexpr int kKMax = 20;
+constexpr unsigned kCellCap = 1000;  // columns per cell and slice that keep the fixed-point sum exact
+constexpr int kMemberCap = 2048;     // members gathered for the decisions
+constexpr int kSubBins = NT;         // sub-bins of the resolve step
+constexpr double kDelta = 4e-9;      // bound on the histogram's cumulative error, relative to the row's sum
+constexpr unsigned kMagic23 = 0x4B400000u;  // bits of 1.5 * 2^23
+
+__device__ unsigned g_nuc_status;
+
+// ------------------------------------------------------------ the grid ----
+// Cells of x = (v - M) * (1 / temp) of width 2^-K: cell j (0 <= j <= ncr)
+// holds the x that round to -j 2^-K.  x below xcut is "underflow" (mass below
+// e^-31 of the maximum's): it only adds to the row's sum.
+struct Grid {
+  float M, ih, il;   // 1 / temp = ih + il (fp32 pair)
+  float magic;       // 1.5 * 2^(23 - K): adding it rounds to a multiple of 2^-K
+  float xcut;        // -(ncr - 1/2) 2^-K
+  float two_s;       // 2^S, S = K + 22
+  unsigned magic_bits;
+  int K, S, ncr;
+};
+
+__device__ Grid make_grid(float M, float mlo, float temp) {
+  Grid g;
+  g.M = M;
+  const double it = 1.0 / static_cast<double>(temp);
+  g.ih = static_cast<float>(it);
+  g.il = static_cast<float>(it - static_cast<double>(g.ih));
+  const double xr = (static_cast<double>(M) - static_cast<double>(mlo)) * it;  // >= 0
+  int K = kKMax;
+  if (xr > 0.0) K = max(kKMin, min(kKMax, static_cast<int>(floor(log2((kCellTarget - 1) / xr)))));
+  g.K = K;
+  g.S = K + 22;
+  g.ncr = static_cast<int>(fmin(floor(ldexp(xr, K)) + 2.0, static_cast<double>(kCells - 2)));
+  g.xcut = static_cast<float>(-ldexp(static_cast<double>(g.ncr) - 0.5, -K));
+  g.magic = ldexpf(1.5f, 23 - K);
+  g.magic_bits = __float_as_uint(g.magic);
+  g.two_s = ldexpf(1.0f, g.S);
+  return g;
+}
+
+// d = v - M in fp32 as the reference rounds it (src/sampler.cpp:81) and
+// x = d / temp in fp32, monotone in v; the same expressions everywhere.  A NaN
+// v gives NaN (never in a cell), -0 the same as +0.
+__device__ __forceinline__ float xof(float v, const Grid& g, float* d_out) {
+  const float d = __fsub_rn(v, g.M);
+  *d_out = d;
+  return __fmul_rn(d, g.ih);
+}
+// Cell of x (only for x >= g.xcut); *t_out = x rounded to the grid + magic.
+__device__ __forceinline__ int cell_of(float xh, const Grid& g, float* t_out) {
+  const float t = __fadd_rn(xh, g.magic);
+  *t_out = t;
+  return static_cast<int>(g.magic_bits - __float_as_uint(t));
+}
+// Cell of a column value, or -1 outside the cells.
+__device__ __forceinline__ int cell_of_v(float v, const Grid& g) {
+  float d, t;
+  const float xh = xof(v, g, &d);
+  return xh >= g.xcut ? cell_of(xh, g, &t) : -1;
+}
+
+// --------------------------------------------------------- the scratch ----
+struct RowState {
+  unsigned maxkey;      // ord32 of the row maximum (atomicMax)
+  unsigned minkey_inv;  // ~ord32 of the smallest finite value (atomicMax); 0 = none
+  unsigned cnt2;        // B slices done
+  unsigned cnt3;        // C slices done
+};
+struct SliceSum {
+  unsigned ucount;   // underflow columns
+  unsigned crowded;  // a cell above kCellCap columns
+  double umass;      // approximate mass of the underflow columns
+};
+// What the B merge leaves for the C kernel (per row of the chunk).
+struct Targets {
+  int fail;            // the row goes to the staged kernel
+  int use_p;           // a top-p cutoff applies
+  int A0, A1, B0, B1;  // cells of the cutoff and of the draw
+  float a_lo, a_hi, b_lo, b_hi;  // value intervals holding their members
+  unsigned cut_before;  // columns before A0
+  unsigned nmem;        // members gathered (C slices, atomic)
+  double cut_base, draw_base;  // cumulative mass before A0 / B0
+  double S, tp, u;
+  unsigned long long s1, s0;   // the row's RNG state after this pick's draw
+};
+
+struct NucArgs {
+  RowArgs a;
+  int ns;            // slices per row
+  int slice;         // columns per slice (multiple of 4)
+  int row0;          // first row of the chunk (B, C kernels)
+  unsigned* fb_count;   // rows listed for the staged kernel
+  RowState* rs;         // [rows]
+  int* fb_list;         // [rows]
+  SliceSum* sums;       // [kChunkRows][ns]
+  uint2* cells;         // [kChunkRows][ns][kCells]: (count, sum of the fixed-point words)
+  Targets* tg;          // [kChunkRows]
+  unsigned long long* members;  // [kChunkRows][kMemberCap] keys
+};
+
+// Scratch layout; the first `zero_bytes` are cleared before every call.
+struct Layout {
+  size_t off_rs, zero_bytes, off_fb, off_sum, off_cells, off_tg, off_mem, bytes;
+};
+static size_t up256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+static Layout layout(int rows, int ns) {
+  const size_t cr = static_cast<size_t>(std::min(rows, kChunkRows));
+  Layout l;
+  l.off_rs = 256;
+  l.zero_bytes = l.off_rs + sizeof(RowState) * static_cast<size_t>(rows);
+  l.off_fb = up256(l.zero_bytes);
+  l.off_sum = up256(l.off_fb + sizeof(int) * static_cast<size_t>(rows));
+  l.off_cells = up256(l.off_sum + sizeof(SliceSum) * cr * static_cast<size_t>(ns));
+  l.off_tg = up256(l.off_cells + sizeof(uint2) * kCells * cr * static_cast<size_t>(ns));
+  l.off_mem = up256(l.off_tg + sizeof(Targets) * cr);
+  l.bytes = up256(l.off_mem + sizeof(unsigned long long) * kMemberCap * cr);
+  return l;
+}
+
+// --------------------------------------------------------- streaming ------
+// f(value, column) for every column of [0, n) of src, each once: a scalar head
+// up to the first 16-byte boundary, the body in 16-byte loads (kU in flight
+// per thread), a scalar tail.  kHbm: streaming loads that keep the lines in
+// L2 for the later passes; otherwise L2-only loads.
+template <int kU, bool kHbm, class F>
+__device__ __forceinline__ void each_col(const float* src, int n, F&& f) {
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(src);
+  int h = static_cast<int>(((16 - (addr & 15)) & 15) >> 2);
+  if (h > n) h = n;
+  if (static_cast<int>(threadIdx.x) < h) f(src[threadIdx.x], static_cast<int>(threadIdx.x));
+  const float4* b4 = reinterpret_cast<const float4*>(src + h);
+  const int n4 = (n - h) >> 2;
+  int q = threadIdx.x;
+  for (; q + (kU - 1) * NT < n4; q += kU * NT) {
+    float4 t[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) t[u] = kHbm ? ld_stream(b4 + q + u * NT) : __ldcg(b4 + q + u * NT);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int j = h + 4 * (q + u * NT);
+      f(t[u].x, j);
+      f(t[u].y, j + 1);
+      f(t[u].z, j + 2);
+      f(t[u].w, j + 3);
+    }
+  }
+  for (; q < n4; q += NT) {
+    const float4 t = kHbm ? ld_stream(b4 + q) : __ldcg(b4 + q);
+    const int j = h + 4 * q;
+    f(t.x, j);
+    f(t.y, j + 1);
+    f(t.z, j + 2);
+    f(t.w, j + 3);
+  }
+  for (int j = h + 4 * n4 + threadIdx.x; j < n; j += NT) f(src[j], j);
+}
+
+// Software-pipelined traversal for the compute-carrying passes: rounds of kU
+// 16-byte streaming loads per thread, the next round issued before the
+// current one is processed, so a round's latency overlaps the previous
+// round's work.  f4(float4, column of .x) for the aligned body, f1(value,
+// column) for the scalar head and tail.
+template <int kU, class F4, class F1>
+__device__ __forceinline__ void each_col_pipe(const float* src, int n, F4&& f4, F1&& f1) {
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(src);
+  int h = static_cast<int>(((16 - (addr & 15)) & 15) >> 2);
+  if (h > n) h = n;
+  if (static_cast<int>(threadIdx.x) < h) f1(src[threadIdx.x], static_cast<int>(threadIdx.x));
+  const float4* b4 = reinterpret_cast<const float4*>(src + h);
+  const int n4 = (n - h) >> 2;
+  constexpr int R = kU * NT;  // vectors per round
+  const int rounds = n4 / R;  // full rounds
+  float4 cur[kU], nxt[kU];
+  if (rounds > 0) {
+#pragma unroll
+    for (int u = 0; u < kU; ++u) cur[u] = ld_stream(b4 + threadIdx.x + u * NT);
+  }
+  for (int r = 0; r < rounds; ++r) {
+    const int q = r * R + threadIdx.x;
+    if (r + 1 < rounds) {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) nxt[u] = ld_stream(b4 + q + R + u * NT);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) f4(cur[u], h + 4 * (q + u * NT));
+#pragma unroll
+    for (int u = 0; u < kU; ++u) cur[u] = nxt[u];
+  }
+  for (int q = rounds * R + threadIdx.x; q < n4; q += NT) f4(ld_stream(b4 + q), h + 4 * q);
+  for (int j = h + 4 * n4 + threadIdx.x; j < n; j += NT) f1(src[j], j);
+}
+
+// -------------------------------------------------------------- shared ----
+struct Shared {
+  NucArgs p;  // the kernel parameters, copied here so that every function reads them from shared memory
+  DevOpts o;
+  Grid g;     // the grid of the row at hand
+  unsigned mbase;  // C items: first member slot reserved by this CTA
+  int kind, row, slice;
+  int last;
+  int flag;
+  float wsf[kW];
+  unsigned wsu[kW];
+  double wsd[kW];
+  int c_lo, c_hi, d_lo, d_hi;
+  unsigned nmem;
+  int sb;  // resolve: target sub-bin
+  double sb_base;
+  unsigned sb_n, sb_cnt_before;
+  int r_found;
+  unsigned long long r_key;
+  double r_cum;
+  unsigned r_rank;
+};
+
+// Dynamic shared memory: B items [kCells] counts + [kCells] fixed-point sums;
+// the B merge [kCells] doubles + [kCells] counts; the C merge the member keys,
+// their weights, a sort buffer and the sub-bins.
+constexpr size_t kHistBytes = static_cast<size_t>(kCells) * 8;
+constexpr size_t kCumBytes = static_cast<size_t>(kCells) * 12;
+constexpr size_t kMemberBytes = static_cast<size_t>(kMemberCap) * 24 + static_cast<size_t>(kSubBins) * 12;
+constexpr size_t kBSmem = std::max(kHistBytes, kCumBytes);             // B slices and the B merge
+constexpr size_t kCSmem = std::max(static_cast<size_t>(kMemberCap) * 8, kMemberBytes);  // C slices and the C merge
+
+template <class T>
+__device__ __forceinline__ T bsum(T x, T* ws) {
+  x = warp_sum(x);
+  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = x;
+  __syncthreads();
+  T r = ws[0];
+#pragma unroll
+  for (int i = 1; i < kW; ++i) r += ws[i];
+  __syncthreads();
+  return r;
+}
+
+// Block scan of (w, c) pairs in thread order: exclusive prefixes and totals.
+__device__ __noinline__ void bscan(double w, unsigned c, Shared& sh, double* wpre, unsigned* cpre, double* wtot,
+                                   unsigned* ctot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double wi = w;
+  unsigned ci = c;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const double y = __shfl_up_sync(0xffffffffu, wi, off);
+    const unsigned cy = __shfl_up_sync(0xffffffffu, ci, off);
+    if (lane >= off) {
+      wi += y;
+      ci += cy;
+    }
+  }
+  if (lane == 31) {
+    sh.wsd[warp] = wi;
+    sh.wsu[warp] = ci;
+  }
+  __syncthreads();
+  double wp = 0.0, wt = 0.0;
+  unsigned cp = 0, ct = 0;
+  for (int i = 0; i < kW; ++i) {
+    if (i < warp) {
+      wp += sh.wsd[i];
+      cp += sh.wsu[i];
+    }
+    wt += sh.wsd[i];
+    ct += sh.wsu[i];
+  }
+  __syncthreads();
+  *wpre = wp + wi - w;
+  *cpre = cp + ci - c;
+  *wtot = wt;
+  *ctot = ct;
+}
+
+// The row's grid from its published maximum and smallest finite value.
+__device__ __forceinline__ Grid row_grid(const RowState* st, float temp) {
+  const unsigned mk = __ldcg(&st->maxkey);
+  const unsigned nk = __ldcg(&st->minkey_inv);
+  const float M = unord32(mk);
+  const float mlo = nk != 0u ? unord32(~nk) : M;
+  return make_grid(M, isfinite(M) && isfinite(mlo) ? mlo : M, temp);
+}
+
+// The reference's weight of a column (src/sampler.cpp:81), fp64.
+__device__ __noinline__ double ref_weight(float v, float M, double temp_d) {
+  return exp(__ddiv_rn(static_cast<double>(__fsub_rn(canon(v), M)), temp_d));
+}
+
+__device__ __forceinline__ void to_fallback(const NucArgs& p, int row) {
+  const unsigned i = atomicAdd(p.fb_count, 1u);
+  p.fb_list[i] = row;
+}
+
+// ------------------------------------------------------------- A items ----
+__device__ __noinline__ void run_a(int row, int s, Shared& sh) {
+  const NucArgs& p = sh.p;
+  const RowArgs& a = p.a;
+  const int lo = s * p.slice;
+  const int n = min(p.slice, a.ncols - lo);
+  const float* src = a.logits + static_cast<long long>(row) * a.ld + lo;
+  const float ninf = -__int_as_float(0x7f800000), pinf = __int_as_float(0x7f800000);
+  float mx = ninf, mn = pinf;
+  each_col<8, true>(src, n, [&](float v, int) {
+    mx = fmaxf(mx, v);                    // a NaN never wins
+    mn = fminf(mn, v > ninf ? v : pinf);  // finite (and +inf) values only
+  });
+  mx = warp_max(mx);
+  mn = warp_min(mn);
+  if ((threadIdx.x & 31) == 0) {
+    sh.wsf[threadIdx.x >> 5] = mx;
+    sh.wsu[threadIdx.x >> 5] = __float_as_uint(mn);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < kW; ++i) {
+      mx = fmaxf(mx, sh.wsf[i]);
+      mn = fminf(mn, __uint_as_float(sh.wsu[i]));
+    }
+    RowState* st = p.rs + row;
+    atomicMax(&st->maxkey, ord32(canon(mx)));
+    if (mn < pinf) atomicMax(&st->minkey_inv, ~ord32(canon(mn)));
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------- B items ----
+__device__ __noinline__ void merge_b(int row, unsigned char* smem, Shared& sh);
+
+__device__ __noinline__ void run_b(int row, int s, unsigned char* smem, Shared& sh) {
+  const NucArgs& p = sh.p;
+  const DevOpts& o = sh.o;
+  const RowArgs& a = p.a;
+  RowState* st = p.rs + row;
+  const int slot = row - p.row0;
+  if (threadIdx.x == 0) sh.g = row_grid(st, o.temp);
+  __syncthreads();
+  const Grid g = sh.g;
+  unsigned* cnt = reinterpret_cast<unsigned*>(smem);
+  unsigned* esm = cnt + kCells;
+  const int nc = g.ncr + 1;
+  for (int c = threadIdx.x; c < nc; c += NT) {
+    cnt[c] = 0u;
+    esm[c] = 0u;
+  }
+  __syncthreads();
+  const int lo = s * p.slice;
+  const int n = min(p.slice, a.ncols - lo);
+  const float* src = a.logits + static_cast<long long>(row) * a.ld + lo;
+  unsigned uc = 0;
+  float um = 0.0f;
+  const float ninf = -__int_as_float(0x7f800000);
+  if (isfinite(g.M)) {
+    // per column: d and x in scalar fp32 with explicit rounding (the cell must
+    // be the same expression everywhere); the rest two columns at a time in
+    // packed fp32x2 arithmetic
+    const float2 ih2 = make_float2(g.ih, g.ih), il2 = make_float2(g.il, g.il);
+    const float2 nmagic2 = make_float2(-g.magic, -g.magic), two_s2 = make_float2(g.two_s, g.two_s);
+    const float2 c6 = make_float2(0.16666667f, 0.16666667f), c2 = make_float2(0.5f, 0.5f);
+    const float2 c1 = make_float2(1.0f, 1.0f), m23 = make_float2(12582912.0f, 12582912.0f);
+    auto one = [&](float d, float xh, float t, float y) {
+      if (xh >= g.xcut) {
+        const int idx = static_cast<int>(g.magic_bits - __float_as_uint(t));
+        atomicAdd(cnt + idx, 1u);
+        atomicAdd(esm + idx, __float_as_uint(y));
+      } else if (d > ninf) {  // finite and below the cells (NaN, -inf: weight 0)
+        ++uc;
+        um += __expf(xh);
+      }
+    };
+    auto two = [&](float va, float vb) {
+      float da, db;
+      const float xa = xof(va, g, &da), xb = xof(vb, g, &db);
+      const float ta = __fadd_rn(xa, g.magic), tb = __fadd_rn(xb, g.magic);
+      const float2 d2 = make_float2(da, db);
+      const float2 gg = __fadd2_rn(make_float2(ta, tb), nmagic2);       // -idx * 2^-K, exact
+      float2 r = __ffma2_rn(d2, ih2, make_float2(-gg.x, -gg.y));       // x - grid point
+      r = __ffma2_rn(d2, il2, r);
+      const float2 e = __fmul2_rn(r, __ffma2_rn(r, __ffma2_rn(r, c6, c2), c1));
+      const float2 y = __ffma2_rn(e, two_s2, m23);                      // bits: kMagic23 + round(e * 2^S)
+      one(da, xa, ta, y.x);
+      one(db, xb, tb, y.y);
+    };
+    each_col_pipe<4>(src, n, [&](const float4& v, int) {
+      two(v.x, v.y);
+      two(v.z, v.w);
+    }, [&](float v, int) {
+      float d;
+      const float xh = xof(v, g, &d);
+      const float t = __fadd_rn(xh, g.magic);
+      const float gg = __fsub_rn(t, g.magic);
+      float r = __fmaf_rn(d, g.ih, -gg);
+      r = __fmaf_rn(d, g.il, r);
+      const float e = __fmul_rn(r, __fmaf_rn(r, __fmaf_rn(r, 0.16666667f, 0.5f), 1.0f));
+      one(d, xh, t, __fmaf_rn(e, g.two_s, 12582912.0f));
+    });
+  }
+  __syncthreads();
+  // flush cells [0, nc) of this slice and its summary into the row's slot
+  uint2* out = p.cells + (static_cast<long long>(slot) * p.ns + s) * kCells;
+  unsigned crowded = 0;
+  for (int c = threadIdx.x; c < nc; c += NT) {
+    const uint2 v = make_uint2(cnt[c], esm[c]);
+    crowded |= v.x > kCellCap ? 1u : 0u;
+    __stcg(out + c, v);
+  }
+  uc = bsum(uc, sh.wsu);
+  crowded = bsum(crowded, sh.wsu);
+  const double umd = bsum(static_cast<double>(um), sh.wsd);
+  if (threadIdx.x == 0) {
+    SliceSum v;
+    v.ucount = uc;
+    v.crowded = crowded;
+    v.umass = umd;
+    p.sums[static_cast<long long>(slot) * p.ns + s] = v;
+    __threadfence();
+    const unsigned old = atomicAdd(&st->cnt2, 1u);
+    sh.last = old == static_cast<unsigned>(p.ns - 1);
+    __threadfence();
+  }
+  __syncthreads();
+  if (sh.last) merge_b(row, smem, sh);
+}
+
+// The row's merged histogram: per-cell cumulative masses, the cells of the
+// top-p cutoff (src/sampler.cpp:92-100) and of the draw (:101-108), and the
+// value intervals holding their members, published for the C items.
+__device__ __noinline__ void merge_b(int row, unsigned char* smem, Shared& sh) {
+  const NucArgs& p = sh.p;
+  const DevOpts& o = sh.o;
+  const Grid& g = sh.g;
+  const RowArgs& a = p.a;
+  const int slot = row - p.row0;
+  const int nc = g.ncr + 1;
+  double* cum = reinterpret_cast<double*>(smem);             // [kCells] inclusive cumulative mass
+  unsigned* cnt = reinterpret_cast<unsigned*>(cum + kCells);  // [kCells] columns before each cell
+  const uint2* cells = p.cells + static_cast<long long>(slot) * p.ns * kCells;
+  const SliceSum* sums = p.sums + static_cast<long long>(slot) * p.ns;
+  if (threadIdx.x == 0) {
+    int f = !isfinite(g.M);
+    for (int s = 0; s < p.ns; ++s) f |= __ldcg(&sums[s].crowded) != 0u;
+    sh.flag = f;
+    sh.c_lo = sh.c_hi = sh.d_lo = sh.d_hi = nc;
+  }
+  __syncthreads();
+  // per-cell sums over the slices: thread t takes the cell pairs 2t, 2t + 1
+  // (+ 2 NT, ...) and issues the 16-byte loads of two slices before adding
+  // any of them
+  const double unit = ldexp(1.0, -g.S);
+  {
+    constexpr int KP = kCells / (2 * NT);  // cell pairs per thread
+    constexpr int SB = 2;                  // slices per batch of loads
+    unsigned n[2 * KP];
+    long long e[2 * KP];
+#pragma unroll
+    for (int k = 0; k < 2 * KP; ++k) {
+      n[k] = 0;
+      e[k] = 0;
+    }
+    const uint4* cells4 = reinterpret_cast<const uint4*>(cells);
+    for (int s0 = 0; s0 < p.ns; s0 += SB) {
+      uint4 v[SB][KP];
+#pragma unroll
+      for (int b = 0; b < SB; ++b)
+#pragma unroll
+        for (int k = 0; k < KP; ++k) {
+          const int c = 2 * (threadIdx.x + k * NT);
+          v[b][k] = s0 + b < p.ns && c < nc ? __ldcg(cells4 + (static_cast<long long>(s0 + b) * kCells + c) / 2)
+                                            : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+      for (int b = 0; b < SB; ++b)
+#pragma unroll
+        for (int k = 0; k < KP; ++k) {
+          n[2 * k] += v[b][k].x;
+          e[2 * k] += static_cast<int>(v[b][k].y - v[b][k].x * kMagic23);
+          n[2 * k + 1] += v[b][k].z;
+          e[2 * k + 1] += static_cast<int>(v[b][k].w - v[b][k].z * kMagic23);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 2 * KP; ++k) {
+      const int c = 2 * (threadIdx.x + (k >> 1) * NT) + (k & 1);
+      if (c < nc) {
+        cum[c] = n[k] ? exp(-ldexp(static_cast<double>(c), -g.K)) *
+                            (static_cast<double>(n[k]) + static_cast<double>(e[k]) * unit)
+                      : 0.0;
+        cnt[c] = n[k];
+      }
+    }
+  }
+  __syncthreads();
+  // thread t owns cells [c0, c1) for the scans
+  const int cpt = (nc + NT - 1) / NT;
+  const int c0 = threadIdx.x * cpt, c1 = min(nc, c0 + cpt);
+  double local = 0.0;
+  unsigned lcnt = 0;
+  for (int c = c0; c < c1; ++c) {
+    local += cum[c];
+    lcnt += cnt[c];
+  }
+  double U = 0.0;
+  for (int s = 0; s < p.ns; ++s) U += __ldcg(&sums[s].umass);
+  double wpre, wtot;
+  unsigned cpre, ctot;
+  bscan(local, lcnt, sh, &wpre, &cpre, &wtot, &ctot);
+  {
+    double run = wpre;
+    unsigned crun = cpre;
+    for (int c = c0; c < c1; ++c) {
+      run += cum[c];
+      cum[c] = run;
+      const unsigned n = cnt[c];
+      cnt[c] = crun;
+      crun += n;
+    }
+  }
+  __syncthreads();
+  const double S = wtot + U;  // the softmax normaliser (src/sampler.cpp:80-85)
+  const double dl = kDelta * S;
+  auto first_reach = [&](double x, int* outc) {  // first cell whose cumulative mass reaches x
+    for (int c = c0; c < c1; ++c)
+      if (cum[c] >= x) {
+        atomicMin(outc, c);
+        break;
+      }
+  };
+  const bool use_p = o.top_p > 0.0f && o.top_p < 1.0f;
+  const double tp = use_p ? static_cast<double>(o.top_p) * S : 0.0;
+  if (use_p) {
+    first_reach(tp - dl, &sh.c_lo);
+    first_reach(tp + dl, &sh.c_hi);
+  }
+  // this pick's uniform (src/sampler.cpp:103)
+  unsigned long long s1 = 0, s0 = 0;
+  double u = 0.0;
+  if (a.rng) {
+    s1 = a.rng[2ll * row];
+    s0 = a.rng[2ll * row + 1];
+    u = rng_unit(s1, s0);
+  }
+  __syncthreads();
+  const int A0 = use_p ? sh.c_lo : nc, A1 = use_p ? sh.c_hi : -1;
+  bool fail = sh.flag != 0 || (use_p && (A0 >= nc || A1 >= nc));
+  // the range of the cutoff's running mass (all of S without a cutoff)
+  const double tot_lo = use_p && !fail ? (A0 > 0 ? cum[A0 - 1] : 0.0) : S;
+  const double tot_hi = use_p && !fail ? cum[A1] : S;
+  if (!fail && u * tot_hi + dl > wtot) fail = true;  // the draw may fall among the underflow columns
+  if (!fail) {
+    first_reach(u * tot_lo - dl, &sh.d_lo);
+    first_reach(u * tot_hi + dl, &sh.d_hi);
+  }
+  __syncthreads();
+  const int B0 = sh.d_lo, B1 = sh.d_hi;
+  if (threadIdx.x == 0) {
+    Targets* t = p.tg + slot;
+    auto before = [&](int c) -> unsigned { return c < nc ? cnt[c] : ctot; };
+    if (!fail && (B0 >= nc || B1 >= nc)) fail = true;
+    if (!fail) {
+      unsigned need = before(B1 + 1) - before(B0);
+      if (use_p) need += before(A1 + 1) - before(A0);
+      if (need > static_cast<unsigned>(kMemberCap)) fail = true;
+    }
+    t->fail = fail;
+    if (!fail) {
+      // value intervals holding every member of [A0, A1] and [B0, B1]: x of
+      // the cells' outer edges, widened by a hundredth of a cell and a
+      // relative 1e-5 for the fp32 roundings of x
+      const double temp_d = static_cast<double>(o.temp);
+      auto vbound = [&](int c, double side) -> float {
+        const double xb = -ldexp(static_cast<double>(c) - 0.5 * side, -g.K);
+        const double w = ldexp(0.01, -g.K) + 1e-5 * fabs(xb);
+        return static_cast<float>(static_cast<double>(g.M) + (xb + side * w) * temp_d);
+      };
+      t->use_p = use_p;
+      t->A0 = A0;
+      t->A1 = A1;
+      t->B0 = B0;
+      t->B1 = B1;
+      t->a_lo = use_p ? vbound(A1, -1.0) : __int_as_float(0x7f800000);
+      t->a_hi = use_p ? vbound(A0, 1.0) : -__int_as_float(0x7f800000);
+      t->b_lo = vbound(B1, -1.0);
+      t->b_hi = vbound(B0, 1.0);
+      t->cut_before = use_p ? before(A0) : 0u;
+      t->cut_base = use_p && A0 > 0 ? cum[A0 - 1] : 0.0;
+      t->draw_base = B0 > 0 ? cum[B0 - 1] : 0.0;
+      t->S = S;
+      t->tp = tp;
+      t->u = u;
+      t->s1 = s1;
+      t->s0 = s0;
+    }
+    t->nmem = 0;
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------- C items ----
+__device__ __noinline__ void merge_c(int row, unsigned char* smem, Shared& sh);
+
+__device__ __noinline__ void run_c(int row, int s, unsigned char* smem, Shared& sh) {
+  const NucArgs& p = sh.p;
+  const DevOpts& o = sh.o;
+  const RowArgs& a = p.a;
+  RowState* st = p.rs + row;
+  const int ms = row - p.row0;
+  const Targets* tg = p.tg + ms;
+  const int fail = __ldcg(&tg->fail);
+  if (!fail) {
+    // the slice's members go to shared memory first, then to the row's list
+    // with one reservation per CTA
+    if (threadIdx.x == 0) sh.nmem = 0;
+    __syncthreads();
+    const Grid g = row_grid(st, o.temp);
+    const int A0 = __ldcg(&tg->A0), A1 = __ldcg(&tg->A1), B0 = __ldcg(&tg->B0), B1 = __ldcg(&tg->B1);
+    const float a_lo = __ldcg(&tg->a_lo), a_hi = __ldcg(&tg->a_hi);
+    const float b_lo = __ldcg(&tg->b_lo), b_hi = __ldcg(&tg->b_hi);
+    unsigned long long* loc = reinterpret_cast<unsigned long long*>(smem);  // [kMemberCap]
+    const int lo = s * p.slice;
+    const int n = min(p.slice, a.ncols - lo);
+    const float* src = a.logits + static_cast<long long>(row) * a.ld + lo;
+    const unsigned gid0 = static_cast<unsigned>(a.col_off + lo);
+    auto test = [&](float v, int j) {
+      if ((v >= a_lo && v <= a_hi) || (v >= b_lo && v <= b_hi)) {
+        const int c = cell_of_v(v, g);
+        if ((c >= A0 && c <= A1) || (c >= B0 && c <= B1)) {
+          const unsigned q = atomicAdd(&sh.nmem, 1u);
+          if (q < static_cast<unsigned>(kMemberCap)) loc[q] = dkey(v, gid0 + static_cast<unsigned>(j));
+        }
+      }
+    };
+    each_col_pipe<4>(src, n, [&](const float4& v, int j) {
+      // one compare pair per vector decides whether any column needs a look
+      const float mn = fminf(fminf(v.x, v.y), fminf(v.z, v.w)), mx = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+      if ((mx >= a_lo && mn <= a_hi) || (mx >= b_lo && mn <= b_hi)) {
+        test(v.x, j);
+        test(v.y, j + 1);
+        test(v.z, j + 2);
+        test(v.w, j + 3);
+      }
+    }, test);
+    __syncthreads();
+    const unsigned cnt = min(sh.nmem, static_cast<unsigned>(kMemberCap));
+    if (threadIdx.x == 0) sh.mbase = cnt ? atomicAdd(&p.tg[ms].nmem, sh.nmem) : 0u;
+    __syncthreads();
+    unsigned long long* mem = p.members + static_cast<long long>(ms) * kMemberCap;
+    for (unsigned i = threadIdx.x; i < cnt; i += NT)
+      if (sh.mbase + i < static_cast<unsigned>(kMemberCap)) mem[sh.mbase + i] = loc[i];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned old = atomicAdd(&st->cnt3, 1u);
+    sh.last = old == static_cast<unsigned>(p.ns - 1);
+    __threadfence();
+  }
+  __syncthreads();
+  if (sh.last) merge_c(row, smem, sh);
+}
+
+// Among members [0, nm) (keys, exact weights), those in cells [c0, c1] in key
+// order: the first at which base + running weight reaches t (> base).  Sets
+// sh.r_found, r_key, r_cum (running weight through it) and r_rank (its rank
+// among the members of [c0, c1]).  Members are binned by x into kSubBins
+// sub-bins (monotone in key order) whose weights are scanned; only the target
+// sub-bin's members are sorted (one warp, at most 32); a crowded sub-bin
+// (ties) sorts every member of the range instead.
+__device__ __noinline__ void resolve(const unsigned long long* mkey, const double* mw, int nm, int c0, int c1,
+                                     double base, double t, double temp_d, double* sbm, unsigned* sbc,
+                                     unsigned long long* buf, Shared& sh) {
+  const Grid g = sh.g;
+  const float xtop = static_cast<float>(-ldexp(static_cast<double>(c0) - 0.5, -g.K));  // upper edge of c0
+  const float scale = static_cast<float>(ldexp(static_cast<double>(kSubBins), g.K) / (c1 - c0 + 1));
+  auto sub_of = [&](unsigned long long k) -> int {  // -1: not in [c0, c1]
+    float d, tt;
+    const float xh = xof(dval(k), g, &d);
+    if (!(xh >= g.xcut)) return -1;
+    const int c = cell_of(xh, g, &tt);
+    if (c < c0 || c > c1) return -1;
+    const float uu = __fmul_rn(__fsub_rn(xtop, xh), scale);  // monotone in -x
+    return min(kSubBins - 1, max(0, static_cast<int>(uu)));
+  };
+  sbm[threadIdx.x] = 0.0;
+  sbc[threadIdx.x] = 0u;
+  __syncthreads();
+  for (int i = threadIdx.x; i < nm; i += NT) {
+    const int b = sub_of(mkey[i]);
+    if (b < 0) continue;
+    atomicAdd(&sbc[b], 1u);
+    atomicAdd(&sbm[b], mw[i]);
+  }
+  __syncthreads();
+  const double m = sbm[threadIdx.x];
+  const unsigned c = sbc[threadIdx.x];
+  double wpre, wtot;
+  unsigned cpre, ctot;
+  bscan(m, c, sh, &wpre, &cpre, &wtot, &ctot);
+  if (threadIdx.x == 0) sh.sb = -1;
+  __syncthreads();
+  const double before = base + wpre;
+  if (c > 0 && before < t && t <= before + m) {
+    sh.sb = threadIdx.x;
+    sh.sb_base = before;
+    sh.sb_n = c;
+    sh.sb_cnt_before = cpre;
+  }
+  __syncthreads();
+  const int sb = sh.sb;
+  if (sb < 0) {
+    if (threadIdx.x == 0) sh.r_found = 0;
+    __syncthreads();
+    return;
+  }
+  const int lane = threadIdx.x & 31;
+  if (sh.sb_n <= 32u) {
+    if (threadIdx.x == 0) sh.nmem = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < nm; i += NT)
+      if (sub_of(mkey[i]) == sb) {
+        const unsigned q = atomicAdd(&sh.nmem, 1u);
+        if (q < 32u) buf[q] = static_cast<unsigned long long>(i);
+      }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const int cnt = static_cast<int>(min(sh.nmem, 32u));
+      const bool have = lane < cnt;
+      unsigned long long k = have ? mkey[buf[lane]] : kNoKey;
+      double w = have ? mw[buf[lane]] : 0.0;
+#pragma unroll
+      for (int kk = 2; kk <= 32; kk <<= 1) {
+#pragma unroll
+        for (int j = kk >> 1; j > 0; j >>= 1) {  // ascending bitonic sort by key, weight alongside
+          const unsigned long long pk = __shfl_xor_sync(0xffffffffu, k, j);
+          const double pw = __shfl_xor_sync(0xffffffffu, w, j);
+          const bool take_min = ((lane & j) == 0) == ((lane & kk) == 0);
+          if (take_min ? (pk < k) : (pk > k)) {
+            k = pk;
+            w = pw;
+          }
+        }
+      }
+      double inc = w;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += y;
+      }
+      const unsigned hits = __ballot_sync(0xffffffffu, have && sh.sb_base + inc >= t);
+      const int L = hits ? __ffs(hits) - 1 : 0;
+      const unsigned long long kL = __shfl_sync(0xffffffffu, k, L);
+      const double iL = __shfl_sync(0xffffffffu, inc, L);
+      if (lane == 0) {
+        sh.r_found = hits != 0 && sh.nmem <= 32u;
+        sh.r_key = kL;
+        sh.r_cum = sh.sb_base + iL;
+        sh.r_rank = sh.sb_cnt_before + static_cast<unsigned>(L);
+      }
+    }
+    __syncthreads();
+    return;
+  }
+  // crowded sub-bin (ties): sort every member of [c0, c1] by key and walk them
+  if (threadIdx.x == 0) sh.nmem = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < nm; i += NT)
+    if (sub_of(mkey[i]) >= 0) buf[atomicAdd(&sh.nmem, 1u)] = mkey[i];
+  __syncthreads();
+  const int cnt = static_cast<int>(sh.nmem);
+  const int P = next_pow2(max(cnt, 2));
+  for (int i = cnt + threadIdx.x; i < P; i += NT) buf[i] = kNoKey;
+  __syncthreads();
+  bitonic_sort_u64(reinterpret_cast<uint64_t*>(buf), P);
+  if (threadIdx.x == 0) {
+    double cm = base;
+    int hit = -1;
+    for (int i = 0; i < cnt; ++i) {
+      cm += ref_weight(dval(buf[i]), g.M, temp_d);
+      if (cm >= t) {
+        hit = i;
+        break;
+      }
+    }
+    sh.r_found = hit >= 0;
+    if (hit >= 0) {
+      sh.r_key = buf[hit];
+      sh.r_cum = cm;
+      sh.r_rank = static_cast<unsigned>(hit);
+    }
+  }
+  __syncthreads();
+}
+
+// The row's pick among the gathered members: the top-p cutoff, then the draw
+// within the kept prefix; results stored, or the row listed for the staged
+// kernel.
+__device__ __noinline__ void merge_c(int row, unsigned char* smem, Shared& sh) {
+  const NucArgs& p = sh.p;
+  const DevOpts& o = sh.o;
+  const RowArgs& a = p.a;
+  const int ms = row - p.row0;
+  const Targets* tg = p.tg + ms;
+  if (threadIdx.x == 0) sh.g = row_grid(p.rs + row, o.temp);
+  __syncthreads();
+  const Grid g = sh.g;
+  unsigned long long* mkey = reinterpret_cast<unsigned long long*>(smem);
+  double* mw = reinterpret_cast<double*>(mkey + kMemberCap);
+  unsigned long long* buf = reinterpret_cast<unsigned long long*>(mw + kMemberCap);
+  double* sbm = reinterpret_cast<double*>(buf + kMemberCap);
+  unsigned* sbc = reinterpret_cast<unsigned*>(sbm + kSubBins);
+  bool ok = __ldcg(&tg->fail) == 0;
+  const unsigned nmem = __ldcg(&tg->nmem);
+  if (nmem > static_cast<unsigned>(kMemberCap)) ok = false;
+  const int nm = static_cast<int>(min(nmem, static_cast<unsigned>(kMemberCap)));
+  const double temp_d = static_cast<double>(o.temp);
+  if (ok) {
+    const unsigned long long* mem = p.members + static_cast<long long>(ms) * kMemberCap;
+    for (int i = threadIdx.x; i < nm; i += NT) {
+      const unsigned long long k = __ldcg(mem + i);
+      mkey[i] = k;
+      mw[i] = ref_weight(dval(k), g.M, temp_d);
+    }
+  }
+  __syncthreads();
+  double tot = 0.0;
+  unsigned keep = static_cast<unsigned>(o.k);
+  int out_id = 0;
+  if (ok) {
+    const int use_p = __ldcg(&tg->use_p);
+    const int A0 = __ldcg(&tg->A0), A1 = __ldcg(&tg->A1), B0 = __ldcg(&tg->B0), B1 = __ldcg(&tg->B1);
+    const double S = __ldcg(&tg->S), u = __ldcg(&tg->u);
+    tot = S;
+    unsigned long long cut_key = kNoKey;
+    if (use_p) {  // the cutoff: first member at which the running mass reaches top_p * S
+      resolve(mkey, mw, nm, A0, A1, __ldcg(&tg->cut_base), __ldcg(&tg->tp), temp_d, sbm, sbc, buf, sh);
+      ok = sh.r_found != 0;
+      tot = sh.r_cum;
+      keep = __ldcg(&tg->cut_before) + sh.r_rank + 1u;
+      cut_key = sh.r_key;
+    }
+    if (ok) {  // the draw: first kept member at which the running mass reaches u * tot
+      const double r = u * tot;
+      const double t = r > 0.0 ? r : 4.9406564584124654e-324;
+      const double draw_base = __ldcg(&tg->draw_base);
+      if (!(t > draw_base)) {
+        ok = false;
+      } else {
+        resolve(mkey, mw, nm, B0, B1, draw_base, t, temp_d, sbm, sbc, buf, sh);
+        ok = sh.r_found != 0 && sh.r_key <= cut_key;
+        out_id = static_cast<int>(did(sh.r_key));
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (!ok) {
+      to_fallback(p, row);
+    } else {
+      if (a.rng) {
+        a.rng[2ll * row] = __ldcg(&tg->s1);
+        a.rng[2ll * row + 1] = __ldcg(&tg->s0);
+      }
+      a.out_ids[row] = out_id;
+      ring_append(a, row, out_id);
+      if (a.stats) {
+        const double nan = __longlong_as_double(0x7ff8000000000000ll);
+        write_stats(a.stats + row, __ldcg(&tg->S), tot, __ldcg(&tg->u), nan, nan, o.k, static_cast<int>(keep),
+                    out_id, 0);
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------- kernels ----
+// One CTA per (row, slice): blockIdx.x = (row - row0) * ns + slice.
+__device__ __forceinline__ void setup(const NucArgs& p, const DevOpts& o, Shared& sh) {
+  if (threadIdx.x == 0) {
+    sh.p = p;
+    sh.o = o;
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(NT, 6) nuc_a_kernel(const NucArgs p, const DevOpts o) {
+  __shared__ Shared sh;
+  setup(p, o, sh);
+  run_a(p.row0 + static_cast<int>(blockIdx.x) / p.ns, static_cast<int>(blockIdx.x) % p.ns, sh);
+}
+
+__global__ void __launch_bounds__(NT, 4) nuc_b_kernel(const NucArgs p, const DevOpts o) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ Shared sh;
+  setup(p, o, sh);
+  run_b(p.row0 + static_cast<int>(blockIdx.x) / p.ns, static_cast<int>(blockIdx.x) % p.ns, smem, sh);
+}
+
+__global__ void __launch_bounds__(NT, 4) nuc_c_kernel(const NucArgs p, const DevOpts o) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ Shared sh;
+  setup(p, o, sh);
+  run_c(p.row0 + static_cast<int>(blockIdx.x) / p.ns, static_cast<int>(blockIdx.x) % p.ns, smem, sh);
+}
+
+}  // namespace nuc
+
+// ------------------------------------------------------------- launcher ---
+bool nucleus_eligible(const DevOpts& o, int vocab) {
+  return !o.greedy && o.k >= vocab && !(o.min_p > 0.0f) && !o.penalize && vocab >= kNucleusMinVocab;
+}
+
+static int slices_of(int ncols) { return (ncols + nuc::kSliceCols - 1) / nuc::kSliceCols; }
+
+size_t nucleus_scratch_bytes(int rows, int ncols) { return nuc::layout(rows, slices_of(ncols)).bytes; }
+
+cudaError_t launch_nucleus(const RowArgs& a, const DevOpts& o, void* scratch, cudaStream_t s) {
+  using namespace nuc;
+  const int ns = slices_of(a.ncols);
+  const Layout l = layout(a.rows, ns);
+  char* b = static_cast<char*>(scratch);
+  cudaError_t e = cudaMemsetAsync(b, 0, l.zero_bytes, s);
+  if (e != cudaSuccess) return e;
+  NucArgs p;
+  p.a = a;
+  p.ns = ns;
+  p.slice = (((a.ncols + ns - 1) / ns) + 3) & ~3;
+  p.row0 = 0;
+  p.fb_count = reinterpret_cast<unsigned*>(b);
+  p.rs = reinterpret_cast<RowState*>(b + l.off_rs);
+  p.fb_list = reinterpret_cast<int*>(b + l.off_fb);
+  p.sums = reinterpret_cast<SliceSum*>(b + l.off_sum);
+  p.cells = reinterpret_cast<uint2*>(b + l.off_cells);
+  p.tg = reinterpret_cast<Targets*>(b + l.off_tg);
+  p.members = reinterpret_cast<unsigned long long*>(b + l.off_mem);
+  static bool attrs = false;
+  if (!attrs) {
+    e = cudaFuncSetAttribute(nuc_b_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBSmem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(nuc_c_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kCSmem));
+    if (e != cudaSuccess) return e;
+    attrs = true;
+  }
+  nuc_a_kernel<<<a.rows * ns, NT, 0, s>>>(p, o);
+  for (int r0 = 0; r0 < a.rows; r0 += kChunkRows) {
+    p.row0 = r0;
+    const int n = std::min(kChunkRows, a.rows - r0);
+    nuc_b_kernel<<<n * ns, NT, kBSmem, s>>>(p, o);
+    nuc_c_kernel<<<n * ns, NT, kCSmem, s>>>(p, o);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // the rows it could not settle, on the staged cluster kernel
+  return launch_general_list(a, o, p.fb_list, p.fb_count, a.rows, s);
+}
+
+cudaError_t nucleus_fallbacks(const void* scratch, cudaStream_t s, unsigned* out) {
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return e;
+  unsigned c = 0;
+  e = cudaMemcpy(&c, scratch, sizeof(c), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) *out = c;
+  return e;
+}
+
+cudaError_t read_nucleus_status(unsigned* st, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(st, nuc::g_nuc_status, sizeof(unsigned));
+  if (e != cudaSuccess) return e;
+  if (clear && *st) {
+    const unsigned z = 0;
+    e = cudaMemcpyToSymbol(nuc::g_nuc_status, &z, sizeof(unsigned));
+  }
+  return e;
+}
+
+}  // namespace vb
