@@ -6,20 +6,23 @@
 // Three streaming kernels, each over every (row, slice of <= kSliceCols
 // columns) with one CTA per slice and no CTA ever waiting for another:
 //
-//   nuc_a_kernel  streams the slice from HBM and publishes its maximum and its
+//   A  streams the slice from HBM and publishes its maximum and its
 //                 smallest finite value (row atomics);
-//   nuc_b_kernel  takes the row maximum M and builds an exact histogram of the
+//   B  takes the row maximum M and builds an exact histogram of the
 //                 slice's masses exp((v - M) / temp) over fine cells of
 //                 x = (v - M) / temp.  The row's last slice to finish (a
 //                 per-row counter) merges the slices' histograms and places the
 //                 top-p cutoff (src/sampler.cpp:92-100) and the draw (:101-108)
 //                 in one or two cells each;
-//   nuc_c_kernel  gathers the slice's members of those cells; the row's last
+//   C  gathers the slice's members of those cells; the row's last
 //                 slice resolves the pick among them with the reference's fp64
 //                 weights, in the reference's order.
 //
-// The B and C kernels run over chunks of kChunkRows rows so that the slices'
-// histograms and the gathered members need scratch for one chunk only.
+// Rows go in chunks of kChunkRows; launch t of nuc_kernel runs A of chunk t,
+// B of chunk t - 1 and C of chunk t - 2 side by side (their CTAs interleaved),
+// so that the HBM-bound A passes overlap the compute of the B passes.  Each
+// phase only reads what an earlier launch wrote, and the histograms, targets
+// and members live in two chunk-sized buffers used by alternate chunks.
 //
 // Exact masses without an exponential per column: cell j holds the columns
 // whose x rounds to -j 2^-K; with r = x + j 2^-K (|r| <= 2^-(K+1)),
@@ -63,12 +66,14 @@ __device__ unsigned g_nuc_status;
 
 // ------------------------------------------------------------ the grid ----
 // Cells of x = (v - M) * (1 / temp) of width 2^-K: cell j (0 <= j <= ncr)
-// holds the x that round to -j 2^-K.  x below xcut is "underflow" (mass below
-// e^-31 of the maximum's): it only adds to the row's sum.
+// holds the x that round to -j 2^-K.  A column whose x rounds below -ncr 2^-K
+// (mass below e^-31 of the maximum's, or weight 0 for -inf / NaN) is
+// "underflow": it only adds to the row's sum, and the B pass counts it in a
+// trash cell ncr + 1 (x is clamped there before rounding).
 struct Grid {
   float M, ih, il;   // 1 / temp = ih + il (fp32 pair)
   float magic;       // 1.5 * 2^(23 - K): adding it rounds to a multiple of 2^-K
-  float xcut;        // -(ncr - 1/2) 2^-K
+  float xcut;        // -(ncr + 1) 2^-K: x is clamped to it before rounding (the trash cell)
   float two_s;       // 2^S, S = K + 22
   unsigned magic_bits;
   int K, S, ncr;
@@ -86,7 +91,7 @@ __device__ Grid make_grid(float M, float mlo, float temp) {
   g.K = K;
   g.S = K + 22;
   g.ncr = static_cast<int>(fmin(floor(ldexp(xr, K)) + 2.0, static_cast<double>(kCells - 2)));
-  g.xcut = static_cast<float>(-ldexp(static_cast<double>(g.ncr) - 0.5, -K));
+  g.xcut = static_cast<float>(-ldexp(static_cast<double>(g.ncr) + 1.0, -K));
   g.magic = ldexpf(1.5f, 23 - K);
   g.magic_bits = __float_as_uint(g.magic);
   g.two_s = ldexpf(1.0f, g.S);
@@ -101,17 +106,48 @@ __device__ __forceinline__ float xof(float v, const Grid& g, float* d_out) {
   *d_out = d;
   return __fmul_rn(d, g.ih);
 }
-// Cell of x (only for x >= g.xcut); *t_out = x rounded to the grid + magic.
+// Cell of x: x clamped to xcut (NaN too), then rounded to the grid; cells
+// above ncr are underflow.  *t_out = the rounded x + magic.  The packed form in
+// run_b computes the same bits as -(clamped x) rounded with -magic.
 __device__ __forceinline__ int cell_of(float xh, const Grid& g, float* t_out) {
-  const float t = __fadd_rn(xh, g.magic);
+  const float t = __fadd_rn(fmaxf(xh, g.xcut), g.magic);
   *t_out = t;
   return static_cast<int>(g.magic_bits - __float_as_uint(t));
 }
-// Cell of a column value, or -1 outside the cells.
+// Cell of a column value, or -1 for underflow.
 __device__ __forceinline__ int cell_of_v(float v, const Grid& g) {
   float d, t;
-  const float xh = xof(v, g, &d);
-  return xh >= g.xcut ? cell_of(xh, g, &t) : -1;
+  const int c = cell_of(xof(v, g, &d), g, &t);
+  return c <= g.ncr ? c : -1;
+}
+
+// ---------------------------------------------- packed fp32x2 (sm_100) ----
+// Two fp32 lanes in one 64-bit register; explicit .rn so that ptxas never
+// contracts a multiply and an add into one rounding (the cell of a column
+// must be the same in every pass).
+typedef unsigned long long f2;
+__device__ __forceinline__ f2 f2pk(float lo, float hi) {
+  f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2up(f2 v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
 }
 
 // --------------------------------------------------------- the scratch ----
@@ -143,14 +179,15 @@ struct NucArgs {
   RowArgs a;
   int ns;            // slices per row
   int slice;         // columns per slice (multiple of 4)
-  int row0;          // first row of the chunk (B, C kernels)
+  int rowa, rowb, rowc;  // first row of this launch's A, B, C chunk
+  int na, nb, nc;        // rows of each (0: the phase has no chunk)
   unsigned* fb_count;   // rows listed for the staged kernel
   RowState* rs;         // [rows]
   int* fb_list;         // [rows]
-  SliceSum* sums;       // [kChunkRows][ns]
-  uint2* cells;         // [kChunkRows][ns][kCells]: (count, sum of the fixed-point words)
-  Targets* tg;          // [kChunkRows]
-  unsigned long long* members;  // [kChunkRows][kMemberCap] keys
+  SliceSum* sums;       // [2 kChunkRows][ns]   (slot = row mod 2 kChunkRows)
+  uint2* cells;         // [2 kChunkRows][ns][kCells]: (count, sum of the fixed-point words)
+  Targets* tg;          // [2 kChunkRows]
+  unsigned long long* members;  // [2 kChunkRows][kMemberCap] keys
 };
 
 // Scratch layout; the first `zero_bytes` are cleared before every call.
@@ -159,7 +196,7 @@ struct Layout {
 };
 static size_t up256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 static Layout layout(int rows, int ns) {
-  const size_t cr = static_cast<size_t>(std::min(rows, kChunkRows));
+  const size_t cr = static_cast<size_t>(std::min(rows, 2 * kChunkRows));
   Layout l;
   l.off_rs = 256;
   l.zero_bytes = l.off_rs + sizeof(RowState) * static_cast<size_t>(rows);
@@ -274,8 +311,7 @@ struct Shared {
 constexpr size_t kHistBytes = static_cast<size_t>(kCells) * 8;
 constexpr size_t kCumBytes = static_cast<size_t>(kCells) * 12;
 constexpr size_t kMemberBytes = static_cast<size_t>(kMemberCap) * 24 + static_cast<size_t>(kSubBins) * 12;
-constexpr size_t kBSmem = std::max(kHistBytes, kCumBytes);             // B slices and the B merge
-constexpr size_t kCSmem = std::max(static_cast<size_t>(kMemberCap) * 8, kMemberBytes);  // C slices and the C merge
+constexpr size_t kSmem = std::max(std::max(kHistBytes, kCumBytes), kMemberBytes);
 
 template <class T>
 __device__ __forceinline__ T bsum(T x, T* ws) {
@@ -385,14 +421,14 @@ __device__ __noinline__ void run_b(int row, int s, unsigned char* smem, Shared& 
   const DevOpts& o = sh.o;
   const RowArgs& a = p.a;
   RowState* st = p.rs + row;
-  const int slot = row - p.row0;
+  const int slot = row % (2 * kChunkRows);
   if (threadIdx.x == 0) sh.g = row_grid(st, o.temp);
   __syncthreads();
   const Grid g = sh.g;
   unsigned* cnt = reinterpret_cast<unsigned*>(smem);
   unsigned* esm = cnt + kCells;
   const int nc = g.ncr + 1;
-  for (int c = threadIdx.x; c < nc; c += NT) {
+  for (int c = threadIdx.x; c <= nc; c += NT) {  // nc: the trash cell
     cnt[c] = 0u;
     esm[c] = 0u;
   }
@@ -404,48 +440,52 @@ __device__ __noinline__ void run_b(int row, int s, unsigned char* smem, Shared& 
   float um = 0.0f;
   const float ninf = -__int_as_float(0x7f800000);
   if (isfinite(g.M)) {
-    // per column: d and x in scalar fp32 with explicit rounding (the cell must
-    // be the same expression everywhere); the rest two columns at a time in
-    // packed fp32x2 arithmetic
-    const float2 ih2 = make_float2(g.ih, g.ih), il2 = make_float2(g.il, g.il);
-    const float2 nmagic2 = make_float2(-g.magic, -g.magic), two_s2 = make_float2(g.two_s, g.two_s);
-    const float2 c6 = make_float2(0.16666667f, 0.16666667f), c2 = make_float2(0.5f, 0.5f);
-    const float2 c1 = make_float2(1.0f, 1.0f), m23 = make_float2(12582912.0f, 12582912.0f);
-    auto one = [&](float d, float xh, float t, float y) {
-      if (xh >= g.xcut) {
-        const int idx = static_cast<int>(g.magic_bits - __float_as_uint(t));
-        atomicAdd(cnt + idx, 1u);
-        atomicAdd(esm + idx, __float_as_uint(y));
-      } else if (d > ninf) {  // finite and below the cells (NaN, -inf: weight 0)
-        ++uc;
-        um += __expf(xh);
-      }
-    };
+    // Two columns at a time in packed fp32x2, without a branch: nx = -x (the
+    // negated product rounds like the product), clamped to -xcut (underflow,
+    // -inf and NaN land in the trash cell ncr + 1), nt = -(nx + magic ...) =
+    // -t, so the cell is the scalar cell_of's; ngg = -(grid point), r = x -
+    // grid point in one rounding, e(r), y = magic23 + round(e 2^S).
+    const f2 nM = f2pk(-g.M, -g.M), nih = f2pk(-g.ih, -g.ih), ih = f2pk(g.ih, g.ih), il = f2pk(g.il, g.il);
+    const f2 nmag = f2pk(-g.magic, -g.magic), mag = f2pk(g.magic, g.magic), tws = f2pk(g.two_s, g.two_s);
+    const f2 c6 = f2pk(0.16666667f, 0.16666667f), c2 = f2pk(0.5f, 0.5f), c1 = f2pk(1.0f, 1.0f);
+    const f2 m23 = f2pk(12582912.0f, 12582912.0f);
+    const float hi = -g.xcut;
+    const unsigned kidx = g.magic_bits + 0x80000000u;  // cell = kidx - bits(-t)
     auto two = [&](float va, float vb) {
-      float da, db;
-      const float xa = xof(va, g, &da), xb = xof(vb, g, &db);
-      const float ta = __fadd_rn(xa, g.magic), tb = __fadd_rn(xb, g.magic);
-      const float2 d2 = make_float2(da, db);
-      const float2 gg = __fadd2_rn(make_float2(ta, tb), nmagic2);       // -idx * 2^-K, exact
-      float2 r = __ffma2_rn(d2, ih2, make_float2(-gg.x, -gg.y));       // x - grid point
-      r = __ffma2_rn(d2, il2, r);
-      const float2 e = __fmul2_rn(r, __ffma2_rn(r, __ffma2_rn(r, c6, c2), c1));
-      const float2 y = __ffma2_rn(e, two_s2, m23);                      // bits: kMagic23 + round(e * 2^S)
-      one(da, xa, ta, y.x);
-      one(db, xb, tb, y.y);
+      const f2 d = add2(f2pk(va, vb), nM);
+      float na, nb;
+      f2up(mul2(d, nih), na, nb);
+      const f2 nt = add2(f2pk(fminf(na, hi), fminf(nb, hi)), nmag);
+      const f2 ngg = add2(nt, mag);
+      f2 r = fma2(d, ih, ngg);
+      r = fma2(d, il, r);
+      const f2 y = fma2(mul2(r, fma2(r, fma2(r, c6, c2), c1)), tws, m23);
+      float ta, tb, ya, yb;
+      f2up(nt, ta, tb);
+      f2up(y, ya, yb);
+      const unsigned ia = kidx - __float_as_uint(ta), ib = kidx - __float_as_uint(tb);
+      atomicAdd(cnt + ia, 1u);
+      atomicAdd(esm + ia, __float_as_uint(ya));
+      atomicAdd(cnt + ib, 1u);
+      atomicAdd(esm + ib, __float_as_uint(yb));
     };
     each_col_pipe<4>(src, n, [&](const float4& v, int) {
       two(v.x, v.y);
       two(v.z, v.w);
-    }, [&](float v, int) {
-      float d;
+    }, [&](float v, int) { two(v, ninf); });  // head and tail: the -inf partner lands in the trash cell
+  }
+  __syncthreads();
+  // underflow columns (rare): their count and approximate mass, in a second
+  // pass over the slice (the trash cell also holds the weight-0 columns and
+  // the head / tail partners, which are told apart here)
+  if (isfinite(g.M) && cnt[nc] != 0u) {
+    each_col<4, true>(src, n, [&](float v, int) {
+      float d, t;
       const float xh = xof(v, g, &d);
-      const float t = __fadd_rn(xh, g.magic);
-      const float gg = __fsub_rn(t, g.magic);
-      float r = __fmaf_rn(d, g.ih, -gg);
-      r = __fmaf_rn(d, g.il, r);
-      const float e = __fmul_rn(r, __fmaf_rn(r, __fmaf_rn(r, 0.16666667f, 0.5f), 1.0f));
-      one(d, xh, t, __fmaf_rn(e, g.two_s, 12582912.0f));
+      if (d > ninf && cell_of(xh, g, &t) > g.ncr) {
+        ++uc;
+        um += __expf(xh);
+      }
     });
   }
   __syncthreads();
@@ -483,7 +523,7 @@ __device__ __noinline__ void merge_b(int row, unsigned char* smem, Shared& sh) {
   const DevOpts& o = sh.o;
   const Grid& g = sh.g;
   const RowArgs& a = p.a;
-  const int slot = row - p.row0;
+  const int slot = row % (2 * kChunkRows);
   const int nc = g.ncr + 1;
   double* cum = reinterpret_cast<double*>(smem);             // [kCells] inclusive cumulative mass
   unsigned* cnt = reinterpret_cast<unsigned*>(cum + kCells);  // [kCells] columns before each cell
@@ -656,7 +696,7 @@ __device__ __noinline__ void run_c(int row, int s, unsigned char* smem, Shared& 
   const DevOpts& o = sh.o;
   const RowArgs& a = p.a;
   RowState* st = p.rs + row;
-  const int ms = row - p.row0;
+  const int ms = row % (2 * kChunkRows);
   const Targets* tg = p.tg + ms;
   const int fail = __ldcg(&tg->fail);
   if (!fail) {
@@ -668,6 +708,7 @@ __device__ __noinline__ void run_c(int row, int s, unsigned char* smem, Shared& 
     const int A0 = __ldcg(&tg->A0), A1 = __ldcg(&tg->A1), B0 = __ldcg(&tg->B0), B1 = __ldcg(&tg->B1);
     const float a_lo = __ldcg(&tg->a_lo), a_hi = __ldcg(&tg->a_hi);
     const float b_lo = __ldcg(&tg->b_lo), b_hi = __ldcg(&tg->b_hi);
+    const bool use_a = A1 >= A0;
     unsigned long long* loc = reinterpret_cast<unsigned long long*>(smem);  // [kMemberCap]
     const int lo = s * p.slice;
     const int n = min(p.slice, a.ncols - lo);
@@ -682,10 +723,23 @@ __device__ __noinline__ void run_c(int row, int s, unsigned char* smem, Shared& 
         }
       }
     };
+    // prefilter per 16-byte vector: the smallest distance of its columns to
+    // each interval's midpoint (packed fp32x2), against the half-width widened
+    // by a relative 1e-6 for the rounding of the distance
+    const float ma = use_a ? 0.5f * (a_lo + a_hi) : __int_as_float(0x7f800000);
+    const float ha = use_a ? 0.5f * (a_hi - a_lo) * (1.0f + 1e-6f) + 1e-30f : -1.0f;
+    const float mb = 0.5f * (b_lo + b_hi), hb = 0.5f * (b_hi - b_lo) * (1.0f + 1e-6f) + 1e-30f;
+    const f2 nma = f2pk(-ma, -ma), nmb = f2pk(-mb, -mb);
     each_col_pipe<4>(src, n, [&](const float4& v, int j) {
-      // one compare pair per vector decides whether any column needs a look
-      const float mn = fminf(fminf(v.x, v.y), fminf(v.z, v.w)), mx = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
-      if ((mx >= a_lo && mn <= a_hi) || (mx >= b_lo && mn <= b_hi)) {
+      const f2 v01 = f2pk(v.x, v.y), v23 = f2pk(v.z, v.w);
+      float a0, a1, a2, a3, b0, b1, b2, b3;
+      f2up(add2(v01, nma), a0, a1);
+      f2up(add2(v23, nma), a2, a3);
+      f2up(add2(v01, nmb), b0, b1);
+      f2up(add2(v23, nmb), b2, b3);
+      const float da = fminf(fminf(fabsf(a0), fabsf(a1)), fminf(fabsf(a2), fabsf(a3)));
+      const float db = fminf(fminf(fabsf(b0), fabsf(b1)), fminf(fabsf(b2), fabsf(b3)));
+      if (da <= ha || db <= hb) {
         test(v.x, j);
         test(v.y, j + 1);
         test(v.z, j + 2);
@@ -727,7 +781,6 @@ __device__ __noinline__ void resolve(const unsigned long long* mkey, const doubl
   auto sub_of = [&](unsigned long long k) -> int {  // -1: not in [c0, c1]
     float d, tt;
     const float xh = xof(dval(k), g, &d);
-    if (!(xh >= g.xcut)) return -1;
     const int c = cell_of(xh, g, &tt);
     if (c < c0 || c > c1) return -1;
     const float uu = __fmul_rn(__fsub_rn(xtop, xh), scale);  // monotone in -x
@@ -850,7 +903,7 @@ __device__ __noinline__ void merge_c(int row, unsigned char* smem, Shared& sh) {
   const NucArgs& p = sh.p;
   const DevOpts& o = sh.o;
   const RowArgs& a = p.a;
-  const int ms = row - p.row0;
+  const int ms = row % (2 * kChunkRows);
   const Targets* tg = p.tg + ms;
   if (threadIdx.x == 0) sh.g = row_grid(p.rs + row, o.temp);
   __syncthreads();
@@ -933,24 +986,22 @@ __device__ __forceinline__ void setup(const NucArgs& p, const DevOpts& o, Shared
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(NT, 6) nuc_a_kernel(const NucArgs p, const DevOpts o) {
-  __shared__ Shared sh;
-  setup(p, o, sh);
-  run_a(p.row0 + static_cast<int>(blockIdx.x) / p.ns, static_cast<int>(blockIdx.x) % p.ns, sh);
-}
-
-__global__ void __launch_bounds__(NT, 4) nuc_b_kernel(const NucArgs p, const DevOpts o) {
+// One launch: CTA i takes phase i mod 3 (C, B, A) and slice i / 3 of that
+// phase's chunk (row = first row + slice index / ns).
+__global__ void __launch_bounds__(NT, 4) nuc_kernel(const NucArgs p, const DevOpts o) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ Shared sh;
+  const int phase = static_cast<int>(blockIdx.x % 3u), j = static_cast<int>(blockIdx.x / 3u);
+  const int n = phase == 0 ? p.nc : (phase == 1 ? p.nb : p.na);
+  if (j >= n * p.ns) return;
   setup(p, o, sh);
-  run_b(p.row0 + static_cast<int>(blockIdx.x) / p.ns, static_cast<int>(blockIdx.x) % p.ns, smem, sh);
-}
-
-__global__ void __launch_bounds__(NT, 4) nuc_c_kernel(const NucArgs p, const DevOpts o) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ Shared sh;
-  setup(p, o, sh);
-  run_c(p.row0 + static_cast<int>(blockIdx.x) / p.ns, static_cast<int>(blockIdx.x) % p.ns, smem, sh);
+  const int s = j % p.ns;
+  if (phase == 0)
+    run_c(p.rowc + j / p.ns, s, smem, sh);
+  else if (phase == 1)
+    run_b(p.rowb + j / p.ns, s, smem, sh);
+  else
+    run_a(p.rowa + j / p.ns, s, sh);
 }
 
 }  // namespace nuc
@@ -975,7 +1026,6 @@ cudaError_t launch_nucleus(const RowArgs& a, const DevOpts& o, void* scratch, cu
   p.a = a;
   p.ns = ns;
   p.slice = (((a.ncols + ns - 1) / ns) + 3) & ~3;
-  p.row0 = 0;
   p.fb_count = reinterpret_cast<unsigned*>(b);
   p.rs = reinterpret_cast<RowState*>(b + l.off_rs);
   p.fb_list = reinterpret_cast<int*>(b + l.off_fb);
@@ -985,18 +1035,21 @@ cudaError_t launch_nucleus(const RowArgs& a, const DevOpts& o, void* scratch, cu
   p.members = reinterpret_cast<unsigned long long*>(b + l.off_mem);
   static bool attrs = false;
   if (!attrs) {
-    e = cudaFuncSetAttribute(nuc_b_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBSmem));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(nuc_c_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kCSmem));
+    e = cudaFuncSetAttribute(nuc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem));
     if (e != cudaSuccess) return e;
     attrs = true;
   }
-  nuc_a_kernel<<<a.rows * ns, NT, 0, s>>>(p, o);
-  for (int r0 = 0; r0 < a.rows; r0 += kChunkRows) {
-    p.row0 = r0;
-    const int n = std::min(kChunkRows, a.rows - r0);
-    nuc_b_kernel<<<n * ns, NT, kBSmem, s>>>(p, o);
-    nuc_c_kernel<<<n * ns, NT, kCSmem, s>>>(p, o);
+  const int chunks = (a.rows + kChunkRows - 1) / kChunkRows;
+  auto rows_of = [&](int c) { return c >= 0 && c < chunks ? std::min(kChunkRows, a.rows - c * kChunkRows) : 0; };
+  for (int t = 0; t < chunks + 2; ++t) {
+    p.rowa = t * kChunkRows;
+    p.rowb = (t - 1) * kChunkRows;
+    p.rowc = (t - 2) * kChunkRows;
+    p.na = rows_of(t);
+    p.nb = rows_of(t - 1);
+    p.nc = rows_of(t - 2);
+    const int most = std::max(p.na, std::max(p.nb, p.nc));
+    nuc_kernel<<<3 * most * ns, NT, kSmem, s>>>(p, o);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
