@@ -98,13 +98,18 @@ def measured_peak():
 
 
 def traffic_per_row(workload: str):
-    """DRAM bytes per row of the dominant kernel from a committed ncu capture
-    (profiles/traffic.json: {workload: {"bytes_per_row": B, ...}}), or None."""
+    """DRAM bytes per row of the step's kernels from a committed ncu capture
+    (profiles/traffic.json: {workload: {"bytes_per_row": B, "rows_captured":
+    R, "source": ...}}): (bytes per row, a label saying where it comes from),
+    or (None, None)."""
     f = ROOT / "profiles" / "traffic.json"
     if not f.is_file():
-        return None
+        return None, None
     d = json.loads(f.read_text()).get(workload)
-    return None if d is None else float(d["bytes_per_row"])
+    if d is None:
+        return None, None
+    return float(d["bytes_per_row"]), (f"scaled by rows from one ncu capture of {d['rows_captured']} rows "
+                                       f"({d['source']})")
 
 
 class Clocks:
@@ -294,7 +299,7 @@ def bench_rows(a, w: wl.Workload, rank: int, world: int, dev):
     del graphs
 
     res = dict(R=R, elapsed_ms=elapsed, launch_ms=launch_ms, copies=copies, batch_bytes=batch_bytes,
-               launches=a.steps * kernels_per_step(w), clocks=clocks.summary() if clocks else None,
+               launches=a.steps * kernels_per_step(w, R), clocks=clocks.summary() if clocks else None,
                graph=not a.no_graph)
     if not a.no_e2e:
         with torch.cuda.stream(stream):  # copies and sampling on one stream
@@ -441,7 +446,7 @@ def bench_sharded(a, w: wl.Workload, rank: int, world: int, dev):
         dist.all_reduce(red, op=dist.ReduceOp.MAX)
     elapsed, launch_ms = red.tolist()
     return dict(R=R, cols=cols, elapsed_ms=elapsed, launch_ms=launch_ms, copies=copies, batch_bytes=batch_bytes,
-                launches=kernels_per_step(w) * a.steps, clocks=clocks.summary() if clocks else None, graph=False)
+                launches=kernels_per_step(w, R) * a.steps, clocks=clocks.summary() if clocks else None, graph=False)
 
 
 # ------------------------------------------------------------ reference arm ----
@@ -844,7 +849,7 @@ def main():
     value = rows_job * a.steps / (res["elapsed_ms"] / 1000.0)
     alg_launch = R * (algorithmic_bytes_per_row(w, cols) + (8 * 64 if sharded else 0))
     achieved = alg_launch / (res["launch_ms"] / 1000.0) / 1e9
-    tr = traffic_per_row(w.name)
+    tr, tr_src = traffic_per_row(w.name)
     line = {
         "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": res["elapsed_ms"] / a.steps, "higher_is_better": True,
@@ -858,6 +863,7 @@ def main():
                      "peak_kind": peak_kind,
                      # per-row traffic was captured on all columns: a rank's shard reads its share
                      "traffic": None if tr is None else tr * R * cols / w.vocab,
+                     "traffic_source": tr_src,
                      "kernel": (("window_kernel + " if uses_window(w) else "") + "split_kernel<emit> + merge")
                      if sharded else kernel_name(w),
                      "alg_bytes_per_launch": alg_launch, "launch_ms": res["launch_ms"]},
@@ -886,11 +892,23 @@ def uses_window(w: wl.Workload) -> bool:
     return w.repeat != 1.0 and w.hist_len > 0 and 0 < w.repeat_last <= 2048
 
 
-def kernels_per_step(w: wl.Workload) -> int:
+NUC_CHUNK_ROWS = 512  # rows per chunk of the streaming full-vocabulary path (nucleus.cu, kChunkRows)
+
+
+def streaming_full_vocab(w: wl.Workload) -> bool:
+    """The options the streaming full-vocabulary kernel takes (nucleus.cu,
+    nucleus_eligible): top_k 0 or >= vocab, no min-p, no penalty."""
+    return (w.temp > 0 and not (0 < w.top_k < w.vocab) and not (w.min_p > 0)
+            and (w.repeat == 1.0 or w.hist_len == 0) and w.vocab >= 4096)
+
+
+def kernels_per_step(w: wl.Workload, rows: int) -> int:
     """Kernels of this library launched by one sampling step."""
     win = 1 if uses_window(w) else 0
     if w.shards > 1:
         return 3 + win   # [window_kernel] + split_kernel<emit> + merge_slices_kernel + merge_kernel
+    if streaming_full_vocab(w):
+        return -(-rows // NUC_CHUNK_ROWS) + 2 + 1   # nuc_kernel per chunk step + general_list_kernel
     return 1 if kernel_name(w) == "general_kernel" else 2 + win
 
 
@@ -900,6 +918,8 @@ def kernel_name(w: wl.Workload) -> str:
         return win + "split_kernel<greedy> + merge_slices_kernel"
     if 0 < w.top_k < w.vocab and w.top_k <= 256:
         return win + "split_kernel<sample> + merge_slices_kernel"
+    if streaming_full_vocab(w):
+        return "nuc_kernel (A, B, C passes; every launch of the step) + general_list_kernel"
     return "general_kernel"
 
 
