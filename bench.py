@@ -364,12 +364,17 @@ def e2e_rows(a, w, R, V, x0, h, off, opts, rng, out, stream, world, dev):
 
 # -------------------------------------------------- vocab-sharded config (c5) ----
 def bench_sharded(a, w: wl.Workload, rank: int, world: int, dev):
-    """Each rank holds V/N contiguous columns of all R rows: shard_topk ->
-    NCCL all-gather of (value, id) candidates -> merge_sample on every rank."""
+    """Each rank holds V/N contiguous columns of all R rows; a step is one
+    verbo_cuda_sharded_sample on the library's communicator: the shard's
+    top-64 (split_kernel<emit> + merge_slices_kernel), ONE NCCL all-gather of
+    the packed (value, id) candidates, merge_kernel on every rank.  Events
+    between the three steps (Comm.mark_next) split every timed step into shard
+    kernel / all-gather / merge; each part is the max over ranks of its mean."""
     import torch
     import torch.distributed as dist
 
     import verbo_b200 as vb
+    from verbo_b200 import sharded
 
     R = a.rows or w.rows
     V = w.vocab
@@ -386,67 +391,116 @@ def bench_sharded(a, w: wl.Workload, rank: int, world: int, dev):
     h, off = wl.make_hist_torch(w, R, dev, seed_offset=0)        # the same histories on every rank
     st = np.array(vb.seed_states(w.sampler_seeds(0, R).tolist()), dtype=np.uint64)
     rng = torch.from_numpy(st.view(np.int64).copy()).to(dev)
-    cv = torch.empty(world, R, k, dtype=torch.float32, device=dev)
-    ci = torch.empty(world, R, k, dtype=torch.int32, device=dev)
-    lv = torch.empty(R, k, dtype=torch.float32, device=dev)
-    li = torch.empty(R, k, dtype=torch.int32, device=dev)
     out = torch.empty(R, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
-    ev = []
+    comm = sharded.make_comm(dev.index)
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(a.steps)]
+    for m in marks:
+        for e in m:
+            e.record(stream)   # creates the events before their handles are passed on
 
-    def step(i, timed=False):
-        if timed:
-            e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            e[0].record(stream)
-        vb.shard_topk(xs[i % copies], rank * cols, V, opts, k, h, off, cand_val=lv, cand_id=li, stream=stream)
-        if timed:
-            e[1].record(stream)
-            ev.append(e)
-        if world > 1:
-            dist.all_gather_into_tensor(cv, lv)
-            dist.all_gather_into_tensor(ci, li)
-        else:
-            cv[0].copy_(lv)
-            ci[0].copy_(li)
-        vb.merge_sample(cv, ci, V, opts, rng=rng, out=out, stream=stream)
+    def step(i, m=None):
+        if m is not None:
+            m[0].record(stream)
+            comm.mark_next(m[1], m[2])
+        comm.sample(xs[i % copies], rank * cols, V, opts, k, rng, h, off, out=out, stream=stream)
+        if m is not None:
+            m[3].record(stream)
 
-    for i in range(a.warmup):
-        step(i)
-    vb.check(stream)
-    clocks = Clocks(torch.cuda.current_device()) if rank == 0 else None
-    if clocks:
-        clocks.start()
-    t_soak = time.perf_counter()
-    i = 0
-    while not a.no_soak:   # the same number of soak steps on every rank (collectives must match)
-        step(i)
-        i += 1
-        done = torch.tensor([1.0 if time.perf_counter() - t_soak >= 1.0 else 0.0], device=dev)
+    try:
+        for i in range(a.warmup):
+            step(i)
+        comm.wait(stream, timeout_ms=60000)
+        vb.check(stream)
+        clocks = Clocks(torch.cuda.current_device()) if rank == 0 else None
+        if clocks:
+            clocks.start()
+        t_soak = time.perf_counter()
+        i = 0
+        while not a.no_soak:   # the same number of soak steps on every rank (collectives must match)
+            step(i)
+            i += 1
+            done = torch.tensor([1.0 if time.perf_counter() - t_soak >= 1.0 else 0.0], device=dev)
+            if world > 1:
+                dist.all_reduce(done, op=dist.ReduceOp.MIN)
+            if done.item() > 0:
+                break
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if world > 1:
-            dist.all_reduce(done, op=dist.ReduceOp.MIN)
-        if done.item() > 0:
-            break
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for i in range(a.steps):
+            step(i, marks[i])
+        t1.record(stream)
+        comm.wait(stream, timeout_ms=60000)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        if clocks:
+            clocks.stop()
+        vb.check(stream)
+        parts = [sum(m[j].elapsed_time(m[j + 1]) for m in marks) / a.steps for j in range(3)]
+        red = torch.tensor([t0.elapsed_time(t1)] + parts, dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(red, op=dist.ReduceOp.MAX)
+        elapsed, shard_ms, gather_ms, merge_ms = red.tolist()
+        e2e = e2e_sharded(a, w, comm, xs[0], h, off, rng, opts, k, rank, cols, world, dev, stream)
+    finally:
+        torch.cuda.synchronize()
+        comm.close()
+    return dict(R=R, cols=cols, elapsed_ms=elapsed, launch_ms=shard_ms, copies=copies, batch_bytes=batch_bytes,
+                launches=kernels_per_step(w, R) * a.steps, clocks=clocks.summary() if clocks else None, graph=False,
+                split={"shard_kernel_ms": shard_ms, "all_gather_ms": gather_ms, "merge_ms": merge_ms,
+                       "step_ms": elapsed / a.steps}, **e2e)
+
+
+def e2e_sharded(a, w, comm, x, h, off, rng, opts, k, rank, cols, world, dev, stream):
+    """The same step through the public API with host buffers: every rank
+    copies its shard and the histories from pinned host memory, calls
+    Comm.sample and reads the ids back, inside the timed region."""
+    import torch
+    import torch.distributed as dist
+
+    steps = a.e2e_steps or min(a.steps, 10)
+    hx = x.cpu().pin_memory()
+    hh = None if h is None else h.cpu().pin_memory()
+    ho = None if off is None else off.cpu().pin_memory()
+    dx = torch.empty_like(x)
+    ids_host = torch.empty(x.shape[0], dtype=torch.int32, pin_memory=True)
+    out = torch.empty(x.shape[0], dtype=torch.int32, device=dev)
+    dh = None if h is None else torch.empty_like(h)
+    do = None if off is None else torch.empty_like(off)
+    h2d = x.numel() * 4 + (0 if h is None else h.numel() * 4 + off.numel() * 8)
+    d2h = x.shape[0] * 4
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        if hh is not None:
+            dh.copy_(hh, non_blocking=True)
+            do.copy_(ho, non_blocking=True)
+        comm.sample(dx, rank * cols, w.vocab, opts, k, rng, dh, do, out=out, stream=stream)
+        ids_host.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    comm.wait(stream, timeout_ms=60000)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    t0.record(stream)
-    for i in range(a.steps):
-        step(i, timed=True)
-    t1.record(stream)
+    e0.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    e1.record(stream)
+    comm.wait(stream, timeout_ms=60000)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    if clocks:
-        clocks.stop()
-    vb.check(stream)
-    red = torch.tensor([t0.elapsed_time(t1), sum(s.elapsed_time(e) for s, e in ev) / a.steps], dtype=torch.float64,
-                       device=dev)
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
-        dist.all_reduce(red, op=dist.ReduceOp.MAX)
-    elapsed, launch_ms = red.tolist()
-    return dict(R=R, cols=cols, elapsed_ms=elapsed, launch_ms=launch_ms, copies=copies, batch_bytes=batch_bytes,
-                launches=kernels_per_step(w, R) * a.steps, clocks=clocks.summary() if clocks else None, graph=False)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    return dict(e2e_ms=float(ms.item()), e2e_steps=steps, h2d=h2d, d2h=d2h)
 
 
 # ------------------------------------------------------------ reference arm ----
@@ -521,6 +575,14 @@ def tail_traffic(tw, R: int):
     return d.get(f"bytes_per_call_r{R}")
 
 
+def head_share(traffic, res, tw):
+    """Traffic of a whole-head capture scaled to a rank's vocab rows of the
+    head (the head dominates the bytes), for the sharded-head step."""
+    if traffic is None or "shard_rows" not in res:
+        return traffic
+    return traffic * res["shard_rows"] / tw.vocab
+
+
 def cpu_tail_rate(tw, q, s, norm, x, seconds: float, threads: int):
     """The reference's AVX2 tail on `x`, repeated within the time budget."""
     from oracle import pyoracle as po
@@ -546,10 +608,11 @@ def cpu_tail_rate(tw, q, s, norm, x, seconds: float, threads: int):
 
 def bench_tail_sharded(a, tw, rank: int, world: int, dev):
     """Tensor-parallel head: rank r holds vocab rows shard_bounds(V, N, r) of
-    the head and the same hidden rows; a step is the shard's tail, its top-8
-    candidates, the NCCL all-gather and the merge (greedy), identical ids on
-    every rank.  Host launches per step (the collective stays outside graphs);
-    the CUDA-event window of each step covers the tail shard."""
+    the head and the same hidden rows; a step is the shard's tail, then
+    verbo_cuda_sharded_sample on the library's communicator (its top-8
+    candidates, one NCCL all-gather, the greedy merge), identical ids on every
+    rank.  Host launches per step (the collective stays outside graphs); the
+    CUDA-event window of each step covers the tail shard."""
     import torch
     import torch.distributed as dist
 
@@ -564,12 +627,9 @@ def bench_tail_sharded(a, tw, rank: int, world: int, dev):
     shard = torch.empty(R, hi - lo, dtype=torch.float32, device=dev)
     k = 8
     opts = vb.Sampling(temp=0.0)
-    lv = torch.empty(R, k, dtype=torch.float32, device=dev)
-    li = torch.empty(R, k, dtype=torch.int32, device=dev)
-    cv = torch.empty(world, R, k, dtype=torch.float32, device=dev)
-    ci = torch.empty(world, R, k, dtype=torch.int32, device=dev)
     out = torch.empty(R, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
+    comm = sharded.make_comm(dev.index)
     ev = []
 
     def step(timed=False):
@@ -580,35 +640,34 @@ def bench_tail_sharded(a, tw, rank: int, world: int, dev):
         if timed:
             e[1].record(stream)
             ev.append(e)
-        vb.shard_topk(shard, lo, tw.vocab, opts, k, cand_val=lv, cand_id=li, stream=stream)
-        if world > 1:
-            dist.all_gather_into_tensor(cv, lv)
-            dist.all_gather_into_tensor(ci, li)
-        else:
-            cv[0].copy_(lv)
-            ci[0].copy_(li)
-        vb.merge_sample(cv, ci, tw.vocab, opts, out=out, stream=stream)
+        comm.sample(shard, lo, tw.vocab, opts, k, out=out, stream=stream)
 
-    for _ in range(a.warmup):
-        step()
-    vb.check(stream)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(a.steps):
-        step(timed=True)
-    t1.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    vb.check(stream)
-    red = torch.tensor([t0.elapsed_time(t1), sum(s_.elapsed_time(e_) for s_, e_ in ev) / a.steps],
-                       dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(red, op=dist.ReduceOp.MAX)
-    t.close()
+    try:
+        for _ in range(a.warmup):
+            step()
+        comm.wait(stream, timeout_ms=60000)
+        vb.check(stream)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(a.steps):
+            step(timed=True)
+        t1.record(stream)
+        comm.wait(stream, timeout_ms=60000)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        vb.check(stream)
+        red = torch.tensor([t0.elapsed_time(t1), sum(s_.elapsed_time(e_) for s_, e_ in ev) / a.steps],
+                           dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(red, op=dist.ReduceOp.MAX)
+    finally:
+        torch.cuda.synchronize()
+        comm.close()
+        t.close()
     return dict(R=R, elapsed_ms=red[0].item(), launch_ms=red[1].item(), shard_rows=hi - lo, clocks=None,
                 graph=False), None
 
@@ -776,14 +835,14 @@ def main_tail(a, rank: int, local_rank: int, world: int):
     cfg = tail_config(tw, R, 1 if sharded_head else world)
     if sharded_head:
         cfg.update(parallelism=f"head vocab shards x{world}", head_rows_per_gpu=res["shard_rows"],
-                   step="tail shard -> shard_topk (k 8) -> NCCL all-gather -> merge_sample (greedy)")
+                   step="tail shard -> verbo_cuda_sharded_sample (k 8, one NCCL all-gather, greedy merge)")
     line = {
         "metric": TAIL_METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": res["elapsed_ms"] / a.steps, "higher_is_better": True,
         "scaling": "strong" if sharded_head else "weak", "vs_baseline": None,
         "dtype": "f32" if tw.dtype == "f32" else "i8/f32", "data": "synthetic", "config": cfg,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "traffic": tail_traffic(tw, R),
+                     "peak_kind": peak_kind, "traffic": head_share(tail_traffic(tw, R), res, tw),
                      "kernel": "tail_norm_kernel + " + head_kernel, "alg_bytes_per_launch": alg,
                      "launch_ms": res["launch_ms"]},
         "clocks": res["clocks"],
@@ -871,7 +930,11 @@ def main():
         "timing": "CUDA graph replay per step" if res.get("graph") else "host launch per step",
         "gpu_launches": res["launches"] * world,
     }
-    if not sharded and "e2e_ms" in res:
+    if "split" in res:
+        line["step_split"] = res["split"]
+        line["config"]["step"] = ("verbo_cuda_sharded_sample: shard top-64 -> one NCCL all-gather of packed "
+                                  "(value, id) candidates -> merge")
+    if "e2e_ms" in res:
         line["e2e"] = {"value": rows_job * res["e2e_steps"] / (res["e2e_ms"] / 1000.0), "unit": "rows/s",
                        "h2d_bytes_per_step": res["h2d"] * world, "d2h_bytes_per_step": res["d2h"] * world}
     else:

@@ -139,6 +139,45 @@ VERBO_CUDA_API int verbo_cuda_merge_sample(const float* cand_val, const int* can
                                            unsigned long long* rng, int* out_ids, verbo_row_stats* stats,
                                            void* stream);
 
+/* ---- vocab-sharded sampling over GPUs, with the library's own collective ----
+   No counterpart in the reference (its sampler runs on one host).  A row whose
+   columns are split over the ranks of a job, one GPU each (the logits of a
+   vocab-parallel LM head), is sampled as verbo_cuda_shard_topk, ONE all-gather
+   of every rank's packed (value, id) candidates over NVLink, and
+   verbo_cuda_merge_sample, all on the caller's stream; every rank gets the
+   same ids.  The communicator is NCCL, loaded at run time (libnccl.so.2).
+   Set-up: rank 0 makes an id with verbo_cuda_comm_unique_id, the caller hands
+   the 128 bytes to every rank (MPI, a store, a file), and every rank calls
+   verbo_cuda_comm_new with it (collective: all ranks must call it). */
+#define VERBO_CUDA_UNIQUE_ID_BYTES 128
+typedef struct verbo_cuda_comm verbo_cuda_comm;
+VERBO_CUDA_API int verbo_cuda_comm_unique_id(unsigned char id[VERBO_CUDA_UNIQUE_ID_BYTES]);
+VERBO_CUDA_API verbo_cuda_comm* verbo_cuda_comm_new(const unsigned char id[VERBO_CUDA_UNIQUE_ID_BYTES], int nranks,
+                                                    int rank, int device);
+VERBO_CUDA_API void verbo_cuda_comm_free(verbo_cuda_comm* c);
+/* One vocab-sharded pick: this rank holds global columns [col_offset,
+   col_offset + shard_cols) of each row (device memory, like
+   verbo_cuda_shard_topk); the penalty applies to the history ids in the shard.
+   k <= 256 candidates per rank, nranks * k <= 4096; needs temp <= 0 or
+   0 < top_k <= k (then the global top-k lies in the union of the shards').
+   rng (2 per row, the same on every rank) is advanced as in verbo_cuda_sample. */
+VERBO_CUDA_API int verbo_cuda_sharded_sample(verbo_cuda_comm* c, const float* logits, int rows, int shard_cols,
+                                             long long ld, int col_offset, int vocab, const int* hist,
+                                             const long long* hist_off, const verbo_sampling* opts, int k,
+                                             unsigned long long* rng, int* out_ids, verbo_row_stats* stats,
+                                             void* stream);
+/* Bounded wait for the work queued on `stream`: returns 0 once it completed;
+   if it has not within timeout_ms, or the communicator reports an error, the
+   communicator is aborted and -1 is returned (a rank that died turns into an
+   error on the others, not a hang). */
+VERBO_CUDA_API int verbo_cuda_comm_wait(verbo_cuda_comm* c, void* stream, int timeout_ms);
+/* Timing of the three steps: the next verbo_cuda_sharded_sample on `c` records
+   `after_shard` (a cudaEvent_t, or NULL) on its stream once the shard's top-k
+   kernel is queued, and `after_gather` once the all-gather is; the caller's
+   own events before and after the call close the shard-kernel and merge
+   intervals.  Applies to that one call, then both are cleared. */
+VERBO_CUDA_API int verbo_cuda_comm_mark_next(verbo_cuda_comm* c, void* after_shard, void* after_gather);
+
 /* Synchronises `stream` and reports device-side failures recorded since the
    last check (then clears them): 0 if none, -1 with a message otherwise. */
 VERBO_CUDA_API int verbo_cuda_check(void* stream);

@@ -29,7 +29,7 @@ from pathlib import Path
 from typing import Optional, Sequence
 
 __all__ = ["Sampling", "Sampler", "VerboCudaError", "load_library", "sample", "sample_noalloc", "full_vocab_fallbacks", "shard_topk", "merge_sample",
-           "seed_states", "check", "version", "ROW_STATS_FIELDS", "Batch", "Tail"]
+           "seed_states", "check", "version", "ROW_STATS_FIELDS", "Batch", "Tail", "Comm"]
 __version__ = "0.1.0"
 
 _HERE = Path(__file__).resolve().parent
@@ -120,6 +120,14 @@ def load_library():
                                                    ctypes.POINTER(_Sampling), _P, _P, _P, _P]),
         "verbo_cuda_check": (ctypes.c_int, [_P]),
         "verbo_cuda_full_vocab_fallbacks": (ctypes.c_int, [_P]),
+        "verbo_cuda_comm_unique_id": (ctypes.c_int, [_P]),
+        "verbo_cuda_comm_new": (_P, [_P, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+        "verbo_cuda_comm_free": (None, [_P]),
+        "verbo_cuda_comm_wait": (ctypes.c_int, [_P, _P, ctypes.c_int]),
+        "verbo_cuda_comm_mark_next": (ctypes.c_int, [_P, _P, _P]),
+        "verbo_cuda_sharded_sample": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong,
+                                                     ctypes.c_int, ctypes.c_int, _P, _P, ctypes.POINTER(_Sampling),
+                                                     ctypes.c_int, _P, _P, _P, _P]),
         "verbo_cuda_sampler_new": (_P, [ctypes.POINTER(_Sampling), ctypes.c_int]),
         "verbo_cuda_sampler_free": (None, [_P]),
         "verbo_cuda_sampler_pick": (ctypes.c_int, [_P, _P, ctypes.c_int]),
@@ -383,6 +391,78 @@ class Batch:
                                             logits.stride(0), _dptr(out), _dptr(stats), _stream(cuda_stream)))
         return out
 
+
+
+UNIQUE_ID_BYTES = 128
+
+
+class Comm:
+    """The library's communicator for vocab-sharded sampling (one per rank and
+    GPU): NCCL, loaded by the library at run time.  Rank 0 makes an id with
+    ``Comm.unique_id()``; every rank passes the same 128 bytes to the
+    constructor (a collective call).  ``sample`` is verbo_cuda_sharded_sample:
+    this rank's column shard -> its k best -> one all-gather -> the merge, on
+    the given stream, with the same ids on every rank."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (ctypes.c_ubyte * UNIQUE_ID_BYTES)()
+        _ok(load_library().verbo_cuda_comm_unique_id(ctypes.addressof(buf)))
+        return bytes(buf)
+
+    def __init__(self, uid: bytes, nranks: int, rank: int, device: int = 0):
+        if len(uid) != UNIQUE_ID_BYTES:
+            raise VerboCudaError(f"the unique id has {UNIQUE_ID_BYTES} bytes")
+        self._lib = load_library()
+        buf = (ctypes.c_ubyte * UNIQUE_ID_BYTES).from_buffer_copy(uid)
+        h = self._lib.verbo_cuda_comm_new(ctypes.addressof(buf), int(nranks), int(rank), int(device))
+        if not h:
+            raise _err()
+        self._h, self.nranks, self.rank, self.device = h, int(nranks), int(rank), int(device)
+
+    def sample(self, shard, col_offset: int, vocab: int, opts: Sampling, k: int, rng=None, hist=None, hist_off=None,
+               out=None, stats=None, stream=None):
+        import torch
+
+        rows, cols = shard.shape
+        if shard.dtype != torch.float32:
+            raise VerboCudaError("logits must be float32")
+        if out is None:
+            out = torch.empty(rows, dtype=torch.int32, device=shard.device)
+        o = opts._c()
+        _ok(self._lib.verbo_cuda_sharded_sample(self._h, _dptr(shard, True), rows, cols, shard.stride(0),
+                                                int(col_offset), int(vocab), _dptr(hist), _dptr(hist_off),
+                                                ctypes.byref(o), int(k), _dptr(rng), _dptr(out), _dptr(stats),
+                                                _stream(stream)))
+        return out
+
+    def wait(self, stream=None, timeout_ms: int = 10000) -> None:
+        """Bounded wait for the stream; on timeout or a collective error the
+        communicator is aborted and VerboCudaError raised."""
+        _ok(self._lib.verbo_cuda_comm_wait(self._h, _stream(stream), int(timeout_ms)))
+
+    def mark_next(self, after_shard=None, after_gather=None) -> None:
+        """The next ``sample`` records these torch.cuda.Events (timing-enabled,
+        recorded at least once so that they exist) on its stream after the
+        shard's top-k kernel and after the all-gather."""
+        def handle(e):
+            if e is None:
+                return None
+            if not e.cuda_event:
+                raise VerboCudaError("record the event once before passing it")
+            return ctypes.c_void_p(e.cuda_event)
+        _ok(self._lib.verbo_cuda_comm_mark_next(self._h, handle(after_shard), handle(after_gather)))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.verbo_cuda_comm_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 TAIL_DTYPES = {"f32": 0, "q8": 1, "q4": 2}  # verbo::DType (include/verbo/verbo.hpp:13)

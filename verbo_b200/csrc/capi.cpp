@@ -5,6 +5,8 @@
 // validates arguments, plans the cluster split and launches the kernels of
 // kernels.cu.  There is no CPU fallback.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>  // types only: NCCL is loaded at run time (dlopen), see Nccl below
 
 #include <algorithm>
 #include <chrono>
@@ -14,6 +16,7 @@
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <utility>
 #include <vector>
 
@@ -881,6 +884,222 @@ VERBO_CUDA_API int verbo_cuda_tail_logits(verbo_cuda_tail* t, const float* x, in
         }
         vb::tail_scratch_attach(t->h, n, sc.data, a);
         cuda_ok(vb::launch_tail(t->h, a, s), "kernel launch");
+        return 0;
+      },
+      -1);
+}
+
+}  // extern "C"
+
+// ================================================ vocab-sharded collective ==
+// The library's own communicator for the vocab-sharded pick: NCCL, loaded at
+// run time (libnccl.so.2, whichever the process resolves, so a process that
+// already has NCCL loaded shares that copy), so that the library has no link
+// dependency on it and callers without NCCL can use everything else.
+namespace {
+
+struct Nccl {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*get_error_string)(ncclResult_t) = nullptr;
+  std::string err;
+};
+
+const Nccl& nccl() {
+  static Nccl n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
+    if (!h) {
+      const char* e = dlerror();
+      n.err = e ? e : "libnccl.so.2 not found";
+      return;
+    }
+    auto sym = [&](const char* name) {
+      void* p = dlsym(h, name);
+      if (!p && n.err.empty()) n.err = std::string("missing ") + name;
+      return p;
+    };
+    n.get_unique_id = reinterpret_cast<decltype(n.get_unique_id)>(sym("ncclGetUniqueId"));
+    n.comm_init_rank = reinterpret_cast<decltype(n.comm_init_rank)>(sym("ncclCommInitRank"));
+    n.comm_destroy = reinterpret_cast<decltype(n.comm_destroy)>(sym("ncclCommDestroy"));
+    n.comm_abort = reinterpret_cast<decltype(n.comm_abort)>(sym("ncclCommAbort"));
+    n.comm_get_async_error = reinterpret_cast<decltype(n.comm_get_async_error)>(sym("ncclCommGetAsyncError"));
+    n.all_gather = reinterpret_cast<decltype(n.all_gather)>(sym("ncclAllGather"));
+    n.get_error_string = reinterpret_cast<decltype(n.get_error_string)>(sym("ncclGetErrorString"));
+  });
+  if (!n.err.empty()) fail("NCCL is not available: " + n.err);
+  return n;
+}
+
+void nccl_ok(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess) fail(std::string(what) + ": " + nccl().get_error_string(r));
+}
+
+}  // namespace
+
+struct verbo_cuda_comm {
+  ncclComm_t comm = nullptr;
+  int nranks = 0, rank = 0, device = 0;
+  uint2* local = nullptr;     // this rank's candidates [rows][k], packed
+  uint2* gathered = nullptr;  // every rank's [nranks][rows][k]
+  size_t cap = 0;             // rows * k the buffers hold
+  cudaEvent_t mark_shard = nullptr, mark_gather = nullptr;  // recorded by the next call only
+  std::mutex mu;
+};
+
+extern "C" {
+
+VERBO_CUDA_API int verbo_cuda_comm_unique_id(unsigned char id[VERBO_CUDA_UNIQUE_ID_BYTES]) {
+  return guard(
+      [&]() {
+        static_assert(sizeof(ncclUniqueId) == VERBO_CUDA_UNIQUE_ID_BYTES, "NCCL unique id size");
+        if (!id) fail("id is NULL");
+        ncclUniqueId u;
+        nccl_ok(nccl().get_unique_id(&u), "ncclGetUniqueId");
+        std::memcpy(id, &u, sizeof(u));
+        return 0;
+      },
+      -1);
+}
+
+VERBO_CUDA_API verbo_cuda_comm* verbo_cuda_comm_new(const unsigned char id[VERBO_CUDA_UNIQUE_ID_BYTES], int nranks,
+                                                    int rank, int device) {
+  return guard(
+      [&]() -> verbo_cuda_comm* {
+        if (!id) fail("id is NULL");
+        if (nranks < 1 || rank < 0 || rank >= nranks) fail("rank must be in [0, nranks)");
+        cuda_ok(cudaSetDevice(device), "cudaSetDevice");
+        ncclUniqueId u;
+        std::memcpy(&u, id, sizeof(u));
+        auto* c = new verbo_cuda_comm;
+        c->nranks = nranks;
+        c->rank = rank;
+        c->device = device;
+        const ncclResult_t r = nccl().comm_init_rank(&c->comm, nranks, u, rank);
+        if (r != ncclSuccess) {
+          delete c;
+          nccl_ok(r, "ncclCommInitRank");
+        }
+        return c;
+      },
+      static_cast<verbo_cuda_comm*>(nullptr));
+}
+
+VERBO_CUDA_API void verbo_cuda_comm_free(verbo_cuda_comm* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  cudaDeviceSynchronize();
+  if (c->comm) nccl().comm_destroy(c->comm);
+  cudaFree(c->local);
+  cudaFree(c->gathered);
+  delete c;
+}
+
+VERBO_CUDA_API int verbo_cuda_comm_wait(verbo_cuda_comm* c, void* stream, int timeout_ms) {
+  return guard(
+      [&]() {
+        if (!c || !c->comm) fail("communicator is NULL or aborted");
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        const auto t0 = std::chrono::steady_clock::now();
+        while (true) {
+          const cudaError_t q = cudaStreamQuery(s);
+          if (q == cudaSuccess) break;
+          if (q != cudaErrorNotReady) cuda_ok(q, "stream");
+          ncclResult_t ae = ncclSuccess;
+          nccl_ok(nccl().comm_get_async_error(c->comm, &ae), "ncclCommGetAsyncError");
+          const bool late = std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms);
+          if ((ae != ncclSuccess && ae != ncclInProgress) || late) {
+            nccl().comm_abort(c->comm);
+            c->comm = nullptr;
+            fail(late ? "the collective did not complete within the time limit; the communicator was aborted"
+                      : std::string("the collective failed (") + nccl().get_error_string(ae) +
+                            "); the communicator was aborted");
+          }
+          std::this_thread::sleep_for(std::chrono::microseconds(50));
+        }
+        return 0;
+      },
+      -1);
+}
+
+VERBO_CUDA_API int verbo_cuda_sharded_sample(verbo_cuda_comm* c, const float* logits, int rows, int shard_cols,
+                                             long long ld, int col_offset, int vocab, const int* hist,
+                                             const long long* hist_off, const verbo_sampling* opts, int k,
+                                             unsigned long long* rng, int* out_ids, verbo_row_stats* stats,
+                                             void* stream) {
+  return guard(
+      [&]() {
+        if (!c || !c->comm) fail("communicator is NULL or aborted");
+        if (!opts) fail("opts is NULL");
+        if (rows < 0) fail("rows must be >= 0");
+        if (rows == 0) return 0;
+        if (!logits || !out_ids) fail("logits and out_ids must not be NULL");
+        if (k < 1 || k > vb::kSplitMaxK) fail("k must be in [1, " + std::to_string(vb::kSplitMaxK) + "]");
+        if (static_cast<long long>(c->nranks) * k > vb::kMaxMerge)
+          fail("nranks * k must be <= " + std::to_string(vb::kMaxMerge));
+        if (vocab < 1 || vocab > vb::kMaxVocab) fail("vocab must be in [1, " + std::to_string(vb::kMaxVocab) + "]");
+        if (shard_cols < 1 || col_offset < 0 || static_cast<long long>(col_offset) + shard_cols > vocab)
+          fail("shard [col_offset, col_offset + shard_cols) must lie in [0, vocab)");
+        if (ld < shard_cols) fail("ld must be >= shard_cols");
+        check_hist(hist, hist_off);
+        vb::DevOpts o = make_opts(*opts, vocab, hist != nullptr);
+        if (!o.greedy && !(opts->top_k > 0 && opts->top_k <= k && opts->top_k < vocab))
+          fail("vocab-sharded sampling needs temp <= 0 or 0 < top_k <= k");
+        if (!o.greedy && !rng) fail("rng state is required when temp > 0");
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        std::lock_guard<std::mutex> lk(c->mu);
+        const size_t need = static_cast<size_t>(rows) * k;
+        if (c->cap < need) {
+          cuda_ok(cudaStreamSynchronize(s), "stream");  // the old buffers may still be in use
+          cudaFree(c->local);
+          cudaFree(c->gathered);
+          c->local = c->gathered = nullptr;
+          c->cap = 0;
+          cuda_ok(cudaMalloc(&c->local, need * sizeof(uint2)), "cudaMalloc candidates");
+          cuda_ok(cudaMalloc(&c->gathered, need * c->nranks * sizeof(uint2)), "cudaMalloc candidates");
+          c->cap = need;
+        }
+        // step 1: this shard's k best (value, global id), packed
+        vb::RowArgs a = row_args(logits, rows, shard_cols, ld, col_offset, vocab, hist, hist_off);
+        a.cand_packed = c->local;
+        a.cand_k = k;
+        plan_split(a);
+        attach_split_scratch(a, o, false, s);
+        cuda_ok(vb::launch_split(a, o, vb::kSplitEmit, s), "kernel launch");
+        const cudaEvent_t ms = c->mark_shard, mg = c->mark_gather;
+        c->mark_shard = c->mark_gather = nullptr;
+        if (ms) cuda_ok(cudaEventRecord(ms, s), "cudaEventRecord");
+        // step 2: one all-gather of every rank's packed candidates
+        nccl_ok(nccl().all_gather(c->local, c->gathered, need, ncclUint64, c->comm, s), "ncclAllGather");
+        if (mg) cuda_ok(cudaEventRecord(mg, s), "cudaEventRecord");
+        // step 3: the merge and the pick, identical on every rank
+        vb::MergeArgs m{};
+        m.cand_packed = c->gathered;
+        m.rows = rows;
+        m.nshards = c->nranks;
+        m.k = k;
+        m.rng = rng;
+        m.out_ids = out_ids;
+        m.stats = stats;
+        cuda_ok(vb::launch_merge(m, o, s), "kernel launch");
+        return 0;
+      },
+      -1);
+}
+
+VERBO_CUDA_API int verbo_cuda_comm_mark_next(verbo_cuda_comm* c, void* after_shard, void* after_gather) {
+  return guard(
+      [&]() {
+        if (!c) fail("communicator is NULL");
+        std::lock_guard<std::mutex> lk(c->mu);
+        c->mark_shard = static_cast<cudaEvent_t>(after_shard);
+        c->mark_gather = static_cast<cudaEvent_t>(after_gather);
         return 0;
       },
       -1);

@@ -219,9 +219,18 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeArgs a,
     if (i < total) {
       const int s = i / a.k, j = i - s * a.k;
       const long long at = (static_cast<long long>(s) * a.rows + row) * a.k + j;
-      const int id = a.cand_id[at];
+      int id;
+      float val;
+      if (a.cand_packed) {
+        const uint2 c = a.cand_packed[at];
+        id = static_cast<int>(c.y);
+        val = __uint_as_float(c.x);
+      } else {
+        id = a.cand_id[at];
+        val = id >= 0 ? a.cand_val[at] : 0.0f;
+      }
       if (id >= 0) {
-        d = dkey(a.cand_val[at], static_cast<uint32_t>(id));
+        d = dkey(val, static_cast<uint32_t>(id));
         ++valid;
       }
     }
@@ -2126,8 +2135,14 @@ __global__ void __launch_bounds__(NT, 6) merge_slices_kernel(const RowArgs a, co
     for (int i = threadIdx.x; i < a.cand_k; i += NT) {
       const long long at = static_cast<long long>(row) * a.cand_k + i;
       const bool ok = i < static_cast<int>(k);
-      a.cand_val[at] = ok ? dval(cand[i]) : -__int_as_float(0x7f800000);
-      a.cand_id[at] = ok ? static_cast<int>(did(cand[i])) : -1;
+      const float val = ok ? dval(cand[i]) : -__int_as_float(0x7f800000);
+      const int id = ok ? static_cast<int>(did(cand[i])) : -1;
+      if (a.cand_packed) {
+        a.cand_packed[at] = make_uint2(__float_as_uint(val), static_cast<unsigned>(id));
+      } else {
+        a.cand_val[at] = val;
+        a.cand_id[at] = id;
+      }
     }
   } else {
     // H's first 4 KB and sel (the k best are in cand now) are free: fp64

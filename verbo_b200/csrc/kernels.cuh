@@ -40,6 +40,7 @@ struct RowArgs {
   verbo_row_stats* stats;
   float* cand_val;  // shard candidates out, [rows][cand_k]
   int* cand_id;
+  uint2* cand_packed;  // or packed (x = value bits, y = id), [rows][cand_k] (used when non-null)
   int cand_k;
   int cluster;  // CTAs per row (a thread-block cluster, or independent slices in the split kernels)
   int slice;    // columns per CTA (multiple of 4)
@@ -106,6 +107,7 @@ cudaError_t launch_split_noalloc(RowArgs& a, const DevOpts& o, int mode, cudaStr
 struct MergeArgs {
   const float* cand_val;  // [nshards][rows][k]
   const int* cand_id;
+  const uint2* cand_packed;  // or packed (x = value bits, y = id), [nshards][rows][k] (used when non-null)
   int rows, nshards, k;
   unsigned long long* rng;
   int* out_ids;

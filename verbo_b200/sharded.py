@@ -4,12 +4,16 @@ Row sharding needs no collective: rows are independent, so each rank samples
 ``row_bounds(rows, world, rank)`` of the batch.
 
 Vocab sharding (a row split over ranks by columns, as a tensor-parallel LM head
-leaves it): every rank runs ``verbo_cuda_shard_topk`` on its contiguous column
-shard ``shard_bounds(vocab, world, rank)``, the per-rank candidate buffers
-``[rows][k]`` are all-gathered into ``[world][rows][k]``, and every rank runs
-``verbo_cuda_merge_sample`` with the same per-row RNG state, so all ranks draw
-the same ids.  The global top_k set lies in the union of the shards' top-k
-sets when top_k <= k, so the result equals the unsharded pick.
+leaves it): every rank holds a contiguous column shard
+``shard_bounds(vocab, world, rank)`` and calls the library's
+``verbo_cuda_sharded_sample`` through a ``verbo_b200.Comm``: the shard's top-k
+(value, global id) candidates, one NCCL all-gather of the packed candidates
+of every rank over NVLink, and the merge with the same per-row RNG state on
+every rank, so all ranks draw the same ids, all on the caller's stream.  The
+global top_k set lies in the union of the shards' top-k sets when
+top_k <= k, so the result equals the unsharded pick.  ``make_comm`` builds the
+communicator: rank 0's NCCL id reaches the other ranks through
+torch.distributed (any backend), the only thing torch is used for here.
 
 Tensor-parallel logits tail: with the LM head split by vocab rows (rank r
 holds rows ``shard_bounds(vocab, world, r)``, e.g. ``verbo_b200.Tail`` built
@@ -18,9 +22,10 @@ logits of its own shard only and feeds them to the same sharded pick
 (``sample_tail_sharded``): no rank ever holds a full logits row, and each reads
 1/world of the head.
 
-The collective is the only cross-rank step; ``gather_candidates`` uses the
-process group's timeout, so a rank that died turns into an error on the
-others instead of a hang.
+``gather_candidates`` is the same exchange through torch.distributed (the
+layout ``verbo_cuda_merge_sample`` expects), for hosts without the library's
+communicator (CPU tests with gloo).  ``Comm.wait`` bounds the wait for a
+collective: a rank that died turns into an error on the others, not a hang.
 """
 from __future__ import annotations
 
@@ -57,24 +62,42 @@ def gather_candidates(cand_val, cand_id, group=None):
     return out_v, out_i
 
 
-def sample_vocab_sharded(shard, col_offset: int, vocab: int, opts, k: int, rng, hist=None, hist_off=None,
-                         out=None, group=None, stream=None):
-    """One vocab-sharded pick over this rank's column shard (CUDA tensors).
-    Returns the ids, identical on every rank."""
+def broadcast_unique_id(make_id, group=None) -> bytes:
+    """The id rank 0 of `group` makes with `make_id()`, on every rank."""
+    import torch.distributed as dist
+
+    obj = [make_id() if dist.get_rank(group) == 0 else None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    return obj[0]
+
+
+def make_comm(device: int, group=None):
+    """The library's communicator over the ranks of `group` (collective: every
+    rank calls it); a single process (no process group) gets a one-rank one."""
+    import torch.distributed as dist
+
     import verbo_b200 as vb
 
-    cv, ci = vb.shard_topk(shard, col_offset, vocab, opts, k, hist, hist_off, stream=stream)
-    gv, gi = gather_candidates(cv, ci, group)
-    return vb.merge_sample(gv, gi, vocab, opts, rng=rng, out=out, stream=stream)
+    if not dist.is_available() or not dist.is_initialized():
+        return vb.Comm(vb.Comm.unique_id(), 1, 0, device)
+    uid = broadcast_unique_id(vb.Comm.unique_id, group)
+    return vb.Comm(uid, dist.get_world_size(group), dist.get_rank(group), device)
 
 
-def sample_tail_sharded(tail, x, col_offset: int, vocab: int, opts, k: int, rng, hist=None, hist_off=None,
-                        out=None, logits=None, group=None, stream=None):
+def sample_vocab_sharded(comm, shard, col_offset: int, vocab: int, opts, k: int, rng, hist=None, hist_off=None,
+                         out=None, stats=None, stream=None):
+    """One vocab-sharded pick over this rank's column shard (CUDA tensors):
+    verbo_cuda_sharded_sample on `comm`.  Returns the ids, identical on every
+    rank."""
+    return comm.sample(shard, col_offset, vocab, opts, k, rng, hist, hist_off, out=out, stats=stats, stream=stream)
+
+
+def sample_tail_sharded(comm, tail, x, col_offset: int, vocab: int, opts, k: int, rng, hist=None, hist_off=None,
+                        out=None, logits=None, stream=None):
     """Tensor-parallel logits tail + pick: `tail` holds the head rows
     [col_offset, col_offset + tail.vocab) of a vocab sharding of the LM head,
     `x` the hidden rows (the same on every rank).  This rank's shard of the
     logits (into `logits` if given) feeds the vocab-sharded pick; returns the
     ids, identical on every rank."""
     shard = tail.logits(x, out=logits, stream=stream)
-    return sample_vocab_sharded(shard, col_offset, vocab, opts, k, rng, hist, hist_off, out=out, group=group,
-                                stream=stream)
+    return sample_vocab_sharded(comm, shard, col_offset, vocab, opts, k, rng, hist, hist_off, out=out, stream=stream)
