@@ -262,6 +262,22 @@ VERBO_CUDA_API void verbo_cuda_tail_free(verbo_cuda_tail* t);
 VERBO_CUDA_API int verbo_cuda_tail_logits(verbo_cuda_tail* t, const float* x, int n, long long ldx, float* logits,
                                           long long ld, void* stream);
 
+/* ---- one decode step of B concurrent generations --------------------------
+   The end of Session::Impl::batch (src/session.cpp:163-169) for the last row
+   of each of B sessions, followed by the pick + accept of verbo::generate
+   (src/sampler.cpp:156-165) for each: `hidden` holds B rows of final hidden
+   state (row i, the residual of generation i's last position before the
+   final norm, at hidden + i*ldx, dim floats; host or device memory) ->
+   verbo_cuda_tail_logits into device rows the batch owns ->
+   verbo_cuda_batch_step on them.  The logits never leave the device.
+   out_ids (B ints) and stats (B rows, optional) may be host or device
+   memory; with either on the host the call returns once they are written,
+   otherwise it is ordered on `cuda_stream`.  `t` and `b` must live on the
+   same device; B is the batch's stream count.  The reference runs one
+   Session and one Sampler per generation on the host, with no batched form. */
+VERBO_CUDA_API int verbo_cuda_batch_decode(verbo_cuda_batch* b, verbo_cuda_tail* t, const float* hidden,
+                                           long long ldx, int* out_ids, verbo_row_stats* stats, void* cuda_stream);
+
 #ifdef __cplusplus
 }
 #endif

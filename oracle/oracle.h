@@ -119,6 +119,18 @@ int ref_logits_tail(int dtype, int vocab, int dim, const void* q, const uint16_t
 int ref_model_tail(const char* dir, int dtype, const int* toks, int n, int threads, int* meta, float* eps_out,
                    float* x_out, float* logits_out, void* q_out, uint16_t* s_out, float* norm_out);
 
+/* The reference's decode loop on a checkpoint (oracle/_ref tail harnesses):
+   verbo::generate (src/sampler.cpp:111-181) of prompt[0..n) with `opts`
+   (seed must be non-zero), max_tokens, no stop text; then the same loop
+   replayed on a fresh Session with the reference's Sampler, copying out for
+   every pick j (at most `cap`) its id and the hidden row its logits came from
+   (x_out + j*dim: the residual of the position that produced them, before the
+   final rmsnorm).  The last pick is the stop id when the generation stopped
+   on one (*stopped = 1).  Returns the number of picks, -1 on an error, -2
+   when the replay's ids differ from generate's (Stats::toks). */
+int ref_decode(const char* dir, int dtype, const int* prompt, int n, const oracle_sampling* opts, int max_tokens,
+               int threads, int cap, int* ids_out, float* x_out, int* stopped);
+
 #ifdef __cplusplus
 }
 #endif

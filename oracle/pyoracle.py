@@ -204,6 +204,8 @@ def _ref_tail_lib(build: str):
                                         ctypes.c_int, ctypes.c_longlong, _P, ctypes.c_longlong, _P, _P, ctypes.c_int]
         lib.ref_model_tail.argtypes = [ctypes.c_char_p, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P, _P,
                                        _P, _P, _P]
+        lib.ref_decode.argtypes = [ctypes.c_char_p, ctypes.c_int, _P, ctypes.c_int, ctypes.POINTER(OracleSampling),
+                                   ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P]
         _ref_tail[build] = lib
     return _ref_tail[build]
 
@@ -283,6 +285,34 @@ def ref_model_tail(model_dir, dtype, toks, build: str = "scalar", threads: int =
     name = {0: "f32", 1: "q8", 2: "q4"}[hdt]
     return {"x": x, "logits": logits, "dtype": name, "q": q, "s": None if hdt == 0 else sc, "norm": norm,
             "eps": float(eps[0])}
+
+
+def ref_decode(model_dir, dtype, prompt, opts: OracleSampling, max_tokens: int, build: str = "scalar",
+               threads: int = 1) -> dict:
+    """verbo::generate of the reference on a checkpoint (one generation), and
+    for every pick its id and the hidden row its logits came from (the
+    residual before the final rmsnorm).  Returns ids (picks,), x (picks, dim)
+    and stopped (the last pick is a stop id)."""
+    lib = _ref_tail_lib(build)
+    dt = DTYPES[dtype] if isinstance(dtype, str) else int(dtype)
+    meta = np.zeros(3, dtype=np.int32)
+    eps = np.zeros(1, dtype=np.float32)
+    path = str(model_dir).encode()
+    if lib.ref_model_tail(path, dt, None, 0, threads, _ptr(meta), _ptr(eps), None, None, None, None, None) != 0:
+        raise RuntimeError(f"the reference could not load {model_dir}")
+    dim = int(meta[0])
+    prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+    cap = max_tokens + 1
+    ids = np.zeros(cap, dtype=np.int32)
+    x = np.zeros((cap, dim), dtype=np.float32)
+    stopped = np.zeros(1, dtype=np.int32)
+    n = lib.ref_decode(path, dt, _ptr(prompt), prompt.size, ctypes.byref(opts), max_tokens, threads, cap, _ptr(ids),
+                       _ptr(x), _ptr(stopped))
+    if n == -2:
+        raise RuntimeError("the replayed decode loop disagrees with verbo::generate")
+    if n < 0:
+        raise RuntimeError(f"ref_decode failed on {model_dir}")
+    return {"ids": ids[:n].copy(), "x": x[:n].copy(), "stopped": bool(stopped[0])}
 
 
 def random_head(dtype: str, vocab: int, dim: int, seed: int = 0):

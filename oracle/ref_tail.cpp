@@ -94,3 +94,68 @@ extern "C" int ref_logits_tail(int dtype, int vocab, int dim, const void* q, con
   matmul(t, a, out, static_cast<int>(ld), pool);
   return 0;
 }
+
+// Residual row of the last position of the last eval: Session::Impl::run
+// splits an eval into batches of bmax rows and batch() leaves the rows of the
+// last one in x, so the last position is row (n - 1) % bmax.
+static const float* last_residual(verbo::Session& s, int n) {
+  const int bmax = 64;  // Session::Impl::bmax (src/session.cpp:28)
+  const int dim = s.model().impl().cfg.dim;
+  return residual_of(s)->data() + static_cast<std::size_t>((n - 1) % bmax) * dim;
+}
+
+extern "C" int ref_decode(const char* dir, int dtype, const int* prompt, int n, const oracle_sampling* opts,
+                          int max_tokens, int threads, int cap, int* ids_out, float* x_out, int* stopped) {
+  using namespace verbo;
+  try {
+    if (!opts || opts->seed == 0 || n < 1 || cap < 1) return -1;
+    auto m = Model::load(dir, static_cast<DType>(dtype));
+    const int dim = m->impl().cfg.dim;
+    const int nv = m->cfg().vocab;
+    GenOpts go;
+    go.max_tokens = max_tokens;
+    go.smp.temp = opts->temp;
+    go.smp.top_k = opts->top_k;
+    go.smp.top_p = opts->top_p;
+    go.smp.min_p = opts->min_p;
+    go.smp.repeat = opts->repeat;
+    go.smp.repeat_last = opts->repeat_last;
+    go.smp.seed = opts->seed;
+    const std::vector<int> pr(prompt, prompt + n);
+    Stats st;
+    {
+      Session ses(m, 0, threads < 1 ? 1 : threads);
+      st = generate(ses, pr, go, [](std::string_view) { return true; });
+    }
+    // the same loop, step by step, keeping each pick's hidden row
+    Session ses(m, 0, threads < 1 ? 1 : threads);
+    Sampler smp(go.smp);
+    for (const int t : pr) smp.accept(t);
+    const float* lg = ses.eval(pr);
+    const float* xr = last_residual(ses, n);
+    int picks = 0, gen = 0;
+    *stopped = 0;
+    while (gen < go.max_tokens) {
+      const int id = smp.pick(lg, nv);
+      if (picks >= cap) return -1;
+      ids_out[picks] = id;
+      std::memcpy(x_out + static_cast<std::size_t>(picks) * dim, xr, sizeof(float) * dim);
+      ++picks;
+      if (m->is_stop(id)) {
+        *stopped = 1;
+        break;
+      }
+      smp.accept(id);
+      ++gen;
+      if (ses.pos() >= ses.ctx() || gen >= go.max_tokens) break;
+      lg = ses.eval(&id, 1);
+      xr = last_residual(ses, 1);
+    }
+    if (gen != st.gen || *stopped != (st.stopped ? 1 : 0)) return -2;
+    for (int j = 0; j < gen; ++j)
+      if (ids_out[j] != st.toks[static_cast<std::size_t>(j)]) return -2;
+    return picks;
+  } catch (...) {
+    return -1;
+  }
+}

@@ -125,6 +125,7 @@ def load_library():
         "verbo_cuda_comm_free": (None, [_P]),
         "verbo_cuda_comm_wait": (ctypes.c_int, [_P, _P, ctypes.c_int]),
         "verbo_cuda_comm_mark_next": (ctypes.c_int, [_P, _P, _P]),
+        "verbo_cuda_batch_decode": (ctypes.c_int, [_P, _P, _P, ctypes.c_longlong, _P, _P, _P]),
         "verbo_cuda_sharded_sample": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong,
                                                      ctypes.c_int, ctypes.c_int, _P, _P, ctypes.POINTER(_Sampling),
                                                      ctypes.c_int, _P, _P, _P, _P]),
@@ -389,6 +390,33 @@ class Batch:
             out = torch.empty(rows, dtype=torch.int32, device=logits.device)
         _ok(self._lib.verbo_cuda_batch_step(self._h, _dptr(logits, True), cols if vocab is None else vocab,
                                             logits.stride(0), _dptr(out), _dptr(stats), _stream(cuda_stream)))
+        return out
+
+    def decode(self, tail: "Tail", hidden, out=None, stats=None, cuda_stream=None):
+        """One decode step of the B generations (verbo_cuda_batch_decode):
+        `hidden` [B, dim] float32 rows of final hidden state (a numpy array,
+        a CPU tensor or a CUDA tensor) -> the tail's logits on the device ->
+        pick + accept.  Returns the ids: a numpy int32 array when `hidden` is
+        on the host (the call then waits for them), else a CUDA tensor; `out`
+        may be either kind."""
+        import numpy as np
+        import torch
+
+        if isinstance(hidden, np.ndarray):
+            hidden = torch.from_numpy(np.ascontiguousarray(hidden, dtype=np.float32))
+        if hidden.dim() != 2 or hidden.shape[0] != self.streams:
+            raise VerboCudaError("hidden must have one row per stream")
+        if hidden.dtype != torch.float32 or (hidden.shape[1] > 1 and hidden.stride(1) != 1):
+            raise VerboCudaError("hidden rows must be contiguous float32")
+        if out is None:
+            out = (torch.empty(self.streams, dtype=torch.int32, device=hidden.device) if hidden.is_cuda
+                   else np.empty(self.streams, dtype=np.int32))
+        out_ptr = out.ctypes.data if isinstance(out, np.ndarray) else out.data_ptr()
+        if isinstance(out, np.ndarray) and (out.dtype != np.int32 or out.size != self.streams):
+            raise VerboCudaError("out must hold one int32 per stream")
+        st_ptr = None if stats is None else (stats.ctypes.data if isinstance(stats, np.ndarray) else stats.data_ptr())
+        _ok(self._lib.verbo_cuda_batch_decode(self._h, tail._h, hidden.data_ptr(), hidden.stride(0), out_ptr, st_ptr,
+                                              _stream(cuda_stream)))
         return out
 
 

@@ -611,6 +611,14 @@ struct verbo_cuda_batch {
   unsigned long long* d_rng = nullptr;
   int* d_stage = nullptr;
   long long stage_cap = 0;
+  // staging of verbo_cuda_batch_decode: host hidden rows in, the step's
+  // logits rows, host ids / stats out
+  float* d_hidden = nullptr;
+  long long hidden_cap = 0;  // floats
+  float* d_logits = nullptr;
+  long long logits_cap = 0;  // floats
+  int* d_ids = nullptr;
+  verbo_row_stats* d_stats = nullptr;
 };
 
 namespace {
@@ -624,7 +632,14 @@ void batch_release(verbo_cuda_batch* b) {
   cudaFree(b->d_off);
   cudaFree(b->d_rng);
   cudaFree(b->d_stage);
+  cudaFree(b->d_hidden);
+  cudaFree(b->d_logits);
+  cudaFree(b->d_ids);
+  cudaFree(b->d_stats);
 }
+
+void batch_run(verbo_cuda_batch* b, const float* logits, int vocab, long long ld, int* out_ids,
+               verbo_row_stats* stats, cudaStream_t s);
 
 void batch_check_stream(const verbo_cuda_batch* b, int i) {
   if (!b) fail("batch is NULL");
@@ -752,7 +767,19 @@ VERBO_CUDA_API int verbo_cuda_batch_step(verbo_cuda_batch* b, const float* logit
         if (vocab < 1 || vocab > vb::kMaxVocab) fail("vocab must be in [1, " + std::to_string(vb::kMaxVocab) + "]");
         if (ld < vocab) fail("ld must be >= vocab");
         cuda_ok(cudaSetDevice(b->device), "cudaSetDevice");
-        const cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+        batch_run(b, logits, vocab, ld, out_ids, stats, static_cast<cudaStream_t>(cuda_stream));
+        return 0;
+      },
+      -1);
+}
+
+}  // extern "C"
+
+namespace {
+
+// One pick + accept per stream from B device rows (arguments checked).
+void batch_run(verbo_cuda_batch* b, const float* logits, int vocab, long long ld, int* out_ids,
+               verbo_row_stats* stats, cudaStream_t s) {
         vb::DevOpts o = make_opts(b->cfg, vocab, b->pen);
         // the rings hold exactly the windows: the CSR view (full-vocabulary
         // kernel) reads each whole ring row, -1 slots marking nothing
@@ -767,12 +794,9 @@ VERBO_CUDA_API int verbo_cuda_batch_step(verbo_cuda_batch* b, const float* logit
           a.ring_len = b->ring_len;
         }
         dispatch_rows(a, o, vocab, s, b->pen ? b->d_win : nullptr, b->win_w);
-        return 0;
-      },
-      -1);
 }
 
-}  // extern "C"
+}  // namespace
 
 // ---------------------------------------------------------------------------
 // Logits producer tail: the head (weights, zero-padded scales, norm weight)
@@ -788,6 +812,8 @@ struct verbo_cuda_tail {
 };
 
 namespace {
+
+void tail_run(verbo_cuda_tail* t, const float* x, int n, long long ldx, float* logits, long long ld, cudaStream_t s);
 
 void tail_release(verbo_cuda_tail* t) {
   if (!t) return;
@@ -863,7 +889,18 @@ VERBO_CUDA_API int verbo_cuda_tail_logits(verbo_cuda_tail* t, const float* x, in
         if (ldx < t->h.dim) fail("ldx must be >= dim");
         if (ld < t->h.vocab) fail("ld must be >= vocab");
         cuda_ok(cudaSetDevice(t->device), "cudaSetDevice");
-        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        tail_run(t, x, n, ldx, logits, ld, static_cast<cudaStream_t>(stream));
+        return 0;
+      },
+      -1);
+}
+
+}  // extern "C"
+
+namespace {
+
+// n device rows of hidden state -> n device rows of logits (arguments checked).
+void tail_run(verbo_cuda_tail* t, const float* x, int n, long long ldx, float* logits, long long ld, cudaStream_t s) {
         vb::TailArgs a{};
         a.x = x;
         a.ldx = ldx;
@@ -884,6 +921,68 @@ VERBO_CUDA_API int verbo_cuda_tail_logits(verbo_cuda_tail* t, const float* x, in
         }
         vb::tail_scratch_attach(t->h, n, sc.data, a);
         cuda_ok(vb::launch_tail(t->h, a, s), "kernel launch");
+}
+
+// Grows a device staging buffer of `count` elements (the old one may still be
+// read by work queued on `s`).
+template <typename T>
+void grow(T*& buf, long long& cap, long long count, cudaStream_t s, const char* what) {
+  if (cap >= count) return;
+  cuda_ok(cudaStreamSynchronize(s), "stream");
+  cudaFree(buf);
+  buf = nullptr;
+  cap = 0;
+  cuda_ok(cudaMalloc(&buf, sizeof(T) * static_cast<size_t>(count)), what);
+  cap = count;
+}
+
+bool on_device(const void* p) {
+  cudaPointerAttributes pa{};
+  cuda_ok(cudaPointerGetAttributes(&pa, p), "cudaPointerGetAttributes");
+  return pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged;
+}
+
+}  // namespace
+
+extern "C" {
+
+VERBO_CUDA_API int verbo_cuda_batch_decode(verbo_cuda_batch* b, verbo_cuda_tail* t, const float* hidden,
+                                           long long ldx, int* out_ids, verbo_row_stats* stats, void* cuda_stream) {
+  return guard(
+      [&]() {
+        if (!b || !t) fail("batch and tail must not be NULL");
+        if (!hidden || !out_ids) fail("hidden and out_ids must not be NULL");
+        if (t->device != b->device) fail("the tail and the batch must live on the same device");
+        const int B = b->streams, dim = t->h.dim, vocab = t->h.vocab;
+        if (vocab > vb::kMaxVocab) fail("vocab must be <= " + std::to_string(vb::kMaxVocab));
+        if (ldx < dim) fail("ldx must be >= dim");
+        cuda_ok(cudaSetDevice(b->device), "cudaSetDevice");
+        const cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+        // the hidden rows: read in place on the device, else one 2-D upload
+        const float* x = hidden;
+        long long lx = ldx;
+        if (!on_device(hidden)) {
+          grow(b->d_hidden, b->hidden_cap, static_cast<long long>(B) * dim, s, "cudaMalloc hidden rows");
+          cuda_ok(cudaMemcpy2DAsync(b->d_hidden, sizeof(float) * dim, hidden, sizeof(float) * ldx, sizeof(float) * dim,
+                                    B, cudaMemcpyHostToDevice, s),
+                  "upload hidden rows");
+          x = b->d_hidden;
+          lx = dim;
+        }
+        grow(b->d_logits, b->logits_cap, static_cast<long long>(B) * vocab, s, "cudaMalloc logits rows");
+        tail_run(t, x, B, lx, b->d_logits, vocab, s);
+        // the logits stay on the device: the pick reads them where the tail wrote them
+        const bool ids_host = !on_device(out_ids);
+        const bool stats_host = stats && !on_device(stats);
+        if (ids_host && !b->d_ids) cuda_ok(cudaMalloc(&b->d_ids, sizeof(int) * B), "cudaMalloc ids");
+        if (stats_host && !b->d_stats) cuda_ok(cudaMalloc(&b->d_stats, sizeof(verbo_row_stats) * B), "cudaMalloc stats");
+        batch_run(b, b->d_logits, vocab, vocab, ids_host ? b->d_ids : out_ids, stats_host ? b->d_stats : stats, s);
+        if (ids_host)
+          cuda_ok(cudaMemcpyAsync(out_ids, b->d_ids, sizeof(int) * B, cudaMemcpyDeviceToHost, s), "download ids");
+        if (stats_host)
+          cuda_ok(cudaMemcpyAsync(stats, b->d_stats, sizeof(verbo_row_stats) * B, cudaMemcpyDeviceToHost, s),
+                  "download stats");
+        if (ids_host || stats_host) cuda_ok(cudaStreamSynchronize(s), "stream");
         return 0;
       },
       -1);
