@@ -955,7 +955,7 @@ def uses_window(w: wl.Workload) -> bool:
     return w.repeat != 1.0 and w.hist_len > 0 and 0 < w.repeat_last <= 2048
 
 
-NUC_CHUNK_ROWS = 512  # rows per chunk of the streaming full-vocabulary path (nucleus.cu, kChunkRows)
+NUC_CHUNK_ROWS = 2048  # rows per chunk of the streaming full-vocabulary path (nucleus.cu, kChunkRows)
 
 
 def streaming_full_vocab(w: wl.Workload) -> bool:

@@ -51,7 +51,7 @@ namespace nuc {
 constexpr int NT = 256;
 constexpr int kW = NT / 32;
 constexpr int kSliceCols = 32768;    // columns of one slice (at most)
-constexpr int kChunkRows = 512;      // rows per B / C launch (their scratch)
+constexpr int kChunkRows = 2048;     // rows per B / C launch (their scratch)
 constexpr int kCells = 2048;         // histogram capacity
 constexpr int kCellTarget = 1024;    // the row's x-range is spread over about this many cells
 constexpr int kKMin = 6;             // cells at most 2^-6 wide: |r| <= 2^-7
