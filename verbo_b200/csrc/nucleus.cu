@@ -3,8 +3,9 @@
 // column, the top-p cutoff and the inverse-CDF draw, without sorting and with
 // every logits row read from HBM once.
 //
-// Three streaming kernels, each over every (row, slice of <= kSliceCols
-// columns) with one CTA per slice and no CTA ever waiting for another:
+// Three streaming passes, each a kernel over every (row, slice of <=
+// kSliceCols columns) with one CTA per slice and no CTA ever waiting for
+// another, then one resolve CTA per row:
 //
 //   A  streams the slice from HBM and publishes its maximum and its
 //                 smallest finite value (row atomics);
@@ -14,15 +15,16 @@
 //                 per-row counter) merges the slices' histograms and places the
 //                 top-p cutoff (src/sampler.cpp:92-100) and the draw (:101-108)
 //                 in one or two cells each;
-//   C  gathers the slice's members of those cells; the row's last
-//                 slice resolves the pick among them with the reference's fp64
+//   C  gathers the slice's members of those cells;
+//   R  resolves the pick among the row's members with the reference's fp64
 //                 weights, in the reference's order.
 //
-// Rows go in chunks of kChunkRows; launch t of nuc_kernel runs A of chunk t,
-// B of chunk t - 1 and C of chunk t - 2 side by side (their CTAs interleaved),
-// so that the HBM-bound A passes overlap the compute of the B passes.  Each
-// phase only reads what an earlier launch wrote, and the histograms, targets
-// and members live in two chunk-sized buffers used by alternate chunks.
+// Rows go in chunks of kChunkRows (A, B, C, R kernels per chunk); each pass
+// only reads what an earlier kernel wrote, so the kernels need no waits, and
+// each has the resources its pass needs: the A pass, a plain stream, runs at
+// full occupancy.  A single fused kernel running the passes of consecutive
+// chunks side by side was slower: its CTAs all carried the largest pass's
+// registers and shared memory.
 //
 // Exact masses without an exponential per column: cell j holds the columns
 // whose x rounds to -j 2^-K; with r = x + j 2^-K (|r| <= 2^-(K+1)),
@@ -155,7 +157,7 @@ struct RowState {
   unsigned maxkey;      // ord32 of the row maximum (atomicMax)
   unsigned minkey_inv;  // ~ord32 of the smallest finite value (atomicMax); 0 = none
   unsigned cnt2;        // B slices done
-  unsigned cnt3;        // C slices done
+  unsigned pad;
 };
 struct SliceSum {
   unsigned ucount;   // underflow columns
@@ -196,7 +198,7 @@ struct Layout {
 };
 static size_t up256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 static Layout layout(int rows, int ns) {
-  const size_t cr = static_cast<size_t>(std::min(rows, 2 * kChunkRows));
+  const size_t cr = static_cast<size_t>(std::min(rows, kChunkRows));
   Layout l;
   l.off_rs = 256;
   l.zero_bytes = l.off_rs + sizeof(RowState) * static_cast<size_t>(rows);
@@ -311,7 +313,10 @@ struct Shared {
 constexpr size_t kHistBytes = static_cast<size_t>(kCells) * 8;
 constexpr size_t kCumBytes = static_cast<size_t>(kCells) * 12;
 constexpr size_t kMemberBytes = static_cast<size_t>(kMemberCap) * 24 + static_cast<size_t>(kSubBins) * 12;
-constexpr size_t kSmem = std::max(std::max(kHistBytes, kCumBytes), kMemberBytes);
+constexpr size_t kBSmem = std::max(kHistBytes, kCumBytes);         // B pass + its row merge
+constexpr size_t kCSmem = static_cast<size_t>(kMemberCap) * 8;     // C pass: the slice's members
+constexpr size_t kRSmem = kMemberBytes;                             // resolve
+constexpr int kBBlocks = 4, kCBlocks = 6;                           // resident CTAs per SM aimed at
 
 template <class T>
 __device__ __forceinline__ T bsum(T x, T* ws) {
@@ -421,7 +426,7 @@ __device__ __noinline__ void run_b(int row, int s, unsigned char* smem, Shared& 
   const DevOpts& o = sh.o;
   const RowArgs& a = p.a;
   RowState* st = p.rs + row;
-  const int slot = row % (2 * kChunkRows);
+  const int slot = row % kChunkRows;
   if (threadIdx.x == 0) sh.g = row_grid(st, o.temp);
   __syncthreads();
   const Grid g = sh.g;
@@ -523,7 +528,7 @@ __device__ __noinline__ void merge_b(int row, unsigned char* smem, Shared& sh) {
   const DevOpts& o = sh.o;
   const Grid& g = sh.g;
   const RowArgs& a = p.a;
-  const int slot = row % (2 * kChunkRows);
+  const int slot = row % kChunkRows;
   const int nc = g.ncr + 1;
   double* cum = reinterpret_cast<double*>(smem);             // [kCells] inclusive cumulative mass
   unsigned* cnt = reinterpret_cast<unsigned*>(cum + kCells);  // [kCells] columns before each cell
@@ -689,14 +694,12 @@ __device__ __noinline__ void merge_b(int row, unsigned char* smem, Shared& sh) {
 }
 
 // ------------------------------------------------------------- C items ----
-__device__ __noinline__ void merge_c(int row, unsigned char* smem, Shared& sh);
-
 __device__ __noinline__ void run_c(int row, int s, unsigned char* smem, Shared& sh) {
   const NucArgs& p = sh.p;
   const DevOpts& o = sh.o;
   const RowArgs& a = p.a;
   RowState* st = p.rs + row;
-  const int ms = row % (2 * kChunkRows);
+  const int ms = row % kChunkRows;
   const Targets* tg = p.tg + ms;
   const int fail = __ldcg(&tg->fail);
   if (!fail) {
@@ -754,15 +757,6 @@ __device__ __noinline__ void run_c(int row, int s, unsigned char* smem, Shared& 
     for (unsigned i = threadIdx.x; i < cnt; i += NT)
       if (sh.mbase + i < static_cast<unsigned>(kMemberCap)) mem[sh.mbase + i] = loc[i];
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned old = atomicAdd(&st->cnt3, 1u);
-    sh.last = old == static_cast<unsigned>(p.ns - 1);
-    __threadfence();
-  }
-  __syncthreads();
-  if (sh.last) merge_c(row, smem, sh);
 }
 
 // Among members [0, nm) (keys, exact weights), those in cells [c0, c1] in key
@@ -903,7 +897,7 @@ __device__ __noinline__ void merge_c(int row, unsigned char* smem, Shared& sh) {
   const NucArgs& p = sh.p;
   const DevOpts& o = sh.o;
   const RowArgs& a = p.a;
-  const int ms = row % (2 * kChunkRows);
+  const int ms = row % kChunkRows;
   const Targets* tg = p.tg + ms;
   if (threadIdx.x == 0) sh.g = row_grid(p.rs + row, o.temp);
   __syncthreads();
@@ -986,22 +980,36 @@ __device__ __forceinline__ void setup(const NucArgs& p, const DevOpts& o, Shared
   __syncthreads();
 }
 
-// One launch: CTA i takes phase i mod 3 (C, B, A) and slice i / 3 of that
-// phase's chunk (row = first row + slice index / ns).
-__global__ void __launch_bounds__(NT, 4) nuc_kernel(const NucArgs p, const DevOpts o) {
+// One kernel per pass, each with the resources its pass needs: the A pass
+// streams with no shared memory at 8 CTAs per SM, the B pass keeps its
+// histogram (and the row merge of its last slice) in 24 KB, the C pass its
+// members in 16 KB; the resolve runs one CTA per row.  CTA i of the A, B and C
+// kernels takes row first + i / ns, slice i mod ns.
+__global__ void __launch_bounds__(NT, 8) nuc_a_kernel(const NucArgs p, const DevOpts o) {
+  __shared__ Shared sh;
+  const int j = static_cast<int>(blockIdx.x);
+  setup(p, o, sh);
+  run_a(p.rowa + j / p.ns, j % p.ns, sh);
+}
+__global__ void __launch_bounds__(NT, kBBlocks) nuc_b_kernel(const NucArgs p, const DevOpts o) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ Shared sh;
-  const int phase = static_cast<int>(blockIdx.x % 3u), j = static_cast<int>(blockIdx.x / 3u);
-  const int n = phase == 0 ? p.nc : (phase == 1 ? p.nb : p.na);
-  if (j >= n * p.ns) return;
+  const int j = static_cast<int>(blockIdx.x);
   setup(p, o, sh);
-  const int s = j % p.ns;
-  if (phase == 0)
-    run_c(p.rowc + j / p.ns, s, smem, sh);
-  else if (phase == 1)
-    run_b(p.rowb + j / p.ns, s, smem, sh);
-  else
-    run_a(p.rowa + j / p.ns, s, sh);
+  run_b(p.rowb + j / p.ns, j % p.ns, smem, sh);
+}
+__global__ void __launch_bounds__(NT, kCBlocks) nuc_c_kernel(const NucArgs p, const DevOpts o) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ Shared sh;
+  const int j = static_cast<int>(blockIdx.x);
+  setup(p, o, sh);
+  run_c(p.rowc + j / p.ns, j % p.ns, smem, sh);
+}
+__global__ void __launch_bounds__(NT, 4) nuc_r_kernel(const NucArgs p, const DevOpts o) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ Shared sh;
+  setup(p, o, sh);
+  merge_c(p.rowc + static_cast<int>(blockIdx.x), smem, sh);
 }
 
 }  // namespace nuc
@@ -1033,23 +1041,24 @@ cudaError_t launch_nucleus(const RowArgs& a, const DevOpts& o, void* scratch, cu
   p.cells = reinterpret_cast<uint2*>(b + l.off_cells);
   p.tg = reinterpret_cast<Targets*>(b + l.off_tg);
   p.members = reinterpret_cast<unsigned long long*>(b + l.off_mem);
-  static bool attrs = false;
-  if (!attrs) {
-    e = cudaFuncSetAttribute(nuc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem));
+  // the resolve's shared memory is above the 48 KB default (per device)
+  static unsigned long long attrs = 0;
+  int dev = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64 || !(attrs >> dev & 1ull)) {
+    e = cudaFuncSetAttribute(nuc_r_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kRSmem));
     if (e != cudaSuccess) return e;
-    attrs = true;
+    if (dev < 64) attrs |= 1ull << dev;
   }
-  const int chunks = (a.rows + kChunkRows - 1) / kChunkRows;
-  auto rows_of = [&](int c) { return c >= 0 && c < chunks ? std::min(kChunkRows, a.rows - c * kChunkRows) : 0; };
-  for (int t = 0; t < chunks + 2; ++t) {
-    p.rowa = t * kChunkRows;
-    p.rowb = (t - 1) * kChunkRows;
-    p.rowc = (t - 2) * kChunkRows;
-    p.na = rows_of(t);
-    p.nb = rows_of(t - 1);
-    p.nc = rows_of(t - 2);
-    const int most = std::max(p.na, std::max(p.nb, p.nc));
-    nuc_kernel<<<3 * most * ns, NT, kSmem, s>>>(p, o);
+  for (int r0 = 0; r0 < a.rows; r0 += kChunkRows) {
+    const int n = std::min(kChunkRows, a.rows - r0);
+    p.rowa = p.rowb = p.rowc = r0;
+    p.na = p.nb = p.nc = n;
+    nuc_a_kernel<<<n * ns, NT, 0, s>>>(p, o);
+    nuc_b_kernel<<<n * ns, NT, kBSmem, s>>>(p, o);
+    nuc_c_kernel<<<n * ns, NT, kCSmem, s>>>(p, o);
+    nuc_r_kernel<<<n, NT, kRSmem, s>>>(p, o);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
