@@ -971,7 +971,7 @@ def kernels_per_step(w: wl.Workload, rows: int) -> int:
     if w.shards > 1:
         return 3 + win   # [window_kernel] + split_kernel<emit> + merge_slices_kernel + merge_kernel
     if streaming_full_vocab(w):
-        return -(-rows // NUC_CHUNK_ROWS) + 2 + 1   # nuc_kernel per chunk step + general_list_kernel
+        return 4 * -(-rows // NUC_CHUNK_ROWS) + 1   # nuc_a/b/c/r_kernel per chunk + general_list_kernel
     return 1 if kernel_name(w) == "general_kernel" else 2 + win
 
 
@@ -982,7 +982,7 @@ def kernel_name(w: wl.Workload) -> str:
     if 0 < w.top_k < w.vocab and w.top_k <= 256:
         return win + "split_kernel<sample> + merge_slices_kernel"
     if streaming_full_vocab(w):
-        return "nuc_kernel (A, B, C passes; every launch of the step) + general_list_kernel"
+        return "nuc_a_kernel + nuc_b_kernel + nuc_c_kernel + nuc_r_kernel (per chunk) + general_list_kernel"
     return "general_kernel"
 
 

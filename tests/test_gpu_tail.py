@@ -65,7 +65,7 @@ def test_golden_hidden_rows_give_the_reference_session_logits(cuda_lib):
 
 
 SHAPES = [(1, 32, 1), (3, 96, 129), (8, 896, 300), (9, 1056, 257), (16, 64, 1000), (17, 160, 513),
-          (33, 128, 700), (64, 896, 129), (65, 1056, 300), (130, 96, 4099)]
+          (33, 128, 700), (64, 896, 129), (65, 1056, 300), (130, 96, 4099), (192, 896, 385), (256, 1056, 1500)]
 
 
 @pytest.mark.parametrize("dtype", ["q8", "q4", "f32"])
@@ -81,6 +81,48 @@ def test_tail_matches_oracle(cuda_lib, dtype, n, dim, vocab):
     want, _, _ = po.logits_tail(dtype, q, s, norm, 1e-6, x)
     got = run_tail(vb, dtype, q, s, norm, 1e-6, x)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+TC_SHAPES = [(33, 128, 700), (64, 896, 129), (65, 1056, 300), (130, 96, 4099), (192, 896, 385), (256, 1056, 1500)]
+
+
+@pytest.mark.parametrize("n,dim,vocab", TC_SHAPES)
+def test_tcgen05_tail_matches_oracle(cuda_lib, monkeypatch, n, dim, vocab):
+    """The tcgen05 head kernel (Q8, more than 32 tokens; selected by
+    VERBO_CUDA_TAIL_TCGEN05=1) bit for bit against the oracle: ragged vocab
+    tiles, partial K chunks (dim 1056, 96) and several token tiles."""
+    need_gpu()
+    import verbo_b200 as vb
+
+    monkeypatch.setenv("VERBO_CUDA_TAIL_TCGEN05", "1")
+    g = np.random.default_rng(n * 1000 + dim + vocab + 7)
+    q, s = po.random_head("q8", vocab, dim, seed=vocab + dim + 7)
+    norm = (1 + 0.25 * g.standard_normal(dim)).astype(np.float32)
+    x = (g.standard_normal((n, dim)) * 3.0).astype(np.float32)
+    want, _, _ = po.logits_tail("q8", q, s, norm, 1e-6, x)
+    got = run_tail(vb, "q8", q, s, norm, 1e-6, x)
+    vb.check()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_tcgen05_tail_full_vocab(cuda_lib, monkeypatch, qwen_head):
+    """256 rows at V = 151936 on the tcgen05 kernel equal the mma.sync
+    kernel's logits bit for bit, and a slice of vocab ids equals the oracle."""
+    need_gpu()
+    import verbo_b200 as vb
+
+    q, s, norm = qwen_head
+    x = (np.random.default_rng(14).standard_normal((256, 896)) * 3.0).astype(np.float32)
+    t = vb.Tail("q8", q, s, norm, 1e-6)
+    xd = torch.from_numpy(x).cuda()
+    base = t.logits(xd).cpu().numpy()
+    monkeypatch.setenv("VERBO_CUDA_TAIL_TCGEN05", "1")
+    tc = t.logits(xd).cpu().numpy()
+    vb.check()
+    assert np.array_equal(tc.view(np.uint32), base.view(np.uint32))
+    ids = np.r_[0:300, 151936 - 300:151936]
+    want, _, _ = po.logits_tail("q8", q[ids], s[ids], norm, 1e-6, x)
+    assert np.array_equal(tc[:, ids].view(np.uint32), want.view(np.uint32))
 
 
 def test_tail_strided_rows_and_extreme_codes(cuda_lib):

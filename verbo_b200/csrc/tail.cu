@@ -12,7 +12,14 @@
 //                       src/kernels.cpp:576-600);
 // tail_head_f32_kernel  F32 heads: the same ring over a tile-major fp32 head,
 //                       one vocab row per consumer thread (dot_f32,
-//                       src/kernels.cpp:570-574).
+//                       src/kernels.cpp:570-574);
+// tail_head_tc_kernel   Q8 heads with more than 32 tokens, on request
+//                       (VERBO_CUDA_TAIL_TCGEN05=1): tcgen05.mma kind::i8 per
+//                       block into tensor memory, the same epilogue in
+//                       epilogue warps.  Bit-identical, but slower than the
+//                       mma.sync kernel here: both are bound by the
+//                       epilogue's fp32 work per block, and the tensor-memory
+//                       round trip of every block adds to it.
 //
 // Every rounding step is the reference scalar build's, in its order: the sum
 // of squares runs sequentially, products and sums are rounded separately
@@ -21,6 +28,7 @@
 // forms, r = fma(scale_w * scale_x, float(block sum), r), in block order.
 #include <cuda_fp16.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include "device.cuh"
@@ -590,6 +598,331 @@ cudaError_t launch_head_f32(const TailHead& h, const TailArgs& a, cudaStream_t s
   return cudaLaunchKernelEx(&cfg, kern, h, a);
 }
 
+// ---------------------------------------------- Q8 heads, > 32 tokens ----
+// tcgen05 form of the quantised head for batches: one CTA per SM, persistent
+// over work items (head tile of M = 128 vocab rows, token tile of N = 64 or
+// 128 tokens), token tiles fastest, so that the CTAs sharing a head tile run
+// together and all but one read it from L2.  The operands stay in the
+// layouts the mma.sync kernel streams: a head block is 128 rows x 128 bytes
+// of K with 16-byte units XOR-swizzled by (row & 7), an activation block N
+// token rows the same way, which is the tensor cores' K-major 128-byte-swizzle
+// layout.
+//
+//   warp 0 (lane 0)   streams each chunk of 4 K blocks (the activation codes
+//                     and the head block with its fp16 scales) into a ring of
+//                     shared-memory stages with bulk copies (full / empty);
+//   warp 1 (lane 0)   issues one tcgen05.mma kind::i8 per 32-element block,
+//                     D = A_b * B_b^T + D, into the next of 512 / N
+//                     accumulators in tensor memory, and commits it to that
+//                     accumulator's barrier;
+//   warps 2..17       the epilogue: warp w reads tensor-memory lanes
+//                     32 (w mod 4) .. +31 (its vocab rows) and a quarter of
+//                     the token columns of one block, refills the accumulator
+//                     with the bits of 1.5 * 2^23 (so that the next block's D,
+//                     read as a float, is 1.5 * 2^23 + its block sum, exact
+//                     since |sum| < 2^22) and releases it, then applies the
+//                     reference's r = fma(sw * sx, float(sum), r) in block order.
+//
+// Every wait is bounded; a timeout records kErrTailWait and the CTA stops.
+constexpr int kTcEpiWarps = 16;
+constexpr int kTcThreads = (2 + kTcEpiWarps) * 32;
+constexpr int kTcStages = 4;
+constexpr size_t kTcSmemLimit = 227 * 1024;
+
+template <int N>
+struct TcCfg {
+  static constexpr int CTAS = N == 64 ? 2 : 1;                  // resident CTAs per SM
+  static constexpr int STAGES = N == 64 ? 3 : kTcStages;
+  static constexpr int ACT = N * kTailChunk;                    // one chunk's activation codes
+  static constexpr int HEAD = TileBytes<false>::TB;             // a head block: weights + scales
+  static constexpr int STAGE = ACT + ((HEAD + 1023) & ~1023);   // parts 1024-byte aligned
+  static constexpr int CPT = N / 4;                             // token columns per epilogue thread
+  static constexpr uint32_t COLS = 512 / CTAS;                  // this CTA's share of tensor memory
+  static constexpr int NBUF = COLS / N;                         // accumulators
+  static size_t smem(int nkc) {
+    return 1024 + static_cast<size_t>(STAGES) * STAGE + static_cast<size_t>(nkc) * 4 * N * 4 + 64 * NBUF + 256;
+  }
+};
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (start address in 16-byte units, SM100 descriptor version 1).
+__device__ __forceinline__ uint64_t tc_desc(const void* p) {
+  const uint64_t addr = (smem_u32(p) >> 4) & 0x3FFFu;
+  return addr | (1ull << 16) | (static_cast<uint64_t>(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+// D[tmem] = A * B^T (+ D when accumulate), 128 x N, int8 x int8 -> int32.
+__device__ __forceinline__ void tc_mma_i8(uint32_t d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// 8 consecutive 32-bit columns of this warp's 32 lanes; complete after tc_wait_ld.
+__device__ __forceinline__ void tc_ld8_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 4 consecutive floats of shared memory, in program order (not hoisted).
+__device__ __forceinline__ float4 lds4(const float* p) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(smem_u32(p)));
+  return v;
+}
+// The magic bits into 16 consecutive columns of this warp's 32 lanes.
+constexpr uint32_t kMagicU = static_cast<uint32_t>(kMagicBits);
+__device__ __forceinline__ void tc_st16_magic(uint32_t taddr) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(kMagicU), "r"(kMagicU), "r"(kMagicU), "r"(kMagicU), "r"(kMagicU), "r"(kMagicU), "r"(kMagicU), "r"(kMagicU),
+      "r"(kMagicU), "r"(kMagicU), "r"(kMagicU), "r"(kMagicU), "r"(kMagicU), "r"(kMagicU), "r"(kMagicU), "r"(kMagicU)
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+template <int N>
+__global__ void __launch_bounds__(kTcThreads, TcCfg<N>::CTAS) tail_head_tc_kernel(TailHead h, TailArgs a) {
+  using C = TcCfg<N>;
+  extern __shared__ __align__(1024) unsigned char sm_raw[];
+  // the 128-byte swizzle is a function of the address: stages start 1024-aligned
+  unsigned char* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
+  const int nkc = h.nkc, nb = h.dim / kTailBlk;
+  const int ncol = a.n_pad / N;
+  const int items = h.ntile * ncol;
+  const int G = gridDim.x;            // a multiple of ncol: this CTA's token tile never changes
+  const int ct = static_cast<int>(blockIdx.x) % ncol;
+  float* XS = reinterpret_cast<float*>(sm + C::STAGES * C::STAGE);  // [nkc][4][N] scales of token tile ct
+  uint64_t* full = reinterpret_cast<uint64_t*>(XS + static_cast<size_t>(nkc) * 4 * N);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* accf = empty + C::STAGES;  // [NBUF] an accumulator holds a finished block
+  uint64_t* acce = accf + C::NBUF;     // [NBUF] an accumulator was read and refilled
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(acce + C::NBUF);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const size_t actb = static_cast<size_t>(N) * (kTailChunk + 16);
+  grid_release();  // the next kernel may be scheduled; a programmatic one waits for this grid
+  if (tid == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1 + kTcEpiWarps);  // the MMAs' commit + every epilogue warp (head scales read)
+    }
+    for (int i = 0; i < C::NBUF; ++i) {
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], kTcEpiWarps);
+    }
+    *abort_flag = 0;
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                 "r"(C::COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  grid_wait();  // the norm kernel's activation blocks are complete and visible
+  for (int i = tid; i < nkc * 4 * N; i += kTcThreads) {
+    const int kc = i / (4 * N);
+    XS[i] = reinterpret_cast<const float*>(a.act + (static_cast<size_t>(kc) * ncol + ct) * actb +
+                                           N * kTailChunk)[i - kc * 4 * N];
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const int q = warp & 3, grp = (warp - 2) >> 2;  // epilogue: lane quadrant, token quarter
+  const uint32_t tl = tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(grp * C::CPT);
+
+  const int mine = static_cast<int>(blockIdx.x) < items ? (items - static_cast<int>(blockIdx.x) + G - 1) / G : 0;
+  const int total = mine * nkc;  // chunks this CTA streams
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int g = 0; g < total; ++g) {
+        const int s = g % C::STAGES;
+        if (g >= C::STAGES && !mbar_wait_bounded(&empty[s], ((g / C::STAGES) - 1) & 1)) {
+          *abort_flag = 1;
+          raise_tail(kErrTailWait);
+          break;
+        }
+        if (*abort_flag) break;
+        const int j = g / nkc, kc = g - j * nkc;
+        const int tile = (static_cast<int>(blockIdx.x) + j * G) / ncol;
+        unsigned char* st = sm + s * C::STAGE;
+        mbar_expect_tx(&full[s], C::ACT + C::HEAD);
+        bulk_g2s_plain(st, a.act + (static_cast<size_t>(kc) * ncol + ct) * actb, C::ACT, &full[s]);
+        bulk_g2s_plain(st + C::ACT, h.tiles + (static_cast<size_t>(tile) * nkc + kc) * C::HEAD, C::HEAD, &full[s]);
+        ++issued;
+      }
+      // no copy may still be in flight when the CTA's shared memory goes away
+      for (int g = issued > C::STAGES ? issued - C::STAGES : 0; g < issued; ++g)
+        (void)mbar_wait_bounded(&full[g % C::STAGES], (g / C::STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // kind::i8: D s32, A and B signed int8, both K-major, N >> 3 at bit 17, M (128) >> 4 at bit 24
+      const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) | (8u << 24);
+      int gb = 0;
+      for (int g = 0; g < total && !*abort_flag; ++g) {
+        const int s = g % C::STAGES;
+        if (!mbar_wait_bounded(&full[s], (g / C::STAGES) & 1)) {
+          *abort_flag = 1;
+          raise_tail(kErrTailWait);
+          break;
+        }
+        tc_fence_after();
+        const unsigned char* st = sm + s * C::STAGE;
+        bool ok = true;
+        for (int bi = 0; bi < 4; ++bi, ++gb) {
+          const int ab = gb % C::NBUF;
+          if (!mbar_wait_bounded(&acce[ab], ((gb / C::NBUF) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          tc_mma_i8(tmem + static_cast<uint32_t>(ab * N), tc_desc(st + C::ACT + 32 * bi), tc_desc(st + 32 * bi), idesc,
+                    0u);  // D = the block's sums alone
+          tc_commit(&accf[ab]);
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          raise_tail(kErrTailWait);
+          break;
+        }
+        tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+      }
+    }
+  } else {
+    const float2 neg = make_float2(-kMagic, -kMagic);
+    const int row = 32 * q + lane;  // vocab row within the tile
+    int g = 0, gb = 0;
+    for (int j = 0; j < mine && !*abort_flag; ++j) {
+      const int tile = (static_cast<int>(blockIdx.x) + j * G) / ncol;
+      float2 acc[C::CPT / 2];
+#pragma unroll
+      for (int i = 0; i < C::CPT / 2; ++i) acc[i] = make_float2(0.0f, 0.0f);
+      bool ok = true;
+      for (int kc = 0; kc < nkc && ok; ++kc, ++g) {
+        const int s = g % C::STAGES;
+        if (!mbar_wait_bounded(&full[s], (g / C::STAGES) & 1)) {
+          ok = false;
+          break;
+        }
+        // this row's four fp16 block scales of the chunk, then the stage may go
+        const uint2 wr = *reinterpret_cast<const uint2*>(sm + s * C::STAGE + C::ACT + TileBytes<false>::A + row * 8);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll 1
+        for (int bi = 0; bi < 4; ++bi, ++gb) {
+          const int ab = gb % C::NBUF;
+          if (!mbar_wait_bounded(&accf[ab], (gb / C::NBUF) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // the block's sums out of tensor memory, the accumulator released at once
+          uint32_t d[C::CPT];
+#pragma unroll
+          for (int c = 0; c < C::CPT; c += 8) tc_ld8_nowait(tl + static_cast<uint32_t>(ab * N + c), d + c);
+          tc_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acce[ab]);
+          if (kc * 4 + bi < nb) {  // blocks past dim (zero padding) are not in the reference's sum
+            const uint32_t wword = bi < 2 ? wr.x : wr.y;
+            const float wf = __half2float(__ushort_as_half(static_cast<unsigned short>(bi & 1 ? wword >> 16 : wword)));
+            const float2 ww = make_float2(wf, wf);
+            const float* xs = XS + (kc * 4 + bi) * N + grp * C::CPT;
+#pragma unroll
+            for (int e = 0; e < C::CPT; e += 4) {
+              const float4 x4 = lds4(xs + e);
+              const float2 c01 = __fmul2_rn(ww, make_float2(x4.x, x4.y));
+              const float2 c23 = __fmul2_rn(ww, make_float2(x4.z, x4.w));
+              // float(sum) exactly: the bits of 1.5 * 2^23 + sum (|sum| < 2^22), less 1.5 * 2^23
+              const float2 f01 = __fadd2_rn(
+                  make_float2(__uint_as_float(d[e] + kMagicU), __uint_as_float(d[e + 1] + kMagicU)), neg);
+              const float2 f23 = __fadd2_rn(
+                  make_float2(__uint_as_float(d[e + 2] + kMagicU), __uint_as_float(d[e + 3] + kMagicU)), neg);
+              acc[e / 2] = __ffma2_rn(c01, f01, acc[e / 2]);
+              acc[e / 2 + 1] = __ffma2_rn(c23, f23, acc[e / 2 + 1]);
+            }
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        raise_tail(kErrTailWait);
+        break;
+      }
+      const int v = tile * kTailRows + row;
+      if (v < h.vocab) {
+#pragma unroll
+        for (int c = 0; c < C::CPT; c += 2) {
+          const int t = ct * N + grp * C::CPT + c;
+          if (t < a.n) a.logits[static_cast<long long>(t) * a.ld + v] = acc[c / 2].x;
+          if (t + 1 < a.n) a.logits[static_cast<long long>(t + 1) * a.ld + v] = acc[c / 2].y;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::COLS) : "memory");
+}
+
+template <int N>
+cudaError_t launch_head_tc(const TailHead& h, const TailArgs& a, cudaStream_t s) {
+  using C = TcCfg<N>;
+  auto kern = tail_head_tc_kernel<N>;
+  const size_t smem = C::smem(h.nkc);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  // persistent, one CTA per SM, a multiple of the token tiles so that each
+  // CTA keeps one token tile; the fewest items per CTA, then the fewest CTAs
+  const int ncol = a.n_pad / N, items = h.ntile * ncol;
+  const int slots = C::CTAS * sms / ncol * ncol;
+  const int per = (items + slots - 1) / slots;
+  const int grid = (items + per * ncol - 1) / (per * ncol) * ncol;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, h, a);
+}
+
+// Token tile of the tcgen05 path (0: the mma.sync path): Q8 heads, more than
+// 32 tokens, when the stages and the resident activation scales fit, and only
+// when VERBO_CUDA_TAIL_TCGEN05=1 selects it: measured on B200 it is slower
+// than the mma.sync kernel (each epilogue warp waits out the tensor-memory
+// load of every block before it can use it), so it is not the default.
+int tc_tokens(const TailHead& h, int n) {
+  const char* sel = std::getenv("VERBO_CUDA_TAIL_TCGEN05");
+  if (!sel || sel[0] != '1' || sel[1] != '\0') return 0;
+  if (h.dtype != kTailQ8 || n <= 32) return 0;
+  const int N = 64;
+  if ((n + N - 1) / N > 16) return 0;  // at most 16 token tiles (the grid holds a multiple of them)
+  const size_t need = N == 64 ? TcCfg<64>::smem(h.nkc) : TcCfg<128>::smem(h.nkc);
+  return need <= kTcSmemLimit ? N : 0;
+}
+
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 }  // namespace
@@ -642,6 +975,7 @@ void tail_pack_tiles(int dtype, int vocab, int dim, const void* q, const uint16_
 
 int tail_token_tile(const TailHead& h, int n) {
   if (h.dtype == kTailF32) return n <= 2 ? 2 : n <= 4 ? 4 : n <= 8 ? 8 : 16;
+  if (const int N = tc_tokens(h, n)) return N;  // every token in one tensor-core tile
   return n <= 8 ? 8 : n <= 16 ? 16 : n <= 32 ? 32 : 64;
 }
 
@@ -682,7 +1016,12 @@ cudaError_t launch_tail(const TailHead& h, const TailArgs& a, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   switch (h.dtype) {
     case kTailQ8:
-      return launch_head_q_nt<false>(h, a, s);
+      switch (tc_tokens(h, a.n)) {
+        case 64:
+          return launch_head_tc<64>(h, a, s);
+        default:
+          return launch_head_q_nt<false>(h, a, s);
+      }
     case kTailQ4:
       return launch_head_q_nt<true>(h, a, s);
     default:
