@@ -262,6 +262,41 @@ VERBO_CUDA_API void verbo_cuda_tail_free(verbo_cuda_tail* t);
 VERBO_CUDA_API int verbo_cuda_tail_logits(verbo_cuda_tail* t, const float* x, int n, long long ldx, float* logits,
                                           long long ld, void* stream);
 
+/* ---- request batching for a server -----------------------------------------
+   The reference's server (cli/serve.cpp:139-218) runs one request at a time
+   behind a global mutex (:168), each through verbo::generate with the
+   request's own Sampling (:149-157).  A verbo_cuda_server keeps up to `slots`
+   requests in flight instead, each with its own options and sampler state on
+   the device: per step, verbo_cuda_server_prepare admits queued requests
+   (Sampler(opts) seeded with opts.seed, then accept(prompt)) and returns which
+   request each row of the step belongs to; the caller's model writes each
+   active request's next logits row there; verbo_cuda_server_step samples all
+   rows (one launch chain per option set) and accepts the ids, a stop id ending
+   its request without being emitted and max_tokens the others, as generate
+   does (src/sampler.cpp:156-165).  With a penalty, 1 <= repeat_last <=
+   max_window (the device ring of the last ids).  Calls on one server are
+   serialised by it; use one CUDA stream per server. */
+typedef struct verbo_cuda_server verbo_cuda_server;
+VERBO_CUDA_API verbo_cuda_server* verbo_cuda_server_new(int slots, int vocab, int max_window, const int* stop_ids,
+                                                        int n_stop, int device);
+VERBO_CUDA_API void verbo_cuda_server_free(verbo_cuda_server* v);
+/* Queues a request (prompt ids host memory, opts->seed != 0); returns its id
+   (>= 0) or -1. */
+VERBO_CUDA_API long long verbo_cuda_server_submit(verbo_cuda_server* v, const int* prompt, int n,
+                                                  const verbo_sampling* opts, int max_tokens);
+/* Admits queued requests into free rows and fills row_req[0..slots) with the
+   request id of each row of the next step (-1: idle); returns the number of
+   active rows A (rows 0..A-1 hold them), 0 when nothing is left. */
+VERBO_CUDA_API int verbo_cuda_server_prepare(verbo_cuda_server* v, long long* row_req, void* cuda_stream);
+/* Samples the prepared step from A logits rows (row r at logits + r*ld, vocab
+   floats, host or device memory); returns how many requests finished. */
+VERBO_CUDA_API int verbo_cuda_server_step(verbo_cuda_server* v, const float* logits, long long ld, void* cuda_stream);
+/* A request's ids so far (up to cap into tokens), their count and whether it
+   ended on a stop id; returns 1 once it finished, 0 before; with release = 1
+   a finished request is forgotten. */
+VERBO_CUDA_API int verbo_cuda_server_result(verbo_cuda_server* v, long long id, int* tokens, int cap, int* n_tokens,
+                                            int* stopped, int release);
+
 /* ---- one decode step of B concurrent generations --------------------------
    The end of Session::Impl::batch (src/session.cpp:163-169) for the last row
    of each of B sessions, followed by the pick + accept of verbo::generate

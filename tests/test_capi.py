@@ -37,7 +37,7 @@ def declared_functions():
 
 def test_exports_match_header(lib):
     declared = declared_functions()
-    assert len(declared) == 32
+    assert len(declared) == 38
     out = subprocess.run(["nm", "-D", "--defined-only", str(build.LIB)], capture_output=True, text=True,
                          check=True).stdout
     exported = sorted(ln.split()[-1] for ln in out.splitlines() if ln.split()[-1].startswith("verbo_cuda_"))

@@ -1,6 +1,8 @@
-"""Request batching (verbo_b200.serving.BatchServer) against verbo::generate.
+"""Request batching (verbo_cuda_server_* through verbo_b200.serving.BatchServer)
+against verbo::generate.
 
-Seven requests share three slots.  A deterministic stand-in model gives each
+Seven requests share three slots (and, in the mixed test, nine requests with
+three option sets share four).  A deterministic stand-in model gives each
 request's t-th logits row from (request id, t), with stop ids planted so that
 some requests end early.  Each request is then replayed on the oracle as the
 reference's generate loop would run it alone (src/sampler.cpp:111-181): a
@@ -48,16 +50,49 @@ def test_batch_server_matches_one_generate_per_request(cuda_lib, opts):
     from verbo_b200.serving import BatchServer
 
     g = np.random.default_rng(31)
-    srv = BatchServer(vb.Sampling(**opts), slots=3, vocab=V, model=stand_in_model)
+    srv = BatchServer(vb.Sampling(**opts), slots=3, vocab=V, model=stand_in_model, stop_ids=STOP)
     reqs = []
     for i in range(7):
         prompt = g.integers(0, V, size=int(g.integers(0, 80))).tolist()
-        reqs.append((srv.submit(prompt, max_tokens=int(g.integers(3, 10)), seed=1000 + i, stop_ids=STOP), prompt))
+        reqs.append((srv.submit(prompt, max_tokens=int(g.integers(3, 10)), seed=1000 + i), prompt))
     done = srv.run()
     assert sorted(done) == [rid for rid, _ in reqs]
-    o = po.sampling(**opts)
+    assert replay(done, [(rid, prompt, opts) for rid, prompt in reqs]) >= 1  # the planted stops were met
+
+
+MIXED = [dict(temp=0.0, repeat=1.3, repeat_last=32),
+         dict(temp=0.8, top_k=40, top_p=0.9, min_p=0.02, repeat=1.15, repeat_last=48),
+         dict(temp=1.0, top_k=0, top_p=0.95, repeat=1.0)]
+
+
+def test_batch_server_mixed_options(cuda_lib):
+    """Requests with different options in flight together: each is sampled
+    with its own (one launch chain per option set over contiguous rows, the
+    rows re-packed as requests come and go) and matches its own generate."""
+    if not torch.cuda.is_available():
+        pytest.fail("gpu tests need a CUDA device")
+    import verbo_b200 as vb
+    from verbo_b200.serving import BatchServer
+
+    g = np.random.default_rng(77)
+    srv = BatchServer(vb.Sampling(), slots=4, vocab=V, model=stand_in_model, stop_ids=STOP)
+    reqs = []
+    for i in range(9):
+        opts = MIXED[i % 3]
+        prompt = g.integers(0, V, size=int(g.integers(0, 60))).tolist()
+        rid = srv.submit(prompt, max_tokens=int(g.integers(2, 9)), seed=500 + i, opts=vb.Sampling(**opts))
+        reqs.append((rid, prompt, opts))
+    done = srv.run()
+    assert sorted(done) == [rid for rid, _, _ in reqs]
+    replay(done, reqs)
+
+
+def replay(done, reqs):
+    """Each request on the oracle as generate would run it alone; returns how
+    many ended on a stop id."""
     stopped = 0
-    for rid, prompt in reqs:
+    for rid, prompt, opts in reqs:
+        o = po.sampling(**opts)
         r = done[rid]
         st = po.seed_states(np.array([r.seed], dtype=np.uint64))
         hist = list(prompt)
@@ -77,4 +112,4 @@ def test_batch_server_matches_one_generate_per_request(cuda_lib, opts):
         else:
             assert len(r.tokens) == r.max_tokens, (rid, len(r.tokens))
         stopped += r.stopped
-    assert stopped >= 1  # the planted stops were met
+    return stopped

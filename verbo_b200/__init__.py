@@ -29,7 +29,7 @@ from pathlib import Path
 from typing import Optional, Sequence
 
 __all__ = ["Sampling", "Sampler", "VerboCudaError", "load_library", "sample", "sample_noalloc", "full_vocab_fallbacks", "shard_topk", "merge_sample",
-           "seed_states", "check", "version", "ROW_STATS_FIELDS", "Batch", "Tail", "Comm"]
+           "seed_states", "check", "version", "ROW_STATS_FIELDS", "Batch", "Server", "Tail", "Comm"]
 __version__ = "0.1.0"
 
 _HERE = Path(__file__).resolve().parent
@@ -126,6 +126,12 @@ def load_library():
         "verbo_cuda_comm_wait": (ctypes.c_int, [_P, _P, ctypes.c_int]),
         "verbo_cuda_comm_mark_next": (ctypes.c_int, [_P, _P, _P]),
         "verbo_cuda_batch_decode": (ctypes.c_int, [_P, _P, _P, ctypes.c_longlong, _P, _P, _P]),
+        "verbo_cuda_server_new": (_P, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int]),
+        "verbo_cuda_server_free": (None, [_P]),
+        "verbo_cuda_server_submit": (ctypes.c_longlong, [_P, _P, ctypes.c_int, _P, ctypes.c_int]),
+        "verbo_cuda_server_prepare": (ctypes.c_int, [_P, _P, _P]),
+        "verbo_cuda_server_step": (ctypes.c_int, [_P, _P, ctypes.c_longlong, _P]),
+        "verbo_cuda_server_result": (ctypes.c_int, [_P, ctypes.c_longlong, _P, ctypes.c_int, _P, _P, ctypes.c_int]),
         "verbo_cuda_sharded_sample": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_longlong,
                                                      ctypes.c_int, ctypes.c_int, _P, _P, ctypes.POINTER(_Sampling),
                                                      ctypes.c_int, _P, _P, _P, _P]),
@@ -419,6 +425,88 @@ class Batch:
                                               _stream(cuda_stream)))
         return out
 
+
+
+class Server:
+    """Request batching with per-request options (verbo_cuda_server_*): up to
+    `slots` requests in flight, each with its own Sampling (seed included) and
+    sampler state on the device.  Per step: ``prepare()`` returns the request
+    id of each row (-1 idle) and the active row count A; the caller writes each
+    active request's next logits row into row r of a [>= A, vocab] float32
+    array (CUDA tensor or numpy); ``step(logits)`` samples and accepts; a stop
+    id or max_tokens finishes a request; ``result(id)`` reads it."""
+
+    def __init__(self, slots: int, vocab: int, max_window: int = 256, stop_ids=(), device: int = 0):
+        import numpy as np
+
+        self._lib = load_library()
+        st = np.ascontiguousarray(list(stop_ids), dtype=np.int32)
+        h = self._lib.verbo_cuda_server_new(int(slots), int(vocab), int(max_window),
+                                            st.ctypes.data if st.size else None, int(st.size), int(device))
+        if not h:
+            raise _err()
+        self._h, self.slots, self.vocab = h, int(slots), int(vocab)
+        self._rows = np.full(self.slots, -1, dtype=np.int64)
+
+    def submit(self, prompt, opts: Sampling, max_tokens: int) -> int:
+        import numpy as np
+
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        c = opts._c()
+        rid = self._lib.verbo_cuda_server_submit(self._h, p.ctypes.data if p.size else None, int(p.size),
+                                                 ctypes.byref(c), int(max_tokens))
+        if rid < 0:
+            raise _err()
+        return int(rid)
+
+    def prepare(self, cuda_stream=None):
+        """(row -> request id array, active rows A)."""
+        n = self._lib.verbo_cuda_server_prepare(self._h, self._rows.ctypes.data, _stream(cuda_stream))
+        if n < 0:
+            raise _err()
+        return self._rows.copy(), int(n)
+
+    def step(self, logits, cuda_stream=None) -> int:
+        import numpy as np
+
+        if isinstance(logits, np.ndarray):
+            arr = np.ascontiguousarray(logits, dtype=np.float32)
+            ptr, ld = arr.ctypes.data, arr.shape[1]
+        else:
+            if logits.dtype.itemsize != 4 or (logits.shape[1] > 1 and logits.stride(1) != 1):
+                raise VerboCudaError("logits rows must be contiguous float32")
+            ptr, ld = logits.data_ptr(), logits.stride(0)
+        n = self._lib.verbo_cuda_server_step(self._h, ptr, int(ld), _stream(cuda_stream))
+        if n < 0:
+            raise _err()
+        return int(n)
+
+    def result(self, rid: int, release: bool = False):
+        """(finished, ids, stopped)."""
+        import numpy as np
+
+        n = ctypes.c_int(0)
+        stopped = ctypes.c_int(0)
+        rc = self._lib.verbo_cuda_server_result(self._h, int(rid), None, 0, ctypes.byref(n), ctypes.byref(stopped), 0)
+        if rc < 0:
+            raise _err()
+        ids = np.zeros(max(n.value, 1), dtype=np.int32)
+        rc = self._lib.verbo_cuda_server_result(self._h, int(rid), ids.ctypes.data, int(ids.size), ctypes.byref(n),
+                                                ctypes.byref(stopped), 1 if release else 0)
+        if rc < 0:
+            raise _err()
+        return bool(rc), ids[:n.value].tolist(), bool(stopped.value)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.verbo_cuda_server_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 UNIQUE_ID_BYTES = 128

@@ -12,6 +12,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <deque>
 #include <map>
 #include <mutex>
 #include <stdexcept>
@@ -1200,6 +1201,339 @@ VERBO_CUDA_API int verbo_cuda_comm_mark_next(verbo_cuda_comm* c, void* after_sha
         c->mark_shard = static_cast<cudaEvent_t>(after_shard);
         c->mark_gather = static_cast<cudaEvent_t>(after_gather);
         return 0;
+      },
+      -1);
+}
+
+}  // extern "C"
+
+// ============================================ request batching (server) ===
+// Continuous batching of generation requests, each with its own sampling
+// options (the reference's server maps every request's JSON options to a
+// Sampling, cli/serve.cpp:149-157, and runs one request at a time behind a
+// mutex, :168).  Active requests occupy rows 0..A-1 of a step, grouped by
+// option set so that each group is a contiguous run of rows that one
+// launch chain samples; the per-request sampler state (RNG, penalty ring)
+// lives in device rows that move with the request (state_gather) when the
+// rows are re-packed.
+namespace {
+
+struct ServerReq {
+  long long id = 0;
+  std::vector<int> prompt;
+  verbo_sampling opts{};
+  int max_tokens = 0;
+  std::vector<int> tokens;
+  bool stopped = false;
+  bool finished = false;
+  bool released = false;  // collected by the caller; freed once no step row lists it
+};
+
+bool same_opts(const verbo_sampling& a, const verbo_sampling& b) {
+  return std::memcmp(&a.temp, &b.temp, sizeof(float)) == 0 && a.top_k == b.top_k &&
+         std::memcmp(&a.top_p, &b.top_p, sizeof(float)) == 0 && std::memcmp(&a.min_p, &b.min_p, sizeof(float)) == 0 &&
+         std::memcmp(&a.repeat, &b.repeat, sizeof(float)) == 0 && a.repeat_last == b.repeat_last;
+}
+
+}  // namespace
+
+struct verbo_cuda_server {
+  int device = 0, slots = 0, vocab = 0, win_w = 0;
+  std::vector<int> stop;                       // the model's stop ids (Model::is_stop)
+  std::deque<ServerReq*> queue;
+  std::vector<ServerReq*> rows;                // row -> request of the prepared step (size A)
+  std::map<long long, ServerReq*> all;         // every request not yet collected
+  long long next_id = 0;
+  bool prepared = false;
+  // device state, double-buffered for re-packing
+  unsigned long long* rng[2] = {nullptr, nullptr};
+  int* win[2] = {nullptr, nullptr};
+  long long* pos[2] = {nullptr, nullptr};
+  int cur = 0;
+  long long* off = nullptr;   // CSR view of the rings: row r at r * win_w
+  int* from = nullptr;        // re-packing map (device)
+  int* stage = nullptr;       // prompt ids on their way to a ring (device, win_w ints)
+  int* ids = nullptr;         // the step's picks (device)
+  float* host_rows = nullptr; // device copy of host logits rows
+  long long host_rows_cap = 0;
+  std::mutex mu;
+};
+
+namespace {
+
+void server_release(verbo_cuda_server* v) {
+  if (!v) return;
+  cudaSetDevice(v->device);
+  cudaDeviceSynchronize();
+  for (int i = 0; i < 2; ++i) {
+    cudaFree(v->rng[i]);
+    cudaFree(v->win[i]);
+    cudaFree(v->pos[i]);
+  }
+  cudaFree(v->off);
+  cudaFree(v->from);
+  cudaFree(v->stage);
+  cudaFree(v->ids);
+  cudaFree(v->host_rows);
+  for (ServerReq* r : v->rows)
+    if (r->released) delete r;
+  for (auto& kv : v->all) delete kv.second;
+  delete v;
+}
+
+}  // namespace
+
+extern "C" {
+
+VERBO_CUDA_API verbo_cuda_server* verbo_cuda_server_new(int slots, int vocab, int max_window, const int* stop_ids,
+                                                        int n_stop, int device) {
+  return guard(
+      [&]() -> verbo_cuda_server* {
+        if (slots < 1 || slots > (1 << 16)) fail("slots must be in [1, 65536]");
+        if (vocab < 1 || vocab > vb::kMaxVocab) fail("vocab must be in [1, " + std::to_string(vb::kMaxVocab) + "]");
+        if (max_window < 1 || max_window > vb::kWinMax)
+          fail("max_window must be in [1, " + std::to_string(vb::kWinMax) + "]");
+        if (n_stop < 0 || (n_stop > 0 && !stop_ids)) fail("stop ids: n_stop >= 0 and a pointer when n_stop > 0");
+        int n = 0;
+        cuda_ok(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+        if (device < 0 || device >= n) fail("no CUDA device " + std::to_string(device));
+        cuda_ok(cudaSetDevice(device), "cudaSetDevice");
+        auto* v = new verbo_cuda_server();
+        v->device = device;
+        v->slots = slots;
+        v->vocab = vocab;
+        v->win_w = (max_window + 3) & ~3;
+        v->stop.assign(stop_ids, stop_ids + n_stop);
+        try {
+          for (int i = 0; i < 2; ++i) {
+            cuda_ok(cudaMalloc(&v->rng[i], 16ull * slots), "cudaMalloc rng");
+            cuda_ok(cudaMalloc(&v->win[i], 4ull * v->win_w * slots), "cudaMalloc rings");
+            cuda_ok(cudaMalloc(&v->pos[i], 8ull * slots), "cudaMalloc ring positions");
+          }
+          cuda_ok(cudaMalloc(&v->off, 8ull * (slots + 1)), "cudaMalloc offsets");
+          cuda_ok(cudaMalloc(&v->from, 4ull * slots), "cudaMalloc map");
+          cuda_ok(cudaMalloc(&v->stage, 4ull * v->win_w), "cudaMalloc staging");
+          cuda_ok(cudaMalloc(&v->ids, 4ull * slots), "cudaMalloc ids");
+          std::vector<long long> off(static_cast<size_t>(slots) + 1);
+          for (int i = 0; i <= slots; ++i) off[i] = static_cast<long long>(i) * v->win_w;
+          cuda_ok(cudaMemcpy(v->off, off.data(), off.size() * 8, cudaMemcpyHostToDevice), "upload offsets");
+        } catch (...) {
+          server_release(v);
+          throw;
+        }
+        return v;
+      },
+      static_cast<verbo_cuda_server*>(nullptr));
+}
+
+VERBO_CUDA_API void verbo_cuda_server_free(verbo_cuda_server* v) { server_release(v); }
+
+VERBO_CUDA_API long long verbo_cuda_server_submit(verbo_cuda_server* v, const int* prompt, int n,
+                                                  const verbo_sampling* opts, int max_tokens) {
+  return guard(
+      [&]() -> long long {
+        if (!v || !opts) fail("server and opts must not be NULL");
+        if (n < 0 || (n > 0 && !prompt)) fail("prompt: n >= 0 and a pointer when n > 0");
+        if (max_tokens < 0) fail("max_tokens must be >= 0");
+        if (opts->seed == 0) fail("seed 0 takes the clock in the reference; give each request its own seed");
+        if (std::isnan(opts->temp) || opts->temp == INFINITY) fail("temp must not be NaN or +inf");
+        if (opts->repeat != 1.0f && (opts->repeat_last < 1 || opts->repeat_last > v->win_w))
+          fail("a repetition penalty needs 1 <= repeat_last <= the server's window (" + std::to_string(v->win_w) + ")");
+        for (int i = 0; i < n; ++i)
+          if (prompt[i] < 0 || prompt[i] >= v->vocab) fail("prompt ids must be in [0, vocab)");
+        std::lock_guard<std::mutex> lk(v->mu);
+        auto* r = new ServerReq();
+        r->id = v->next_id++;
+        r->prompt.assign(prompt, prompt + n);
+        r->opts = *opts;
+        r->max_tokens = max_tokens;
+        v->all[r->id] = r;
+        if (max_tokens == 0)
+          r->finished = true;
+        else
+          v->queue.push_back(r);
+        return r->id;
+      },
+      -1ll);
+}
+
+// Admits queued requests into free rows, re-packs the rows by option set and
+// returns the step's row -> request map (row_req[0..slots), -1 for idle
+// rows).  Returns the number of active rows A (rows 0..A-1), 0 when idle.
+VERBO_CUDA_API int verbo_cuda_server_prepare(verbo_cuda_server* v, long long* row_req, void* cuda_stream) {
+  return guard(
+      [&]() {
+        if (!v || !row_req) fail("server and row_req must not be NULL");
+        std::lock_guard<std::mutex> lk(v->mu);
+        cuda_ok(cudaSetDevice(v->device), "cudaSetDevice");
+        const cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+        // rows of the last step keep their state; new requests go to the rows after them
+        std::vector<std::pair<ServerReq*, int>> live;  // request, its state row now
+        for (int r = 0; r < static_cast<int>(v->rows.size()); ++r)
+          if (!v->rows[r]->finished) live.emplace_back(v->rows[r], r);
+        // free state rows: those not held by a live request
+        std::vector<char> held(static_cast<size_t>(v->slots), 0);
+        for (auto& p : live) held[p.second] = 1;
+        std::vector<int> free_rows;
+        for (int r = 0; r < v->slots; ++r)
+          if (!held[r]) free_rows.push_back(r);
+        size_t fi = 0;
+        while (!v->queue.empty() && fi < free_rows.size()) {
+          ServerReq* q = v->queue.front();
+          v->queue.pop_front();
+          const int r = free_rows[fi++];
+          // Sampler(opts) with the request's seed, then accept(prompt): only
+          // the last repeat_last ids can reach the window (src/sampler.cpp:26-48)
+          unsigned long long st[2];
+          seed_state(q->opts.seed, st);
+          int* w = v->win[v->cur] + static_cast<long long>(r) * v->win_w;
+          cuda_ok(cudaMemcpyAsync(v->rng[v->cur] + 2ll * r, st, sizeof(st), cudaMemcpyHostToDevice, s), "upload rng");
+          cuda_ok(cudaMemsetAsync(w, 0xff, 4ull * v->win_w, s), "clear ring");
+          cuda_ok(cudaMemsetAsync(v->pos[v->cur] + r, 0, 8, s), "clear ring position");
+          if (q->opts.repeat != 1.0f && !q->prompt.empty()) {
+            const int len = q->opts.repeat_last;
+            const int np = static_cast<int>(q->prompt.size());
+            const int skip = np > len ? np - len : 0;
+            cuda_ok(cudaMemcpyAsync(v->stage, q->prompt.data() + skip, 4ull * (np - skip), cudaMemcpyHostToDevice, s),
+                    "upload prompt");
+            cuda_ok(vb::launch_ring_accept(v->win[v->cur], v->win_w, len, v->pos[v->cur], r, v->stage, np - skip, skip, s),
+                    "kernel launch");
+            cuda_ok(cudaStreamSynchronize(s), "stream");  // the staging buffer is reused by the next admission
+          }
+          live.emplace_back(q, r);
+        }
+        // group by option set (first appearance order), stable within a group
+        std::vector<std::pair<ServerReq*, int>> order;
+        std::vector<char> taken(live.size(), 0);
+        for (size_t i = 0; i < live.size(); ++i) {
+          if (taken[i]) continue;
+          for (size_t j = i; j < live.size(); ++j)
+            if (!taken[j] && same_opts(live[i].first->opts, live[j].first->opts)) {
+              order.push_back(live[j]);
+              taken[j] = 1;
+            }
+        }
+        for (ServerReq* q : v->rows)
+          if (q->released) delete q;  // collected while its row was still listed
+        v->rows.clear();
+        bool identity = true;
+        std::vector<int> from(order.size());
+        for (size_t r = 0; r < order.size(); ++r) {
+          v->rows.push_back(order[r].first);
+          from[r] = order[r].second;
+          identity = identity && from[r] == static_cast<int>(r);
+        }
+        if (!identity) {  // move the states to their new rows
+          const int nxt = v->cur ^ 1;
+          cuda_ok(cudaMemcpyAsync(v->from, from.data(), 4ull * from.size(), cudaMemcpyHostToDevice, s), "upload map");
+          cuda_ok(vb::launch_state_gather(v->from, static_cast<int>(from.size()), v->rng[v->cur], v->rng[nxt],
+                                          v->win[v->cur], v->win[nxt], v->win_w, v->pos[v->cur], v->pos[nxt], s),
+                  "kernel launch");
+          cuda_ok(cudaStreamSynchronize(s), "stream");  // the map buffer is reused by the next re-packing
+          v->cur = nxt;
+        }
+        for (int r = 0; r < v->slots; ++r)
+          row_req[r] = r < static_cast<int>(v->rows.size()) ? v->rows[r]->id : -1;
+        v->prepared = true;
+        return static_cast<int>(v->rows.size());
+      },
+      -1);
+}
+
+// Samples the prepared step: `logits` holds the A active rows (row r at
+// logits + r*ld, host or device memory), each sampled with its request's
+// options; every request takes its id (a stop id ends it without being
+// emitted, as in verbo::generate, src/sampler.cpp:156-165) and the requests
+// that stop or reach max_tokens finish.  Returns the number that finished.
+VERBO_CUDA_API int verbo_cuda_server_step(verbo_cuda_server* v, const float* logits, long long ld, void* cuda_stream) {
+  return guard(
+      [&]() {
+        if (!v) fail("server is NULL");
+        std::lock_guard<std::mutex> lk(v->mu);
+        if (!v->prepared) fail("call verbo_cuda_server_prepare before each step");
+        v->prepared = false;
+        const int A = static_cast<int>(v->rows.size());
+        if (A == 0) return 0;
+        if (!logits) fail("logits must not be NULL");
+        if (ld < v->vocab) fail("ld must be >= vocab");
+        cuda_ok(cudaSetDevice(v->device), "cudaSetDevice");
+        const cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+        const float* rows = logits;
+        long long lr = ld;
+        if (!on_device(logits)) {
+          grow(v->host_rows, v->host_rows_cap, static_cast<long long>(A) * v->vocab, s, "cudaMalloc logits rows");
+          cuda_ok(cudaMemcpy2DAsync(v->host_rows, 4ull * v->vocab, logits, 4ull * ld, 4ull * v->vocab, A,
+                                    cudaMemcpyHostToDevice, s),
+                  "upload logits rows");
+          rows = v->host_rows;
+          lr = v->vocab;
+        }
+        // one launch chain per run of rows with the same options
+        for (int r0 = 0; r0 < A;) {
+          int r1 = r0 + 1;
+          while (r1 < A && same_opts(v->rows[r0]->opts, v->rows[r1]->opts)) ++r1;
+          const verbo_sampling& so = v->rows[r0]->opts;
+          const bool pen = so.repeat != 1.0f;
+          vb::DevOpts o = make_opts(so, v->vocab, pen);
+          if (pen) o.repeat_last = v->win_w;  // the CSR view reads whole rings; -1 slots mark nothing
+          int* ring = v->win[v->cur] + static_cast<long long>(r0) * v->win_w;
+          vb::RowArgs a = row_args(rows + static_cast<long long>(r0) * lr, r1 - r0, v->vocab, lr, 0, v->vocab,
+                                   pen ? ring : nullptr, pen ? v->off : nullptr);
+          a.rng = v->rng[v->cur] + 2ll * r0;
+          a.out_ids = v->ids + r0;
+          if (pen) {
+            a.ring_pos = v->pos[v->cur] + r0;
+            a.ring_len = so.repeat_last;
+          }
+          dispatch_rows(a, o, v->vocab, s, pen ? ring : nullptr, v->win_w);
+          r0 = r1;
+        }
+        std::vector<int> got(static_cast<size_t>(A));
+        cuda_ok(cudaMemcpyAsync(got.data(), v->ids, 4ull * A, cudaMemcpyDeviceToHost, s), "download ids");
+        cuda_ok(cudaStreamSynchronize(s), "stream");
+        int finished = 0;
+        for (int r = 0; r < A; ++r) {
+          ServerReq* q = v->rows[r];
+          const int id = got[static_cast<size_t>(r)];
+          if (std::find(v->stop.begin(), v->stop.end(), id) != v->stop.end())
+            q->stopped = true;
+          else
+            q->tokens.push_back(id);
+          if (q->stopped || static_cast<int>(q->tokens.size()) >= q->max_tokens) {
+            q->finished = true;
+            ++finished;
+          }
+        }
+        return finished;
+      },
+      -1);
+}
+
+// A request's state: 1 finished, 0 still running or queued, -1 unknown id.
+// Fills n_tokens, stopped and up to cap of its ids; a finished request is
+// forgotten once collected with release = 1.
+VERBO_CUDA_API int verbo_cuda_server_result(verbo_cuda_server* v, long long id, int* tokens, int cap, int* n_tokens,
+                                            int* stopped, int release) {
+  return guard(
+      [&]() {
+        if (!v) fail("server is NULL");
+        std::lock_guard<std::mutex> lk(v->mu);
+        auto it = v->all.find(id);
+        if (it == v->all.end()) fail("unknown request id " + std::to_string(id));
+        ServerReq* q = it->second;
+        const int n = static_cast<int>(q->tokens.size());
+        if (n_tokens) *n_tokens = n;
+        if (stopped) *stopped = q->stopped ? 1 : 0;
+        if (tokens && cap > 0) std::memcpy(tokens, q->tokens.data(), 4ull * std::min(n, cap));
+        const int done = q->finished ? 1 : 0;
+        if (done && release) {
+          v->all.erase(it);
+          if (std::find(v->rows.begin(), v->rows.end(), q) != v->rows.end())
+            q->released = true;  // the next prepare frees it
+          else
+            delete q;
+        }
+        return done;
       },
       -1);
 }

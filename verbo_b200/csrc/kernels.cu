@@ -2197,6 +2197,32 @@ cudaError_t launch_ring_accept(int* win, int win_w, int ring_len, long long* pos
   return cudaGetLastError();
 }
 
+// Per-row sampler state moved to new rows: row r of the output takes row
+// from[r] of the input (RNG state, penalty ring and its position).  One CTA
+// per output row.
+__global__ void __launch_bounds__(256) state_gather_kernel(const int* from, int n, const unsigned long long* rng_in,
+                                                           unsigned long long* rng_out, const int* win_in, int* win_out,
+                                                           int win_w, const long long* pos_in, long long* pos_out) {
+  const int r = blockIdx.x;
+  if (r >= n) return;
+  const int f = from[r];
+  const int* src = win_in + static_cast<long long>(f) * win_w;
+  int* dst = win_out + static_cast<long long>(r) * win_w;
+  for (int i = threadIdx.x; i < win_w; i += 256) dst[i] = src[i];
+  if (threadIdx.x == 0) {
+    rng_out[2ll * r] = rng_in[2ll * f];
+    rng_out[2ll * r + 1] = rng_in[2ll * f + 1];
+    pos_out[r] = pos_in[f];
+  }
+}
+cudaError_t launch_state_gather(const int* from, int n, const unsigned long long* rng_in, unsigned long long* rng_out,
+                                const int* win_in, int* win_out, int win_w, const long long* pos_in,
+                                long long* pos_out, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  state_gather_kernel<<<n, 256, 0, s>>>(from, n, rng_in, rng_out, win_in, win_out, win_w, pos_in, pos_out);
+  return cudaGetLastError();
+}
+
 namespace split {
 // Copies each row's penalty window (its last repeat_last history ids,
 // src/sampler.cpp:58-64) into win[row][0, win_w), padded with -1.

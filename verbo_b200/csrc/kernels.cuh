@@ -65,6 +65,11 @@ struct RowArgs {
 // last n = ids[0, n) (n <= ring_len): one CTA.
 cudaError_t launch_ring_accept(int* win, int win_w, int ring_len, long long* pos, int row, const int* ids, int n,
                                int skip, cudaStream_t s);
+// Row r of the output state takes row from[r] of the input: the RNG state
+// (2 words), the penalty ring (win_w ids) and its position.
+cudaError_t launch_state_gather(const int* from, int n, const unsigned long long* rng_in, unsigned long long* rng_out,
+                                const int* win_in, int* win_out, int win_w, const long long* pos_in,
+                                long long* pos_out, cudaStream_t s);
 
 // Split-row kernels: one CTA of kSplitThreads per (row, slice of <= kSplitSlice
 // columns) publishes a partial result; a per-row merge kernel follows on the

@@ -1,19 +1,20 @@
-"""Request batching over the device-resident streams (verbo_cuda_batch_*).
+"""Request batching for a server, over the library's verbo_cuda_server_*.
 
 The reference's server (cli/serve.cpp:139-218) runs one request at a time
-behind a global mutex, each through verbo::generate (src/sampler.cpp:111-181):
-accept the prompt, then pick / stop check / accept until a stop id or
-max_tokens.  ``BatchServer`` keeps up to ``slots`` requests in one
-``verbo_b200.Batch`` instead: a request takes a free slot (reset with its seed,
-accept its prompt), every step samples all slots in one launch chain from the
-rows the caller's model produced, and a request leaves its slot when it meets
-a stop id (not emitted, as in generate) or its token limit, letting the next
-queued request in.  Only the ids cross to the host each step; stop checks stay
-on the host as in generate.  Idle slots are sampled too (their ids ignored).
+behind a global mutex (:168), each through verbo::generate
+(src/sampler.cpp:111-181) with the request's own Sampling (:149-157): accept
+the prompt, then pick / stop check / accept until a stop id or max_tokens.
+``BatchServer`` keeps up to ``slots`` requests in flight in one
+``verbo_b200.Server`` instead: a request takes a free row (its Sampler seeded
+with its seed, its prompt accepted), every step samples all rows from the
+logits rows the caller's model produced, one launch chain per option set, and
+a request leaves when it meets a stop id (not emitted, as in generate) or its
+token limit, letting the next queued request in.  Only the ids cross to the
+host each step; the scheduling itself is the C ABI's, so a C++ server can drive
+the same object (verbo_cuda_server_prepare / _step / _result).
 """
 from __future__ import annotations
 
-from collections import deque
 from dataclasses import dataclass, field
 from typing import Callable, Dict, List, Optional, Sequence
 
@@ -23,7 +24,7 @@ class Request:
     prompt: List[int]
     max_tokens: int
     seed: int
-    stop_ids: Sequence[int] = ()
+    opts: object = None
     rid: int = -1
     tokens: List[int] = field(default_factory=list)
     stopped: bool = False  # ended on a stop id (else on max_tokens)
@@ -32,61 +33,52 @@ class Request:
 class BatchServer:
     """Continuous batching of generation requests on one GPU.
 
-    ``model(slot_requests, out)`` fills ``out`` (CUDA float32 [slots, vocab])
-    with the next logits row of each slot's request (``None`` for an idle slot,
-    whose row may hold anything finite)."""
+    ``model(row_requests, out)`` fills ``out`` (CUDA float32 [slots, vocab])
+    with the next logits row of each row's request (``None`` for an idle row,
+    whose row may hold anything finite).  ``opts`` is the default Sampling; a
+    request may bring its own.  ``stop_ids`` is the model's stop set."""
 
-    def __init__(self, opts, slots: int, vocab: int, model: Callable, device: int = 0):
+    def __init__(self, opts, slots: int, vocab: int, model: Callable, device: int = 0, stop_ids: Sequence[int] = (),
+                 max_window: int = 256):
         import torch
 
         import verbo_b200 as vb
 
-        self.vocab, self.slots, self.model = vocab, slots, model
-        self.batch = vb.Batch(opts, slots, device)
+        self.opts, self.vocab, self.slots, self.model = opts, vocab, slots, model
+        self.server = vb.Server(slots, vocab, max_window=max_window, stop_ids=stop_ids, device=device)
         self.logits = torch.zeros((slots, vocab), dtype=torch.float32, device=f"cuda:{device}")
-        self.ids = torch.empty(slots, dtype=torch.int32, device=f"cuda:{device}")
-        self.active: List[Optional[Request]] = [None] * slots
-        self.queue: deque = deque()
+        self.reqs: Dict[int, Request] = {}
         self.done: Dict[int, Request] = {}
-        self._next = 0
 
-    def submit(self, prompt: Sequence[int], max_tokens: int, seed: int, stop_ids: Sequence[int] = ()) -> int:
+    def submit(self, prompt: Sequence[int], max_tokens: int, seed: int, opts=None) -> int:
+        import dataclasses
+
         if seed == 0:
             raise ValueError("seed 0 means the clock in the reference; give each request its own seed")
-        r = Request(list(prompt), int(max_tokens), int(seed), tuple(stop_ids), rid=self._next)
-        self._next += 1
+        o = dataclasses.replace(opts if opts is not None else self.opts, seed=int(seed))
+        rid = self.server.submit(list(prompt), o, int(max_tokens))
+        r = Request(list(prompt), int(max_tokens), int(seed), o, rid=rid)
         if r.max_tokens <= 0:
-            self.done[r.rid] = r
+            self.server.result(rid, release=True)
+            self.done[rid] = r
         else:
-            self.queue.append(r)
-        return r.rid
-
-    def _admit(self) -> None:
-        for s in range(self.slots):
-            if self.active[s] is None and self.queue:
-                r = self.queue.popleft()
-                self.batch.reset(s, r.seed)
-                self.batch.accept(s, r.prompt)
-                self.active[s] = r
+            self.reqs[rid] = r
+        return rid
 
     def step(self) -> bool:
-        """One sampling step over all slots; False when nothing is left to do."""
-        self._admit()
-        if not any(self.active):
+        """One sampling step over the active rows; False when nothing is left."""
+        rows, n = self.server.prepare()
+        if n == 0:
             return False
-        self.model(self.active, self.logits)
-        ids = self.batch.step(self.logits, out=self.ids).cpu().numpy()
-        for s, r in enumerate(self.active):
-            if r is None:
-                continue
-            t = int(ids[s])
-            if t in r.stop_ids:
-                r.stopped = True
-            else:
-                r.tokens.append(t)
-            if r.stopped or len(r.tokens) >= r.max_tokens:
-                self.done[r.rid] = r
-                self.active[s] = None
+        active: List[Optional[Request]] = [self.reqs[int(rid)] if rid >= 0 else None for rid in rows]
+        self.model(active, self.logits)
+        self.server.step(self.logits)
+        for r in active[:n]:
+            finished, ids, stopped = self.server.result(r.rid, release=True)
+            r.tokens = ids
+            if finished:
+                r.stopped = stopped
+                self.done[r.rid] = self.reqs.pop(r.rid)
         return True
 
     def run(self) -> Dict[int, Request]:
