@@ -348,13 +348,14 @@ def test_full_vocab_weights_match_reference_sums(temp):
         np.testing.assert_allclose(st["sum"], ost[:, -1]["sum"], rtol=rtol)
 
 
-@pytest.mark.parametrize("k", [32, 50, 64])
+@pytest.mark.parametrize("k", [32, 50, 64, 100, 128, 200, 256])
 def test_topk_concentrated_in_few_slices(k):
-    # For 32 <= k <= 64 a slice emits only its top-m (m = 24 at V = 151936)
-    # and the merge checks each slice's threshold against the k-th value
-    # found.  Rows whose k best sit in one or two slices (slices are 10240
-    # columns) fail that check for those slices, which the merge then
-    # resolves exactly; the ids must not notice.
+    # For 32 <= k <= 256 a slice emits only its top-m (m = max(16,
+    # ceil(k / 14), ceil(k / 4)) at V = 151936: 15 slices) and the merge
+    # checks each slice's threshold against the k-th value found.  Rows whose
+    # k best sit in one or two slices (slices are 10240 columns) fail that
+    # check for those slices, which the merge then resolves exactly; the ids
+    # must not notice.
     g = np.random.default_rng(k + 7)
     V, S = 151936, 10240
     x = g.standard_normal((6, V)).astype(np.float32)

@@ -1378,7 +1378,11 @@ constexpr int NT = kSplitThreads;
 constexpr int NW = NT / 32;
 constexpr int kBinsS = 2048;  // 11-bit digits of the candidate key
 constexpr int kUnionCap = 2048;  // union of a row's candidates staged in the merge kernel
-constexpr int kAugCap = 256;     // exact keys of slices whose certificate failed
+constexpr int kAugCap = 3 * kSliceCap;  // exact keys of the (at most 3) slices whose certificate failed
+// The merge's room for those keys: k <= 64 needs one slice's worth (at most 3
+// bad slices of at most 64 keys), larger k three; the smaller allocation keeps
+// the merge's occupancy for the common k.
+__host__ __device__ constexpr int aug_cap(uint32_t k) { return k <= 64u ? kSliceCap : kAugCap; }
 
 struct Shared {
   unsigned long long ws64[NW];
@@ -1643,15 +1647,16 @@ __device__ __noinline__ void mark_csr_window(const RowArgs& a, const DevOpts& o,
 }
 
 // Candidates a top-k slice must certainly hold: its whole top-kl, except in
-// rows of C >= 2 slices with 32 <= k <= 64, where the top-m with
-// m = max(kTopM, ceil(k / (C - 1))) suffices: C - 1 full slices give the
-// union at least k keys, and a slice whose threshold is above the union's
-// k-th value (it then holds m of the k best, so at most (k - 1) / m slices
-// can) is resolved exactly by the merge.
+// rows of C >= 2 slices with 32 <= k <= kSplitMaxK, where the top-m with
+// m = max(kTopM, ceil(k / (C - 1)), ceil(k / 4)) suffices: C - 1 full slices
+// give the union at least k keys, and a slice whose threshold is above the
+// union's k-th value (it then holds m of the k best, so at most
+// (k - 1) / m <= 3 slices can) is resolved exactly by the merge.
 __device__ __forceinline__ uint32_t split_top_m(uint32_t k, int C, uint32_t kl) {
-  if (C < 2 || k < 32u || k > 64u) return kl;
+  if (C < 2 || k < 32u || k > static_cast<uint32_t>(kSplitMaxK)) return kl;
   const uint32_t per = (k + static_cast<uint32_t>(C) - 2u) / static_cast<uint32_t>(C - 1);
-  return min(kl, max(static_cast<uint32_t>(kTopM), per));
+  const uint32_t quarter = (k + 3u) / 4u;
+  return min(kl, max(max(static_cast<uint32_t>(kTopM), per), quarter));
 }
 
 // The exact top-kl of a slice by radix selection, for slices whose bound
@@ -2070,7 +2075,7 @@ __global__ void __launch_bounds__(NT, 6) merge_slices_kernel(const RowArgs a, co
       const int n = max(0, min(a.ncols - lo, a.slice));
       const long long g_lo = static_cast<long long>(a.col_off) + lo;
       const uint32_t kl = min(k, static_cast<uint32_t>(n));
-      if (naug + kl > static_cast<uint32_t>(kAugCap)) {  // unreachable by the bound on bad slices
+      if (naug + kl > static_cast<uint32_t>(aug_cap(k))) {  // unreachable by the bound on bad slices
         if (threadIdx.x == 0) raise_status(kErrSelect);
         break;
       }
@@ -2306,8 +2311,9 @@ static cudaError_t launch_split_lz(const RowArgs& a0, const DevOpts& o, cudaStre
   if (e != cudaSuccess) return e;
   // the per-row merge runs after every slice of the batch (same stream)
   if (kMode == kSplitGreedy) return launch_after(split::merge_slices_kernel<kMode>, a.rows, 32, 0, s, a, o);
+  const uint32_t kk = kMode == kSplitEmit ? static_cast<uint32_t>(std::min(a.cand_k, a.ncols)) : static_cast<uint32_t>(o.k);
   return launch_after(split::merge_slices_kernel<kMode>, a.rows, split::NT,
-                      static_cast<size_t>(split::kBinsS * 4 + (split::kUnionCap + split::kAugCap) * 8), s, a, o);
+                      static_cast<size_t>(split::kBinsS * 4 + (split::kUnionCap + split::aug_cap(kk)) * 8), s, a, o);
 }
 template <int kMode, bool kPen>
 static cudaError_t launch_split_t(const RowArgs& a, const DevOpts& o, cudaStream_t s) {

@@ -80,9 +80,9 @@ constexpr int kSplitSlice = kSplitThreads * kSplitChunks * 4;     // 10240 colum
 constexpr int kSliceCap = 256;                                    // candidates a slice may publish
 constexpr int kSplitMaxK = kSliceCap;                             // largest top_k of the split top-k kernel
 constexpr int kMaxSlices = 32;
-// Top-k slices of rows with >= 2 slices and 32 <= k <= 64 emit only their
-// top-m, m = max(kTopM, ceil(k / (slices - 1))), with their threshold as a
-// certificate the merge checks (kernels.cu, merge_slices_kernel).
+// Top-k slices of rows with >= 2 slices and 32 <= k <= kSplitMaxK emit only
+// their top-m, m = max(kTopM, ceil(k / (slices - 1)), ceil(k / 4)), with their
+// threshold as a certificate the merge checks (kernels.cu, merge_slices_kernel).
 constexpr int kTopM = 16;
 
 // Dense penalty windows: when every row's window (its last repeat_last ids)
