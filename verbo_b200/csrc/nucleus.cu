@@ -295,6 +295,7 @@ struct Shared {
   int flag;
   float wsf[kW];
   unsigned wsu[kW];
+  unsigned wsc[kW];
   double wsd[kW];
   int c_lo, c_hi, d_lo, d_hi;
   unsigned nmem;
@@ -427,17 +428,17 @@ __device__ __noinline__ void run_b(int row, int s, unsigned char* smem, Shared& 
   const RowArgs& a = p.a;
   RowState* st = p.rs + row;
   const int slot = row % kChunkRows;
-  if (threadIdx.x == 0) sh.g = row_grid(st, o.temp);
-  __syncthreads();
-  const Grid g = sh.g;
   unsigned* cnt = reinterpret_cast<unsigned*>(smem);
   unsigned* esm = cnt + kCells;
-  const int nc = g.ncr + 1;
-  for (int c = threadIdx.x; c <= nc; c += NT) {  // nc: the trash cell
+  // the grid (thread 0, an L2 round trip) while every cell is cleared
+  if (threadIdx.x == 0) sh.g = row_grid(st, o.temp);
+  for (int c = threadIdx.x; c < kCells; c += NT) {
     cnt[c] = 0u;
     esm[c] = 0u;
   }
   __syncthreads();
+  const Grid g = sh.g;
+  const int nc = g.ncr + 1;  // cells 0..ncr, and nc: the trash cell (ncr <= kCells - 2)
   const int lo = s * p.slice;
   const int n = min(p.slice, a.ncols - lo);
   const float* src = a.logits + static_cast<long long>(row) * a.ld + lo;
@@ -502,14 +503,27 @@ __device__ __noinline__ void run_b(int row, int s, unsigned char* smem, Shared& 
     crowded |= v.x > kCellCap ? 1u : 0u;
     __stcg(out + c, v);
   }
-  uc = bsum(uc, sh.wsu);
-  crowded = bsum(crowded, sh.wsu);
-  const double umd = bsum(static_cast<double>(um), sh.wsd);
+  // the slice's summary in one reduction round (warp sums, then thread 0)
+  {
+    const unsigned wu = warp_sum(uc), wc = warp_sum(crowded);
+    const double wm = warp_sum(static_cast<double>(um));
+    if ((threadIdx.x & 31) == 0) {
+      sh.wsu[threadIdx.x >> 5] = wu;
+      sh.wsc[threadIdx.x >> 5] = wc;
+      sh.wsd[threadIdx.x >> 5] = wm;
+    }
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
     SliceSum v;
-    v.ucount = uc;
-    v.crowded = crowded;
-    v.umass = umd;
+    v.ucount = 0;
+    v.crowded = 0;
+    v.umass = 0.0;
+    for (int i = 0; i < kW; ++i) {
+      v.ucount += sh.wsu[i];
+      v.crowded += sh.wsc[i];
+      v.umass += sh.wsd[i];
+    }
     p.sums[static_cast<long long>(slot) * p.ns + s] = v;
     __threadfence();
     const unsigned old = atomicAdd(&st->cnt2, 1u);
