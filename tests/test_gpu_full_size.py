@@ -168,3 +168,51 @@ def test_c5_sharded_full_size():
     assert np.array_equal(ci[0].cpu().numpy(), oi) and np.array_equal(cv[0].cpu().numpy(), ov)
     ora, ost, orng = oracle_parallel(x, opts, seeds, h, off)
     judge("c5", w, ids, stats_np(st), ora, ost, from_dev_rng(rng), orng)
+
+
+# Full-size rows on the other paths: the staged cluster kernel (full
+# vocabulary with min-p and a penalty, several waves of 37 resident rows),
+# large top-k (certified top-m slices, k up to 256) and the streaming path at
+# a sharper temperature (fewer, heavier members per cell).
+EXTRA = {
+    "general_minp_penalty": ("c4", 1024, dict(temp=1.0, top_k=0, top_p=0.95, min_p=0.02, repeat=1.1), 64),
+    "topk_128": ("c3", 1024, dict(top_k=128), None),
+    "topk_256": ("c5", 512, dict(top_k=256, min_p=0.0), None),
+    "nucleus_sharp": ("c4", 2048, dict(temp=0.4, top_p=0.9), None),
+}
+
+
+@pytest.mark.parametrize("name", list(EXTRA))
+def test_other_paths_full_size(name):
+    import verbo_b200 as vb
+    from verbo_b200 import workloads as wl
+
+    cfg, rows, over, hist_len = EXTRA[name]
+    w = wl.WORKLOADS[cfg].with_rows(rows)
+    x = wl.make_rows_np(w, rows)
+    opts = w.sampling_kwargs()
+    opts.update(over)
+    if hist_len is not None:
+        g = np.random.default_rng(rows + hist_len)
+        h = g.integers(0, w.vocab, size=rows * hist_len).astype(np.int32)
+        off = np.arange(rows + 1, dtype=np.int64) * hist_len
+        opts["repeat_last"] = hist_len
+    elif opts.get("repeat", 1.0) != 1.0:
+        h, off = wl.make_hist_np(w, rows)
+    else:
+        h = off = None
+    seeds = w.sampler_seeds(0, rows)
+    dx = torch.from_numpy(x).cuda()
+    dh = None if h is None else torch.from_numpy(h).cuda()
+    do = None if off is None else torch.from_numpy(off).cuda()
+    rng = to_dev_rng(po.seed_states(seeds))
+    st = torch.zeros(rows * vb.ROW_STATS_BYTES, dtype=torch.uint8, device="cuda")
+    ids = vb.sample(dx, vb.Sampling(**opts), rng=rng, hist=dh, hist_off=do, stats=st).cpu().numpy()
+    vb.check()
+    del dx
+    ora, ost, orng = oracle_parallel(x, opts, seeds, h, off)
+    from dataclasses import replace
+
+    ws = replace(w, name=name, temp=opts["temp"], top_k=opts["top_k"], top_p=opts["top_p"], min_p=opts["min_p"],
+                 repeat=opts["repeat"], hist_len=0 if h is None else int(off[1] - off[0]), shards=1)
+    judge(name, ws, ids, stats_np(st), ora, ost, from_dev_rng(rng), orng)
