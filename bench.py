@@ -66,7 +66,7 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--config", default="c4", choices=sorted(wl.WORKLOADS) + ["tail"])
+    p.add_argument("--config", default="c4", choices=sorted(wl.WORKLOADS) + ["tail", "decode"])
     p.add_argument("--head", default="q8", choices=["q8", "q4", "f32"], help="head dtype of --config tail")
     p.add_argument("--shard-head", action="store_true",
                    help="--config tail: tensor-parallel head (vocab rows split over the ranks), each step "
@@ -796,6 +796,159 @@ def bench_reference_tail(a, tw, world: int):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------- decode step (B rows) ----
+DECODE_METRIC = "decoded rows/s of B concurrent generations: hidden rows (host) -> Q8 LM head -> pick + accept -> ids (host)"
+DECODE_OPTS = dict(temp=0.7, top_k=40, top_p=0.9, min_p=0.0, repeat=1.1, repeat_last=64)  # the reference's defaults + a penalty
+DECODE_PROMPT = 64
+
+
+def decode_config(tw, rows: int, world: int) -> dict:
+    return {"workload": (f"decode: {rows} generations x one step: {tw.dim}-dim hidden rows (N(0, {tw.scale}^2), host) "
+                         f"-> rmsnorm -> q8 LM head {tw.vocab} x {tw.dim} -> temp 0.7, top_k 40, top_p 0.9, "
+                         f"repeat 1.1 over the last 64 ids -> ids (host)"),
+            "vocab": tw.vocab, "dim": tw.dim, "rows_per_gpu": rows, "global_rows": rows * world,
+            "parallelism": f"rows x{world}", "entry": "verbo_cuda_batch_decode"}
+
+
+def cpu_decode_rate(tw, q, s, norm, x, hist, seconds: float, threads: int):
+    """The reference's decode step on the host for the same rows: its AVX2
+    tail (rmsnorm, quant_act, matmul on a Pool) and its Sampler per row
+    (history fed through accept), repeated within the time budget."""
+    from oracle import pyoracle as po
+
+    ref = po.ref_tail_available("avx2") and po.ref_available()
+    rows = x.shape[0]
+    off = np.arange(rows + 1, dtype=np.int64) * hist.shape[1]
+    seeds = np.arange(1, rows + 1, dtype=np.uint64)
+    o = po.sampling(**DECODE_OPTS)
+
+    def run():
+        if ref:
+            lg, _, _ = po.ref_logits_tail(tw.dtype, q, s, norm, tw.eps, x, build="avx2", threads=threads)
+            po.ref_sample_rows(lg, o, seeds, hist.ravel(), off, threads=threads)
+        else:
+            lg, _, _ = po.logits_tail(tw.dtype, q, s, norm, tw.eps, x)
+            po.sample_rows(lg, o, po.seed_states(seeds), hist.ravel(), off)
+
+    run()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        reps += 1
+        if time.perf_counter() - t0 > seconds or reps >= 1000:
+            break
+    dt = time.perf_counter() - t0
+    return rows * reps / dt, ("reference" if ref else "port"), (threads if ref else 1), reps
+
+
+def main_decode(a, rank: int, local_rank: int, world: int):
+    """One decode step of B generations through verbo_cuda_batch_decode: the
+    sessions' final hidden rows in host memory, the Q8 head's logits on the
+    device, the pick + accept of every generation, the ids back in host
+    memory - the whole call timed, per step."""
+    tw = wl.TAIL.with_dtype("q8")
+    B = a.rows or 64
+    q, s, norm = tw.make_head()
+    g = np.random.default_rng(11)
+    hist = g.integers(0, tw.vocab, size=(B, DECODE_PROMPT)).astype(np.int32)
+    if a.impl == "reference":
+        if rank == 0:
+            from oracle import pyoracle as po
+
+            x = tw.make_hidden_np(B)
+            per_step = min(2.0, 150.0 / (a.steps + a.warmup))
+            rate, kind, cores, reps = cpu_decode_rate(tw, q, s, norm, x, hist, per_step * a.steps, po.host_threads())
+            line = {"metric": DECODE_METRIC, "value": rate, "unit": "rows/s", "n_gpus": world, "steps": a.steps,
+                    "warmup": a.warmup, "ms_per_step": B / rate * 1000.0, "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "i8/f32", "data": "synthetic", "impl": "reference",
+                    "config": decode_config(tw, B, 1),
+                    "cpu_baseline": {"value": rate, "unit": "rows/s", "cores": cores, "kind": kind,
+                                     "sample": f"the {B} rows of one step x {reps} passes"},
+                    "e2e": {"value": rate, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import verbo_b200 as vb
+
+    vb.load_library()  # fails loudly if the CUDA library is missing
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    try:
+        tail = vb.Tail("q8", q, s, norm, tw.eps, device=local_rank)
+        batch = vb.Batch(vb.Sampling(**DECODE_OPTS), B, device=local_rank)
+        for i in range(B):
+            batch.reset(i, 1 + i + rank * B)
+            batch.accept(i, hist[i])
+        copies = 4
+        xs = [torch.from_numpy(tw.make_hidden_np(B, seed_offset=rank * 16 + c)).pin_memory() for c in range(copies)]
+        ids = np.empty(B, dtype=np.int32)
+        stream = torch.cuda.current_stream()
+        for i in range(a.warmup):
+            batch.decode(tail, xs[i % copies], out=ids, cuda_stream=stream)
+        vb.check(stream)
+        clocks = Clocks(torch.cuda.current_device()) if rank == 0 else None
+        if clocks:
+            clocks.start()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(a.steps):
+            batch.decode(tail, xs[i % copies], out=ids, cuda_stream=stream)  # host ids: the call waits for them
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        if clocks:
+            clocks.stop()
+        vb.check(stream)
+        red = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(red, op=dist.ReduceOp.MAX)
+        elapsed = float(red.item())
+        tail.close()
+        batch.close()
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    if rank != 0:
+        return
+    from oracle import pyoracle as po
+
+    peak, peak_kind = measured_peak()
+    value = B * world * a.steps / (elapsed / 1000.0)
+    ms = elapsed / a.steps
+    # per step: the head once, the hidden rows in, the logits written by the tail and read by the pick
+    alg = tw.head_bytes() + B * tw.dim * 4 + 2 * B * tw.vocab * 4
+    achieved = alg / (ms / 1000.0) / 1e9
+    x0 = xs[0].numpy()
+    rate, kind, cores, reps = cpu_decode_rate(tw, q, s, norm, x0, hist, a.cpu_seconds, po.host_threads())
+    line = {
+        "metric": DECODE_METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "i8/f32", "data": "synthetic", "config": decode_config(tw, B, world),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "traffic": None,
+                     "kernel": "tail_norm_kernel + tail head kernel + the pick's kernels (whole step)",
+                     "alg_bytes_per_launch": alg, "launch_ms": ms},
+        "clocks": clocks.summary() if clocks else None,
+        "timing": "host call per step (host hidden rows in, host ids out)",
+        # per step: the tail (norm + head kernel, one fused kernel up to 8 rows), split_kernel + merge_slices_kernel
+        "gpu_launches": ((1 if B <= 8 else 2) + 2) * a.steps * world,
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": B * tw.dim * 4 * world,
+                "d2h_bytes_per_step": B * 4 * world},
+        "cpu_baseline": {"value": rate, "unit": "rows/s", "cores": cores, "kind": kind,
+                         "sample": f"the {B} rows of one step x {reps} passes"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main_tail(a, rank: int, local_rank: int, world: int):
     tw = wl.TAIL.with_dtype(a.head)
     if a.rows:
@@ -869,6 +1022,9 @@ def main():
     rank, local_rank, world = dist_env()
     if a.config == "tail":
         main_tail(a, rank, local_rank, world)
+        return
+    if a.config == "decode":
+        main_decode(a, rank, local_rank, world)
         return
     w = wl.WORKLOADS[a.config]
     if a.rows:
