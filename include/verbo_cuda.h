@@ -182,8 +182,8 @@ VERBO_CUDA_API int verbo_cuda_comm_mark_next(verbo_cuda_comm* c, void* after_sha
    last check (then clears them): 0 if none, -1 with a message otherwise. */
 VERBO_CUDA_API int verbo_cuda_check(void* stream);
 
-/* Diagnostics of the full-vocabulary path (top_k == 0 or >= vocab, no min-p,
-   no penalty; no counterpart in the reference): synchronises `stream` and
+/* Diagnostics of the full-vocabulary path (top_k == 0 or >= vocab, no
+   penalty; no counterpart in the reference): synchronises `stream` and
    returns how many rows of the last such call on it were settled by the
    staged cluster kernel instead of the streaming one (rows whose cutoff or
    draw fell among crowded or underflow columns), or -1 on error. */

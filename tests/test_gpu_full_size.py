@@ -172,13 +172,18 @@ def test_c5_sharded_full_size():
 
 # Full-size rows on the other paths: the staged cluster kernel (full
 # vocabulary with min-p and a penalty, several waves of 37 resident rows),
-# large top-k (certified top-m slices, k up to 256) and the streaming path at
-# a sharper temperature (fewer, heavier members per cell).
+# large top-k (certified top-m slices, k up to 256), the streaming path at a
+# sharper temperature (fewer, heavier members per cell) and the streaming
+# path with min-p (src/sampler.cpp:86-91) where min-p cuts the kept prefix
+# first, where top-p does, and without top-p.
 EXTRA = {
     "general_minp_penalty": ("c4", 1024, dict(temp=1.0, top_k=0, top_p=0.95, min_p=0.02, repeat=1.1), 64),
     "topk_128": ("c3", 1024, dict(top_k=128), None),
     "topk_256": ("c5", 512, dict(top_k=256, min_p=0.0), None),
     "nucleus_sharp": ("c4", 2048, dict(temp=0.4, top_p=0.9), None),
+    "nucleus_minp_first": ("c4", 1024, dict(temp=1.0, top_p=0.99, min_p=0.3), None),
+    "nucleus_topp_first": ("c4", 1024, dict(temp=1.0, top_p=0.8, min_p=0.02), None),
+    "nucleus_minp_only": ("c4", 1024, dict(temp=0.7, top_p=1.0, min_p=0.1), None),
 }
 
 
@@ -215,4 +220,12 @@ def test_other_paths_full_size(name):
 
     ws = replace(w, name=name, temp=opts["temp"], top_k=opts["top_k"], top_p=opts["top_p"], min_p=opts["min_p"],
                  repeat=opts["repeat"], hist_len=0 if h is None else int(off[1] - off[0]), shards=1)
-    judge(name, ws, ids, stats_np(st), ora, ost, from_dev_rng(rng), orng)
+    fb = vb.full_vocab_fallbacks() if name.startswith("nucleus") else None
+    judge(name, ws, ids, stats_np(st), ora, ost, from_dev_rng(rng), orng, fb)
+    if fb is not None and name.startswith("nucleus_minp"):  # the streaming kernel settles (almost) every row
+        assert fb <= rows // 100, f"{fb} of {rows} rows went to the staged kernel"
+    if name.startswith("nucleus_minp") or name == "nucleus_topp_first":
+        # the kept count is the reference's, min(min-p prefix, top-p prefix),
+        # except where the cut itself is a boundary decision
+        bad = (stats_np(st)["keep"] != ost["keep"]) & ~(ost["cut_margin"] < BOUNDARY)
+        assert not bad.any(), f"{name}: kept counts differ in {int(bad.sum())} rows"

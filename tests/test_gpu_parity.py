@@ -326,12 +326,14 @@ def test_full_vocab_weights_match_reference_sums(temp):
     # The reference sums glibc exp() values one by one in sorted order, whose
     # own rounding is bounded by about N * eps = 151936 * 2^-53 = 1.7e-11
     # relative.  Two kernels compute the normaliser, each with its own bound:
-    #  * the streaming kernel (top_k 0, no min-p, no penalty; nucleus.cu) sums
-    #    per-cell masses exp(-j 2^-K) (1 + e(r)) with e(r) in fp32 and fixed
-    #    point: within 4e-9 relative (its kDelta), about 1e-9 when the cells
-    #    are at their widest (2^-6, temp 0.05 over N(0, 3^2) below);
-    #  * the staged cluster kernel (min-p here) sums fixed-point masses of a
-    #    table-driven fp64 exponential: within 5e-11.
+    #  * the streaming kernel (top_k 0, top-p and / or min-p, no penalty;
+    #    nucleus.cu) sums per-cell masses exp(-j 2^-K) (1 + e(r)) with e(r) in
+    #    fp32 and fixed point: within 4e-9 relative (its kDelta), about 1e-9
+    #    when the cells are at their widest (2^-6, temp 0.05 over N(0, 3^2)
+    #    below);
+    #  * the staged cluster kernel (top_k above 256 and below the vocabulary
+    #    here) sums fixed-point masses of a table-driven fp64 exponential:
+    #    within 5e-11.
     # Both far inside the 1e-5 of the parity criteria; an error in either
     # exponential would show at 1e-3.  The ranges go from nearly all-underflow
     # (temp 0.05 over N(0, 3^2)) to a narrow band (temp 6).  Sampled ids agree
@@ -341,7 +343,9 @@ def test_full_vocab_weights_match_reference_sums(temp):
     x = np.stack([g.standard_normal(V) * 3, g.standard_normal(V) * 0.5, g.uniform(-20, 0, V)]).astype(np.float32)
     seeds = np.arange(3, dtype=np.uint64) + np.uint64(4000 + int(temp * 100))
     for opts, rtol in ((dict(temp=temp, top_k=0, top_p=0.99), 4e-9),
-                       (dict(temp=temp, top_k=0, top_p=1.0, min_p=0.01), 5e-11)):
+                       (dict(temp=temp, top_k=0, top_p=1.0, min_p=0.01), 4e-9),
+                       (dict(temp=temp, top_k=0, top_p=0.9, min_p=0.05), 4e-9),
+                       (dict(temp=temp, top_k=100000, top_p=1.0, min_p=0.01), 5e-11)):
         ids, st, _ = run_gpu(x, opts, seeds, steps=2)
         ora, ost, _ = run_oracle(x, opts, seeds, steps=2)
         compare(ids, ora, ost, f"temp={temp} {opts}")

@@ -126,8 +126,8 @@ cudaError_t launch_general(const RowArgs& a, const DevOpts& o, cudaStream_t s);
 cudaError_t launch_general_list(const RowArgs& a, const DevOpts& o, const int* list, const unsigned* count,
                                 int max_rows, cudaStream_t s);
 
-// Streaming full-vocabulary path (nucleus.cu): top_k == 0 or >= vocab,
-// min_p == 0, no penalty, vocab >= kNucleusMinVocab.  One persistent kernel
+// Streaming full-vocabulary path (nucleus.cu): top_k == 0 or >= vocab, no
+// penalty, vocab >= kNucleusMinVocab (top-p and min-p both taken).  One persistent kernel
 // reads every row once from HBM and settles almost every row; the rest go to
 // the staged kernel above (launched by launch_nucleus on the same stream).
 constexpr int kNucleusMinVocab = 4096;

@@ -14,7 +14,8 @@
 //                 x = (v - M) / temp.  The row's last slice to finish (a
 //                 per-row counter) merges the slices' histograms and places the
 //                 top-p cutoff (src/sampler.cpp:92-100) and the draw (:101-108)
-//                 in one or two cells each;
+//                 in one or two cells each, and the min-p boundary
+//                 (:86-91) in the cells around x = ln(min_p);
 //   C  gathers the slice's members of those cells;
 //   R  resolves the pick among the row's members with the reference's fp64
 //                 weights, in the reference's order.
@@ -63,6 +64,8 @@ constexpr int kMemberCap = 2048;     // members gathered for the decisions
 constexpr int kSubBins = NT;         // sub-bins of the resolve step
 constexpr double kDelta = 4e-9;      // bound on the histogram's cumulative error, relative to the row's sum
 constexpr unsigned kMagic23 = 0x4B400000u;  // bits of 1.5 * 2^23
+constexpr int kQFix = 44;            // fixed-point fraction bits of the min-p boundary's mass (weights <= 1)
+constexpr int kQCap = 1024;          // columns of the min-p boundary cells one C slice may hold
 
 __device__ unsigned g_nuc_status;
 
@@ -167,10 +170,20 @@ struct SliceSum {
 // What the B merge leaves for the C kernel (per row of the chunk).
 struct Targets {
   int fail;            // the row goes to the staged kernel
-  int use_p;           // a top-p cutoff applies
+  int use_p;           // a top-p cutoff may decide the kept prefix
+  int use_m;           // min-p: 0 none, 1 its boundary in cells [Q0, Q1], 2 it keeps every cell
   int A0, A1, B0, B1;  // cells of the cutoff and of the draw
+  int Q0, Q1;          // cells of the min-p boundary (use_m == 1)
   float a_lo, a_hi, b_lo, b_hi;  // value intervals holding their members
+  float q_lo, q_hi;
   unsigned cut_before;  // columns before A0
+  unsigned q_before;    // columns before Q0 (use_m == 2: in every cell)
+  double q_base;        // mass before Q0 (use_m == 2: of every cell)
+  // columns of [Q0, Q1] with weight >= min_p, counted by the C slices
+  // (atomics): their number, mass in 2^-kQFix units (exact, in any order),
+  // largest key; and the smallest key of cell 0 (the first column)
+  unsigned q_n, q_over;  // q_over: a slice had more than kQCap of them (the row goes to the staged kernel)
+  unsigned long long q_mass, q_last, q_first;
   unsigned nmem;        // members gathered (C slices, atomic)
   double cut_base, draw_base;  // cumulative mass before A0 / B0
   double S, tp, u;
@@ -306,6 +319,9 @@ struct Shared {
   unsigned long long r_key;
   double r_cum;
   unsigned r_rank;
+  // C items: the CTA's count of the min-p boundary (see Targets)
+  unsigned q_n, q_cnt;
+  unsigned long long q_mass, q_last, q_first;
 };
 
 // Dynamic shared memory: B items [kCells] counts + [kCells] fixed-point sums;
@@ -315,7 +331,7 @@ constexpr size_t kHistBytes = static_cast<size_t>(kCells) * 8;
 constexpr size_t kCumBytes = static_cast<size_t>(kCells) * 12;
 constexpr size_t kMemberBytes = static_cast<size_t>(kMemberCap) * 24 + static_cast<size_t>(kSubBins) * 12;
 constexpr size_t kBSmem = std::max(kHistBytes, kCumBytes);         // B pass + its row merge
-constexpr size_t kCSmem = static_cast<size_t>(kMemberCap) * 8;     // C pass: the slice's members
+constexpr size_t kCSmem = static_cast<size_t>(kMemberCap + kQCap) * 8;  // C pass: members, min-p boundary keys
 constexpr size_t kRSmem = kMemberBytes;                             // resolve
 constexpr int kBBlocks = 4, kCBlocks = 6;                           // resident CTAs per SM aimed at
 
@@ -612,7 +628,11 @@ __device__ __noinline__ void merge_b(int row, unsigned char* smem, Shared& sh) {
     lcnt += cnt[c];
   }
   double U = 0.0;
-  for (int s = 0; s < p.ns; ++s) U += __ldcg(&sums[s].umass);
+  unsigned Uc = 0;
+  for (int s = 0; s < p.ns; ++s) {
+    U += __ldcg(&sums[s].umass);
+    Uc += __ldcg(&sums[s].ucount);
+  }
   double wpre, wtot;
   unsigned cpre, ctot;
   bscan(local, lcnt, sh, &wpre, &cpre, &wtot, &ctot);
@@ -652,11 +672,58 @@ __device__ __noinline__ void merge_b(int row, unsigned char* smem, Shared& sh) {
     u = rng_unit(s1, s0);
   }
   __syncthreads();
-  const int A0 = use_p ? sh.c_lo : nc, A1 = use_p ? sh.c_hi : -1;
-  bool fail = sh.flag != 0 || (use_p && (A0 >= nc || A1 >= nc));
-  // the range of the cutoff's running mass (all of S without a cutoff)
-  const double tot_lo = use_p && !fail ? (A0 > 0 ? cum[A0 - 1] : 0.0) : S;
-  const double tot_hi = use_p && !fail ? cum[A1] : S;
+  int A0 = use_p ? sh.c_lo : nc, A1 = use_p ? sh.c_hi : -1;
+  bool fail = sh.flag != 0;
+  // min-p (src/sampler.cpp:86-91): the max's weight is exp(0) = 1, so the
+  // kept prefix is every column with weight >= min_p, at least one; its
+  // boundary lies in the cells around x* = ln(min_p), widened for the fp32
+  // roundings of x.  use_m 2: x* lies below every cell and no column
+  // underflows, so min-p keeps every cell.
+  int use_m = 0, Q0 = nc, Q1 = -1;
+  bool m_unsure = false;  // the boundary may reach the underflow columns
+  if (o.min_p > 0.0f) {
+    // the cells of x* -+ (a hundredth of a cell + a relative 1e-5), the
+    // slack of the fp32 x against the exact d / temp (as in vbound below)
+    const double xs = log(static_cast<double>(o.min_p));
+    const double eps = ldexp(0.01, -g.K) + 1e-5 * fabs(xs);
+    const double lo = rint(-ldexp(xs + eps, g.K)), hi = rint(-ldexp(xs - eps, g.K));
+    if (lo > static_cast<double>(g.ncr)) {
+      use_m = 2;
+      m_unsure = Uc != 0;
+    } else {
+      use_m = 1;
+      Q0 = static_cast<int>(fmax(lo, 0.0));
+      Q1 = static_cast<int>(fmin(hi, static_cast<double>(g.ncr)));
+      m_unsure = hi > static_cast<double>(g.ncr) && Uc != 0;
+    }
+  }
+  const bool p_beyond = use_p && (A0 >= nc || A1 >= nc);  // the cutoff lies among the underflow columns
+  // the ranges of each cut's running mass; the kept prefix is the shorter
+  double lo_p = S, hi_p = S, lo_m = S, hi_m = S;
+  if (use_p && !p_beyond) {
+    lo_p = A0 > 0 ? cum[A0 - 1] : 0.0;
+    hi_p = cum[A1];
+  }
+  if (use_m == 1) {
+    lo_m = Q0 > 0 ? cum[Q0 - 1] : 0.0;
+    hi_m = cum[Q1];
+  } else if (use_m == 2) {
+    lo_m = hi_m = wtot;
+  }
+  bool need_p = use_p && !p_beyond, need_m = use_m == 1;
+  if (need_p && use_m == 1 && A0 > Q1) need_p = false;  // min-p keeps fewer columns for certain
+  if (need_m && need_p && A1 < Q0) need_m = false;      // top-p does
+  if (!need_p) lo_p = hi_p = S;
+  if (!need_m && use_m == 1) lo_m = hi_m = S;
+  if (p_beyond && !(use_m == 1 && !m_unsure)) fail = true;  // top-p may cut among the underflow columns
+  if (m_unsure && !(need_p && A1 < Q0)) fail = true;     // so may min-p
+  if (use_m == 2 && need_p) use_m = 0;                 // top-p cuts within the cells, before min-p
+  if (use_m == 1 && !need_m) use_m = 0;
+  if (!need_p) {
+    A0 = nc;
+    A1 = -1;
+  }
+  const double tot_lo = fmin(lo_p, lo_m), tot_hi = fmin(hi_p, hi_m);
   if (!fail && u * tot_hi + dl > wtot) fail = true;  // the draw may fall among the underflow columns
   if (!fail) {
     first_reach(u * tot_lo - dl, &sh.d_lo);
@@ -670,7 +737,7 @@ __device__ __noinline__ void merge_b(int row, unsigned char* smem, Shared& sh) {
     if (!fail && (B0 >= nc || B1 >= nc)) fail = true;
     if (!fail) {
       unsigned need = before(B1 + 1) - before(B0);
-      if (use_p) need += before(A1 + 1) - before(A0);
+      if (A1 >= A0) need += before(A1 + 1) - before(A0);
       if (need > static_cast<unsigned>(kMemberCap)) fail = true;
     }
     t->fail = fail;
@@ -684,17 +751,30 @@ __device__ __noinline__ void merge_b(int row, unsigned char* smem, Shared& sh) {
         const double w = ldexp(0.01, -g.K) + 1e-5 * fabs(xb);
         return static_cast<float>(static_cast<double>(g.M) + (xb + side * w) * temp_d);
       };
-      t->use_p = use_p;
+      const bool pa = A1 >= A0;
+      t->use_p = pa;
+      t->use_m = use_m;
       t->A0 = A0;
       t->A1 = A1;
       t->B0 = B0;
       t->B1 = B1;
-      t->a_lo = use_p ? vbound(A1, -1.0) : __int_as_float(0x7f800000);
-      t->a_hi = use_p ? vbound(A0, 1.0) : -__int_as_float(0x7f800000);
+      t->Q0 = use_m == 1 ? Q0 : nc;
+      t->Q1 = use_m == 1 ? Q1 : -1;
+      t->a_lo = pa ? vbound(A1, -1.0) : __int_as_float(0x7f800000);
+      t->a_hi = pa ? vbound(A0, 1.0) : -__int_as_float(0x7f800000);
       t->b_lo = vbound(B1, -1.0);
       t->b_hi = vbound(B0, 1.0);
-      t->cut_before = use_p ? before(A0) : 0u;
-      t->cut_base = use_p && A0 > 0 ? cum[A0 - 1] : 0.0;
+      t->q_lo = use_m == 1 ? vbound(Q1, -1.0) : __int_as_float(0x7f800000);
+      t->q_hi = use_m == 1 ? vbound(Q0, 1.0) : -__int_as_float(0x7f800000);
+      t->cut_before = pa ? before(A0) : 0u;
+      t->cut_base = pa && A0 > 0 ? cum[A0 - 1] : 0.0;
+      t->q_before = use_m == 1 ? before(Q0) : ctot;
+      t->q_base = use_m == 1 ? (Q0 > 0 ? cum[Q0 - 1] : 0.0) : wtot;
+      t->q_n = 0;
+      t->q_over = 0;
+      t->q_mass = 0;
+      t->q_last = 0;
+      t->q_first = kNoKey;
       t->draw_base = B0 > 0 ? cum[B0 - 1] : 0.0;
       t->S = S;
       t->tp = tp;
@@ -708,6 +788,22 @@ __device__ __noinline__ void merge_b(int row, unsigned char* smem, Shared& sh) {
 }
 
 // ------------------------------------------------------------- C items ----
+// A column of the min-p boundary cells (src/sampler.cpp:86-91), after the
+// scan: counted into the CTA's totals when its weight, as the reference
+// computes it, reaches min_p (the max's weight is exp(0) = 1).
+__device__ __forceinline__ void q_note(unsigned long long k, int c, float M, Shared& sh) {
+  const double w = ref_weight(dval(k), M, static_cast<double>(sh.o.temp));
+  if (w >= static_cast<double>(sh.o.min_p)) {
+    atomicAdd(&sh.q_n, 1u);
+    atomicAdd(&sh.q_mass, __double2ull_rn(ldexp(w, kQFix)));
+    atomicMax(&sh.q_last, k);
+  }
+  if (c == 0) atomicMin(&sh.q_first, k);
+}
+
+// kMinP: the call has min-p, so rows may carry a min-p boundary to count; the
+// form without it keeps the scan loop free of that bookkeeping.
+template <bool kMinP>
 __device__ __noinline__ void run_c(int row, int s, unsigned char* smem, Shared& sh) {
   const NucArgs& p = sh.p;
   const DevOpts& o = sh.o;
@@ -723,17 +819,34 @@ __device__ __noinline__ void run_c(int row, int s, unsigned char* smem, Shared& 
     __syncthreads();
     const Grid g = row_grid(st, o.temp);
     const int A0 = __ldcg(&tg->A0), A1 = __ldcg(&tg->A1), B0 = __ldcg(&tg->B0), B1 = __ldcg(&tg->B1);
+    const int Q0 = kMinP ? __ldcg(&tg->Q0) : 0, Q1 = kMinP ? __ldcg(&tg->Q1) : -1;
     const float a_lo = __ldcg(&tg->a_lo), a_hi = __ldcg(&tg->a_hi);
     const float b_lo = __ldcg(&tg->b_lo), b_hi = __ldcg(&tg->b_hi);
-    const bool use_a = A1 >= A0;
+    const float q_lo = kMinP ? __ldcg(&tg->q_lo) : 0.0f, q_hi = kMinP ? __ldcg(&tg->q_hi) : -1.0f;
+    const bool use_a = A1 >= A0, use_q = kMinP && Q1 >= Q0;
     unsigned long long* loc = reinterpret_cast<unsigned long long*>(smem);  // [kMemberCap]
     const int lo = s * p.slice;
     const int n = min(p.slice, a.ncols - lo);
     const float* src = a.logits + static_cast<long long>(row) * a.ld + lo;
     const unsigned gid0 = static_cast<unsigned>(a.col_off + lo);
+    unsigned long long* qloc = loc + kMemberCap;  // [kQCap] keys of the min-p boundary cells
+    if (kMinP) {
+      if (threadIdx.x == 0) {
+        sh.q_n = 0;
+        sh.q_cnt = 0;
+        sh.q_mass = 0;
+        sh.q_last = 0;
+        sh.q_first = kNoKey;
+      }
+      __syncthreads();
+    }
     auto test = [&](float v, int j) {
-      if ((v >= a_lo && v <= a_hi) || (v >= b_lo && v <= b_hi)) {
+      if ((v >= a_lo && v <= a_hi) || (v >= b_lo && v <= b_hi) || (kMinP && v >= q_lo && v <= q_hi)) {
         const int c = cell_of_v(v, g);
+        if (kMinP && c >= Q0 && c <= Q1) {
+          const unsigned q = atomicAdd(&sh.q_cnt, 1u);
+          if (q < static_cast<unsigned>(kQCap)) qloc[q] = dkey(v, gid0 + static_cast<unsigned>(j));
+        }
         if ((c >= A0 && c <= A1) || (c >= B0 && c <= B1)) {
           const unsigned q = atomicAdd(&sh.nmem, 1u);
           if (q < static_cast<unsigned>(kMemberCap)) loc[q] = dkey(v, gid0 + static_cast<unsigned>(j));
@@ -746,7 +859,9 @@ __device__ __noinline__ void run_c(int row, int s, unsigned char* smem, Shared& 
     const float ma = use_a ? 0.5f * (a_lo + a_hi) : __int_as_float(0x7f800000);
     const float ha = use_a ? 0.5f * (a_hi - a_lo) * (1.0f + 1e-6f) + 1e-30f : -1.0f;
     const float mb = 0.5f * (b_lo + b_hi), hb = 0.5f * (b_hi - b_lo) * (1.0f + 1e-6f) + 1e-30f;
-    const f2 nma = f2pk(-ma, -ma), nmb = f2pk(-mb, -mb);
+    const float mq = use_q ? 0.5f * (q_lo + q_hi) : 0.0f;
+    const float hq = use_q ? 0.5f * (q_hi - q_lo) * (1.0f + 1e-6f) + 1e-30f : -1.0f;
+    const f2 nma = f2pk(-ma, -ma), nmb = f2pk(-mb, -mb), nmq = f2pk(-mq, -mq);
     each_col_pipe<4>(src, n, [&](const float4& v, int j) {
       const f2 v01 = f2pk(v.x, v.y), v23 = f2pk(v.z, v.w);
       float a0, a1, a2, a3, b0, b1, b2, b3;
@@ -756,7 +871,14 @@ __device__ __noinline__ void run_c(int row, int s, unsigned char* smem, Shared& 
       f2up(add2(v23, nmb), b2, b3);
       const float da = fminf(fminf(fabsf(a0), fabsf(a1)), fminf(fabsf(a2), fabsf(a3)));
       const float db = fminf(fminf(fabsf(b0), fabsf(b1)), fminf(fabsf(b2), fabsf(b3)));
-      if (da <= ha || db <= hb) {
+      bool hit = da <= ha || db <= hb;
+      if (kMinP && use_q) {  // min-p boundary cells (a uniform branch: one row per CTA)
+        float q0, q1, q2, q3;
+        f2up(add2(v01, nmq), q0, q1);
+        f2up(add2(v23, nmq), q2, q3);
+        hit |= fminf(fminf(fabsf(q0), fabsf(q1)), fminf(fabsf(q2), fabsf(q3))) <= hq;
+      }
+      if (hit) {
         test(v.x, j);
         test(v.y, j + 1);
         test(v.z, j + 2);
@@ -764,8 +886,29 @@ __device__ __noinline__ void run_c(int row, int s, unsigned char* smem, Shared& 
       }
     }, test);
     __syncthreads();
+    if (use_q) {  // the boundary's columns: weights and counts, out of the scan loop
+      const unsigned qc = min(sh.q_cnt, static_cast<unsigned>(kQCap));
+      for (unsigned i = threadIdx.x; i < qc; i += NT) {
+        const unsigned long long k = qloc[i];
+        float d, t;
+        q_note(k, cell_of(xof(dval(k), g, &d), g, &t), g.M, sh);
+      }
+      __syncthreads();
+    }
     const unsigned cnt = min(sh.nmem, static_cast<unsigned>(kMemberCap));
-    if (threadIdx.x == 0) sh.mbase = cnt ? atomicAdd(&p.tg[ms].nmem, sh.nmem) : 0u;
+    if (threadIdx.x == 0) {
+      sh.mbase = cnt ? atomicAdd(&p.tg[ms].nmem, sh.nmem) : 0u;
+      if (use_q && sh.q_cnt > static_cast<unsigned>(kQCap)) atomicOr(&p.tg[ms].q_over, 1u);
+      if (use_q) {  // the slice's count of the min-p boundary, one atomic per field
+        Targets* tw = p.tg + ms;
+        if (sh.q_n) {
+          atomicAdd(&tw->q_n, sh.q_n);
+          atomicAdd(&tw->q_mass, sh.q_mass);
+          atomicMax(&tw->q_last, sh.q_last);
+        }
+        if (sh.q_first != kNoKey) atomicMin(&tw->q_first, sh.q_first);
+      }
+    }
     __syncthreads();
     unsigned long long* mem = p.members + static_cast<long long>(ms) * kMemberCap;
     for (unsigned i = threadIdx.x; i < cnt; i += NT)
@@ -951,6 +1094,33 @@ __device__ __noinline__ void merge_c(int row, unsigned char* smem, Shared& sh) {
       keep = __ldcg(&tg->cut_before) + sh.r_rank + 1u;
       cut_key = sh.r_key;
     }
+    const int use_m = __ldcg(&tg->use_m);
+    if (ok && use_m == 1 && __ldcg(&tg->q_over) != 0u) ok = false;
+    if (ok && use_m == 1) {
+      // min-p (src/sampler.cpp:86-91): the columns with weight >= min_p (the
+      // max's weight is exp(0) = 1), at least the first; the kept prefix is
+      // the shorter of the two cuts
+      unsigned km = __ldcg(&tg->q_before) + __ldcg(&tg->q_n);
+      double tm = __ldcg(&tg->q_base) + ldexp(static_cast<double>(__ldcg(&tg->q_mass)), -kQFix);
+      unsigned long long lastm = __ldcg(&tg->q_n) ? __ldcg(&tg->q_last) : kNoKey;
+      if (km == 0u) {  // min_p above every weight: the first column alone, weight exp(0) = 1
+        km = 1u;
+        lastm = __ldcg(&tg->q_first);
+        tm = 1.0;
+        if (lastm == kNoKey) ok = false;
+      }
+      if (km < keep) {
+        keep = km;
+        tot = tm;
+        cut_key = lastm;
+      }
+    } else if (ok && use_m == 2) {  // min-p keeps every cell
+      const unsigned km = __ldcg(&tg->q_before);
+      if (km < keep) {
+        keep = km;
+        tot = __ldcg(&tg->q_base);
+      }
+    }
     if (ok) {  // the draw: first kept member at which the running mass reaches u * tot
       const double r = u * tot;
       const double t = r > 0.0 ? r : 4.9406564584124654e-324;
@@ -1012,12 +1182,13 @@ __global__ void __launch_bounds__(NT, kBBlocks) nuc_b_kernel(const NucArgs p, co
   setup(p, o, sh);
   run_b(p.rowb + j / p.ns, j % p.ns, smem, sh);
 }
+template <bool kMinP>
 __global__ void __launch_bounds__(NT, kCBlocks) nuc_c_kernel(const NucArgs p, const DevOpts o) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ Shared sh;
   const int j = static_cast<int>(blockIdx.x);
   setup(p, o, sh);
-  run_c(p.rowc + j / p.ns, j % p.ns, smem, sh);
+  run_c<kMinP>(p.rowc + j / p.ns, j % p.ns, smem, sh);
 }
 __global__ void __launch_bounds__(NT, 4) nuc_r_kernel(const NucArgs p, const DevOpts o) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -1030,7 +1201,7 @@ __global__ void __launch_bounds__(NT, 4) nuc_r_kernel(const NucArgs p, const Dev
 
 // ------------------------------------------------------------- launcher ---
 bool nucleus_eligible(const DevOpts& o, int vocab) {
-  return !o.greedy && o.k >= vocab && !(o.min_p > 0.0f) && !o.penalize && vocab >= kNucleusMinVocab;
+  return !o.greedy && o.k >= vocab && !o.penalize && vocab >= kNucleusMinVocab;
 }
 
 static int slices_of(int ncols) { return (ncols + nuc::kSliceCols - 1) / nuc::kSliceCols; }
@@ -1071,7 +1242,10 @@ cudaError_t launch_nucleus(const RowArgs& a, const DevOpts& o, void* scratch, cu
     p.na = p.nb = p.nc = n;
     nuc_a_kernel<<<n * ns, NT, 0, s>>>(p, o);
     nuc_b_kernel<<<n * ns, NT, kBSmem, s>>>(p, o);
-    nuc_c_kernel<<<n * ns, NT, kCSmem, s>>>(p, o);
+    if (o.min_p > 0.0f)
+      nuc_c_kernel<true><<<n * ns, NT, kCSmem, s>>>(p, o);
+    else
+      nuc_c_kernel<false><<<n * ns, NT, kCSmem, s>>>(p, o);
     nuc_r_kernel<<<n, NT, kRSmem, s>>>(p, o);
   }
   e = cudaGetLastError();
