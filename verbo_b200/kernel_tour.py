@@ -13,8 +13,8 @@ the rows of every sampling step are larger than the 126 MB L2:
            (window_kernel, split_kernel top-k, merge_slices_kernel)
   c4       verbo_cuda_sample, 512 x 151936 full-vocabulary nucleus
            (nuc_a/b/c kernels and the resolve, general_list_kernel)
-  staged   verbo_cuda_sample, 256 x 151936 top_k 0 with min_p 0.02
-           (general_kernel, 8-CTA clusters)
+  staged   verbo_cuda_sample, 256 x 151936 top_k 100000 with min_p 0.02
+           (general_kernel, 8-CTA clusters: top_k above 256)
   c5       verbo_cuda_shard_topk over 8 column shards + verbo_cuda_merge_sample,
            512 x 151936 (window_kernel, split_kernel emit, merge_slices_kernel,
            merge_kernel)
@@ -99,7 +99,7 @@ def main() -> None:
     step("c2", lambda: sample(c2))
     step("c3", lambda: sample(c3))
     step("c4", lambda: sample(c4))
-    step("staged", lambda: sample(st, temp=1.0, top_p=0.95, min_p=0.02))
+    step("staged", lambda: sample(st, temp=1.0, top_k=100000, top_p=0.95, min_p=0.02))
 
     def shards():
         w, x, dh, do, rng = c5
