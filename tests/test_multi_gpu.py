@@ -32,7 +32,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_vocab_sharded_over_two_gpus_matches_unsharded(cuda_lib):
+def test_vocab_sharded_over_two_gpus_matches_oracle(cuda_lib):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
